@@ -1,0 +1,271 @@
+"""Headline benchmark: Uno-Qwen3-8B Psi-Spec output tokens/s (linear sampler).
+
+Config: Qwen3-8B architecture with random-init weights and a
+random rank-64 conditional-LoRA adapter on every linear, bf16; 64 concurrent
+requests with prompt lengths uniform in [128, 1024] and Zipf(1.1) token ids;
+temperature 1.0; diffusion block size 8; 256-token KV pages; CUDA graphs for
+decode batch sizes 1..64.  ``--gpus N`` runs tensor parallel degree N (strong
+scaling: the same 64-request batch is split across N GPUs), one process per GPU
+under ``torch.distributed.run``.
+
+A *step* is one engine decode step: one Psi-Spec cycle (draft forward + verify
+forward + accept/resample) for every running request.  ``value`` is committed
+output tokens per second over exactly ``--steps`` steps after ``--warmup``
+steps, timed with CUDA events on every rank (barrier + synchronize on both
+sides) and reduced with MAX over ranks.  The per-step working set (16 GB of
+weights plus the KV cache) is far larger than L2, so no L2 flush is needed.
+``e2e`` is the same metric through the public ``LLM.generate`` API over the
+whole workload (prefill included), wall-clock, which copies each step's inputs
+host->device from pinned memory and reads committed tokens back every step.
+
+``--impl reference`` runs the unmodified reference package from
+``baseline/_ref`` through its own ``LLM`` API on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "Uno-Qwen3-8B Psi-Spec output tok/s at TP=1/2/4/8; per-request tok/s; TPF"
+BASELINE_TOKS = None  # BASELINE.json publishes no number (chart estimate only)
+VOCAB = 151936
+MASK_ID = 151669
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--block", type=int, default=8)
+    ap.add_argument("--new-tokens", type=int, default=2048)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-tokens", type=int, default=0, help="override new tokens for the e2e run")
+    return ap.parse_args()
+
+
+def make_prompts(batch: int, seed: int) -> list[list[int]]:
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(VOCAB - 2) + 1
+    lens = rng.integers(128, 1025, size=batch)
+    prompts = []
+    for n in lens:
+        ranks = rng.zipf(1.1, size=int(n)) - 1
+        prompts.append([int(perm[r % len(perm)]) for r in ranks])
+    return prompts
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path: str):
+        self.path = path
+        self.proc = None
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax.append(float(parts[2].split()[0]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def engine_kwargs(args, tp: int) -> dict:
+    ladder = list(range(1, 9)) + list(range(10, 33, 2)) + list(range(40, 65, 4))
+    return dict(
+        tensor_parallel_size=tp,
+        max_num_seqs=args.batch,
+        max_model_len=1024 + args.new_tokens + 64,
+        max_num_batched_tokens=16384,
+        kvcache_block_size=256,
+        max_diffusion_block_size=args.block,
+        cuda_graph_block_sizes=sorted({1, args.block}),
+        cuda_graph_batch_sizes=[b for b in ladder if b <= args.batch],
+        dummy_lora_rank=64,
+        dummy_lora_alpha=128.0,
+        gpu_memory_utilization=0.90,
+        seed=args.seed,
+    )
+
+
+def run_native(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    sys.path.insert(0, ROOT)
+    from uno_b200 import LLM, SamplingParams
+    from uno_b200.engine.worker import serve_follower
+
+    kw = engine_kwargs(args, world)
+    if world > 1:
+        kw["distributed_init"] = "env"
+        os.environ.setdefault("TORCH_DISTRIBUTED_TIMEOUT_MINUTES", "5")
+    if rank != 0:
+        serve_follower("preset:qwen3-8b", **kw)
+        return
+    llm = LLM("preset:qwen3-8b", **kw)
+    sp = SamplingParams(temperature=1.0, max_tokens=args.new_tokens, diffusion_block_size=args.block,
+                        mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed)
+    prompts = make_prompts(args.batch, args.seed)
+
+    # ---------------- device-timed steady-state decode steps
+    for p in prompts:
+        llm.add_request(p, sp)
+    while llm.scheduler.waiting:
+        llm.step()  # prefill (unchunked) until every request is admitted
+    for _ in range(args.warmup):
+        llm.step()
+    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out", "bench_clocks.csv") if os.path.isdir(
+        os.path.join(ROOT, "gpurun_out")) else "/tmp/bench_clocks.csv")
+    clocks.start()
+    llm.call("timer_start")
+    tokens = 0
+    stats0 = {k: sum(s.stats[k] for s in llm.scheduler.running) for k in ("forwards", "accepts")}
+    for _ in range(args.steps):
+        outputs, n = llm.step()
+        tokens += -n
+    ms = llm.call("timer_stop")
+    clock_info = clocks.stop()
+    stats1 = {k: sum(s.stats[k] for s in llm.scheduler.running) for k in ("forwards", "accepts")}
+    running = len(llm.scheduler.running)
+    # launches per step: count kernels of one extra step under the profiler (not timed)
+    launches = count_launches(llm)
+    # drain the remaining work so the engine is idle
+    while not llm.is_finished():
+        llm.step()
+
+    # ---------------- end-to-end through the public API
+    e2e = None
+    if not args.no_e2e:
+        new_tokens = args.e2e_tokens or args.new_tokens
+        sp2 = SamplingParams(temperature=1.0, max_tokens=new_tokens, diffusion_block_size=args.block,
+                             mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed + 1)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        outs = llm.generate(prompts, sp2, use_tqdm=False, detokenize=False)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        total = sum(len(o["token_ids"]) for o in outs)
+        st = llm.last_generate_stats
+        ws = llm.model_runner.workspace
+        h2d = int(ws.host64.numel() * 8 + ws.host32.numel() * 4) * 2 + args.batch * args.block * 4
+        e2e = {"value": total / dt, "unit": "tok/s", "seconds": dt, "output_tokens": total,
+               "tpf": st.get("accepts", 0) / max(1, st.get("forwards", 0)),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": args.batch * (args.block + 2) * 8,
+               "api": "uno_b200.LLM.generate"}
+    tps = tokens / (ms / 1e3)
+    d_acc = stats1["accepts"] - stats0["accepts"]
+    d_fwd = stats1["forwards"] - stats0["forwards"]
+    line = {
+        "metric": METRIC,
+        "value": tps,
+        "unit": "tok/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": (tps / BASELINE_TOKS) if BASELINE_TOKS else None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights, Zipf(1.1) prompt ids)",
+        "config": {"model": "Uno-Qwen3-8B (random init) + rank-64 gated LoRA", "global_batch": args.batch,
+                   "seq_len": "prompt U[128,1024] + 2048 new", "block_size": args.block,
+                   "sampler": "linear Psi-Spec, T=1.0", "kv_page": 256,
+                   "parallelism": f"tp{args.gpus}", "l2": "working set >> L2 (16 GB weights + KV per step)",
+                   "running_requests": running},
+        "tpf": d_acc / max(1, d_fwd),
+        "clocks": clock_info,
+        "e2e": e2e,
+        "gpu_launches": launches * args.steps if launches is not None else None,
+        "impl": "native",
+    }
+    print(json.dumps(line), flush=True)
+    llm.exit()
+
+
+def count_launches(llm):
+    """Kernels of the extension launched by one decode step (profiled, untimed)."""
+    import torch
+
+    if llm.is_finished():
+        return None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            llm.step()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        mine = [n for n in names if any(k in n for k in (
+            "gemm_bf16_kernel", "paged_attention", "attention_combine", "rmsnorm", "embedding_kernel",
+            "gumbel_sample", "argmax_kernel", "fused_verify", "topk_lse", "build_tree", "walk_tree",
+            "copy_tree_kv", "qk_norm_rope", "silu_mul"))]
+        return len(mine)
+    except Exception:  # pragma: no cover - profiler availability
+        return None
+
+
+def run_reference(args):
+    from bench_reference import run  # the reference arm lives beside bench.py
+
+    run(args)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -347,6 +347,11 @@ class ModelRunner:
                 shapes.append((Mode.BLOCK, L, True))
         if self.config.tree_verify_size is not None:
             shapes.append((Mode.TREE, self.config.tree_verify_size, False))
+        from uno_b200.ops import cuda as cuda_ops
+
+        cfg = self.config.hf_config
+        cuda_ops.reserve_attention_scratch(self.device, ws.max_tokens,
+                                           cfg.num_attention_heads // self.world_size, 16)
         torch.cuda.synchronize()
         free0 = torch.cuda.mem_get_info()[0]
         pool = torch.cuda.graph_pool_handle()
@@ -389,6 +394,30 @@ class ModelRunner:
             return self.run_prefill(seqs, sp)
         self._timing_step += 1
         return self.decoder.run_cycle(seqs, sp)
+
+    # ------------------------------------------------------------ bench hooks
+    def timer_start(self) -> None:
+        """Barrier + synchronise, then record a start event on this rank."""
+        if self.world_size > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+        self._t0 = torch.cuda.Event(enable_timing=True)
+        self._t0.record()
+
+    def timer_stop(self) -> float:
+        """Elapsed device ms since ``timer_start``, max over TP ranks."""
+        t1 = torch.cuda.Event(enable_timing=True)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([self._t0.elapsed_time(t1)], device=self.device)
+        if self.world_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            dist.barrier()
+        return float(ms.item())
 
     def reset_decode_timing(self) -> None:
         self._timing_step = 0

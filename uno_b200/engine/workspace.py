@@ -57,7 +57,7 @@ class DecodeWorkspace:
             self.lora_mask[:n_tokens].copy_(self.host_lora[:n_tokens], non_blocking=True)
         self.prefix_lens.copy_(self.prefix_lens64)
 
-    def meta(self, mode: Mode, B: int, Q: int, lora: bool) -> ForwardMeta:
+    def meta(self, mode: Mode, B: int, Q: int, lora: bool, max_kv: int = 0) -> ForwardMeta:
         T = B * Q
         return ForwardMeta(
             mode=mode,
@@ -68,6 +68,7 @@ class DecodeWorkspace:
             suffix_mask=self.suffix_mask_flat[:T].view(B, Q),
             seqlen_q=Q,
             lora_mask=self.lora_mask[:T] if lora else None,
+            max_kv=max_kv or self.max_pages * self.page_size,
         )
 
 

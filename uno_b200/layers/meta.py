@@ -47,6 +47,8 @@ class ForwardMeta:
     lora_mask: torch.Tensor | None = None      # [T] float32
     # prefill computes logits only at these rows (last token of each request)
     logits_indices: torch.Tensor | None = None
+    # upper bound on keys any request of this forward can see (split planning)
+    max_kv: int = 0
 
     @property
     def batch_size(self) -> int:

@@ -167,7 +167,8 @@ class DecoderForCausalLM(nn.Module):
             self.lm_head.weight = self.model.embed_tokens.weight
         self.register_buffer(
             "cos_sin_cache",
-            cos_sin_cache(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta, cfg.rope_scaling),
+            cos_sin_cache(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta, cfg.rope_scaling,
+                          device=self.lm_head.weight.device),
             persistent=False,
         )
 

@@ -1,0 +1,175 @@
+// Python bindings of the uno_b200 sm_100a kernels (module ``uno_b200._C``).
+#include <torch/extension.h>
+
+#include "uno_ops.h"
+
+namespace uno {
+
+// Forward declarations (defined in the .cu files).
+void rmsnorm_launch(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
+                    at::Tensor& y, double eps, int groups);
+void embedding_launch(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t start);
+void silu_mul_launch(const at::Tensor& x, at::Tensor& out);
+void qk_norm_rope_store_launch(const at::Tensor& qkv, at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache,
+                               const at::Tensor& slots, const at::Tensor& positions, const at::Tensor& cos_sin,
+                               const c10::optional<at::Tensor>& qw, const c10::optional<at::Tensor>& kw, double eps,
+                               int hq, int hkv, int D, int page);
+void copy_tree_kv_launch(at::Tensor& cache, const at::Tensor& tables, const at::Tensor& src, const at::Tensor& dst,
+                         int page);
+void argmax_launch(const at::Tensor& x, at::Tensor& out);
+void gumbel_sample_launch(const at::Tensor& x, at::Tensor& out, double inv_temp, int64_t seed, int64_t offset);
+void fused_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at::Tensor& spec, double inv_temp,
+                         int64_t seed, int64_t offset, at::Tensor& accepted, at::Tensor& corr);
+void topk_lse_launch(const at::Tensor& x, int K, double inv_temp, at::Tensor& ids, at::Tensor& lp);
+void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at::Tensor& lp, int Qn, at::Tensor& tok,
+                       at::Tensor& par, at::Tensor& dep, at::Tensor& mass, at::Tensor& count);
+void walk_tree_launch(const at::Tensor& tok, const at::Tensor& par, const at::Tensor& tgt, int max_depth, int64_t pad,
+                      at::Tensor& committed, at::Tensor& accepted, at::Tensor& lengths);
+
+static int* g_err[64] = {nullptr};
+
+int* device_error_flag() {
+  int dev;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (g_err[dev] == nullptr) {
+    C10_CUDA_CHECK(cudaMalloc(&g_err[dev], sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(g_err[dev], 0, sizeof(int)));
+  }
+  return g_err[dev];
+}
+
+static int64_t read_error_flag(bool reset) {
+  int* f = device_error_flag();
+  int h = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&h, f, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) C10_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
+  return h;
+}
+
+// Every pointer handed to a kernel must live on the current CUDA device: a
+// host or foreign-device tensor is rejected here instead of faulting on the GPU.
+
+template <typename T>
+static T* ptr_or_null(const c10::optional<at::Tensor>& t, const char* what = "tensor argument") {
+  if (!(t.has_value() && t->defined())) return nullptr;
+  check_dev(*t, what);
+  return reinterpret_cast<T*>(t->data_ptr());
+}
+
+// Generic GEMM entry: out = epilogue(a[M,K] . b[N,K]^T).
+static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t bn, c10::optional<at::Tensor> c,
+                 c10::optional<at::Tensor> r, c10::optional<at::Tensor> h, int64_t n_base, double lora_scale,
+                 c10::optional<at::Tensor> row_mask, c10::optional<at::Tensor> q_out,
+                 c10::optional<at::Tensor> k_cache, c10::optional<at::Tensor> v_cache,
+                 c10::optional<at::Tensor> slots, c10::optional<at::Tensor> positions,
+                 c10::optional<at::Tensor> cos_sin, c10::optional<at::Tensor> q_norm_w,
+                 c10::optional<at::Tensor> k_norm_w, double eps, int64_t hq, int64_t hkv, int64_t page,
+                 int64_t max_ctas) {
+  check_dev(a, "gemm A");
+  check_dev(b, "gemm B");
+  UNO_CHECK_BF16(a);
+  UNO_CHECK_BF16(b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: shape mismatch");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm operands must be K-contiguous");
+  GemmParams p{};
+  p.M = a.size(0);
+  p.N = b.size(0);
+  p.K = a.size(1);
+  if (p.M == 0) return;
+  p.C = ptr_or_null<__nv_bfloat16>(c);
+  p.ldc = c.has_value() ? c->stride(0) : 0;
+  p.R = ptr_or_null<const __nv_bfloat16>(r);
+  p.ldr = r.has_value() ? r->stride(0) : 0;
+  p.H = ptr_or_null<__nv_bfloat16>(h);
+  p.ldh = h.has_value() ? h->stride(0) : 0;
+  TORCH_CHECK(p.ldc % 8 == 0 && p.ldr % 8 == 0 && p.ldh % 8 == 0, "output strides must be multiples of 8");
+  p.n_base = n_base;
+  p.lora_scale = lora_scale;
+  p.row_mask = ptr_or_null<const float>(row_mask);
+  p.q_out = ptr_or_null<__nv_bfloat16>(q_out);
+  p.k_cache = ptr_or_null<__nv_bfloat16>(k_cache);
+  p.v_cache = ptr_or_null<__nv_bfloat16>(v_cache);
+  p.slots = ptr_or_null<const int64_t>(slots);
+  p.positions = ptr_or_null<const int64_t>(positions);
+  p.cos_sin = ptr_or_null<const float>(cos_sin);
+  p.q_norm_w = ptr_or_null<const __nv_bfloat16>(q_norm_w);
+  p.k_norm_w = ptr_or_null<const __nv_bfloat16>(k_norm_w);
+  p.eps = eps;
+  p.num_q_heads = hq;
+  p.num_kv_heads = hkv;
+  p.page_size = page;
+  p.err = device_error_flag();
+  int tile = pick_bn(p.M, p.N, (int)bn);
+  if ((epi == 1 || epi == 4 || epi == 5 || epi == 6) && tile == 64) tile = 128;
+  gemm_dispatch((int)epi, tile, a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), p, cur_stream(), (int)max_ctas);
+}
+
+static void rms_norm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, at::Tensor& y,
+                     double eps, int64_t groups) {
+  rmsnorm_launch(x, residual, w, y, eps, (int)groups);
+}
+
+static void attention(const at::Tensor& q, at::Tensor& o, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      const at::Tensor& block_tables, c10::optional<at::Tensor> prefix_lens,
+                      c10::optional<at::Tensor> suffix_mask, c10::optional<at::Tensor> cu_q,
+                      c10::optional<at::Tensor> cu_k, int64_t mode, int64_t B, int64_t Q, int64_t max_q,
+                      double scale, int64_t num_splits, int64_t keys_per_split, c10::optional<at::Tensor> o_part,
+                      c10::optional<at::Tensor> lse_part) {
+  check_dev(q, "q");
+  check_dev(o, "attention output");
+  check_dev(k_cache, "k_cache");
+  check_dev(v_cache, "v_cache");
+  check_dev(block_tables, "block_tables");
+  UNO_CHECK_BF16(q);
+  UNO_CHECK_CONTIG(q);
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt, "block_tables must be int32");
+  TORCH_CHECK(o.is_contiguous() && o.numel() == q.numel(), "attention output must match q");
+  AttnLaunch a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.o_part = ptr_or_null<float>(o_part);
+  a.lse_part = ptr_or_null<float>(lse_part);
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.num_pages = k_cache.size(0);
+  a.hkv = k_cache.size(1);
+  a.page = k_cache.size(2);
+  a.head_dim = k_cache.size(3);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = block_tables.stride(0);
+  a.prefix_lens = ptr_or_null<const int>(prefix_lens);
+  a.suffix_mask = ptr_or_null<const int64_t>(suffix_mask);
+  a.cu_q = ptr_or_null<const int>(cu_q);
+  a.cu_k = ptr_or_null<const int>(cu_k);
+  a.B = B;
+  a.Q = Q;
+  a.T = q.size(0);
+  a.max_q = max_q;
+  a.hq = q.size(1);
+  a.scale = scale;
+  a.mode = mode;
+  a.num_splits = num_splits;
+  a.keys_per_split = keys_per_split;
+  a.err = device_error_flag();
+  if (a.T == 0 || B == 0) return;
+  paged_attention_launch(a, cur_stream());
+}
+
+}  // namespace uno
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemm", &uno::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("rms_norm", &uno::rms_norm);
+  m.def("embedding", &uno::embedding_launch);
+  m.def("silu_mul", &uno::silu_mul_launch);
+  m.def("qk_norm_rope_store", &uno::qk_norm_rope_store_launch);
+  m.def("copy_tree_kv", &uno::copy_tree_kv_launch);
+  m.def("attention", &uno::attention);
+  m.def("argmax", &uno::argmax_launch);
+  m.def("gumbel_sample", &uno::gumbel_sample_launch);
+  m.def("fused_verify", &uno::fused_verify_launch);
+  m.def("topk_lse", &uno::topk_lse_launch);
+  m.def("build_tree", &uno::build_tree_launch);
+  m.def("walk_tree", &uno::walk_tree_launch);
+  m.def("error_flag", &uno::read_error_flag, py::arg("reset") = false);
+}

@@ -1,0 +1,586 @@
+// Sampling, Psi-Spec verification and draft-tree kernels.
+//
+// Randomness: element v of row r in call (seed, offset) uses Philox-4x32-10
+// with key (seed, offset) and counter (v / 4, r, stream id, 0); the four 32-bit
+// outputs serve four consecutive vocabulary entries.  The values depend only on
+// (seed, offset, row, v), so every TP rank that makes the same call draws the
+// same numbers and a partial vocabulary shard can be sampled consistently.
+//
+// * argmax_kernel           greedy decoding (lowest index wins ties)
+// * gumbel_sample_kernel    categorical sample of softmax(x / T) as
+//                           argmax(x / T - log(E)), E ~ Exp(1)
+// * fused_verify_kernel     speculative acceptance test + residual resample
+//                           from raw target/draft logits (two passes over V);
+//                           semantics of ``engine/fused_verify_kernel.py:8-98``
+// * topk_lse_kernel         per-row top-K token ids with log-softmax values
+//                           (draft-tree candidates, ``engine/tree_builder.py:8-127``)
+// * build_tree_kernel       best-first fixed-budget tree, one warp per request
+//                           (``engine/tree_builder.py:130-330``)
+// * walk_tree_kernel        target-sample walk of the tree (``engine/tree_walk.py:8-146``)
+#include "common.cuh"
+#include "uno_ops.h"
+
+namespace uno {
+
+constexpr int SAMPLE_THREADS = 512;
+
+struct ArgBest {
+  float v;
+  int i;
+};
+
+__device__ __forceinline__ ArgBest better(ArgBest a, ArgBest b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+
+__device__ __forceinline__ ArgBest warp_best(ArgBest a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgBest b{__shfl_xor_sync(0xffffffff, a.v, o), __shfl_xor_sync(0xffffffff, a.i, o)};
+    a = better(a, b);
+  }
+  return a;
+}
+
+__device__ ArgBest block_best(ArgBest a) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  a = warp_best(a);
+  __syncthreads();
+  if (lane == 0) {
+    sv[warp] = a.v;
+    si[warp] = a.i;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    ArgBest b{-INFINITY, 0x7fffffff};
+    if (lane < (int)(blockDim.x >> 5)) b = ArgBest{sv[lane], si[lane]};
+    b = warp_best(b);
+    if (lane == 0) {
+      sv[0] = b.v;
+      si[0] = b.i;
+    }
+  }
+  __syncthreads();
+  return ArgBest{sv[0], si[0]};
+}
+
+__device__ float block_sum(float v) {
+  __shared__ float s[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) s[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (int)(blockDim.x >> 5) ? s[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) s[0] = t;
+  }
+  __syncthreads();
+  return s[0];
+}
+
+__device__ float block_max(float v) {
+  __shared__ float s[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) s[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (int)(blockDim.x >> 5) ? s[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) s[0] = t;
+  }
+  __syncthreads();
+  return s[0];
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
+  uint4 w = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Gumbel noise -log(E), E = -log(U), for 8 consecutive entries starting at v0 (v0 % 4 == 0).
+__device__ __forceinline__ void gumbel8(uint32_t seed, uint32_t offset, uint32_t row, uint32_t stream, int v0,
+                                        float* g) {
+  Philox4 a = philox4x32_10((uint32_t)(v0 >> 2), row, stream, 0u, seed, offset);
+  Philox4 b = philox4x32_10((uint32_t)(v0 >> 2) + 1u, row, stream, 0u, seed, offset);
+  const uint32_t bits[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) g[i] = -__logf(-__logf(u01(bits[i])));
+}
+
+__device__ __forceinline__ float gumbel1(uint32_t seed, uint32_t offset, uint32_t row, uint32_t stream, int v) {
+  Philox4 a = philox4x32_10((uint32_t)(v >> 2), row, stream, 0u, seed, offset);
+  const uint32_t bits[4] = {a.x, a.y, a.z, a.w};
+  return -__logf(-__logf(u01(bits[v & 3])));
+}
+
+// ------------------------------------------------------------------ argmax
+__global__ void __launch_bounds__(SAMPLE_THREADS) argmax_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V,
+                                                               int64_t* __restrict__ out) {
+  const __nv_bfloat16* row = x + (size_t)blockIdx.x * ld;
+  ArgBest best{-INFINITY, 0x7fffffff};
+  const int nvec = V / 8;
+  for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
+    float v[8];
+    load8(row + c * 8, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best = better(best, ArgBest{v[i], c * 8 + i});
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgBest{__bfloat162float(row[i]), i});
+  best = block_best(best);
+  if (threadIdx.x == 0) out[blockIdx.x] = best.i;
+}
+
+// ---------------------------------------------------------- gumbel sample
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+    gumbel_sample_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V, float inv_temp, uint32_t seed,
+                         uint32_t offset, int64_t* __restrict__ out) {
+  const __nv_bfloat16* row = x + (size_t)blockIdx.x * ld;
+  ArgBest best{-INFINITY, 0x7fffffff};
+  const int nvec = V / 8;
+  for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
+    float v[8], g[8];
+    load8(row + c * 8, v);
+    gumbel8(seed, offset, blockIdx.x, 1u, c * 8, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best = better(best, ArgBest{v[i] * inv_temp + g[i], c * 8 + i});
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x)
+    best = better(best, ArgBest{__bfloat162float(row[i]) * inv_temp + gumbel1(seed, offset, blockIdx.x, 1u, i), i});
+  best = block_best(best);
+  if (threadIdx.x == 0) out[blockIdx.x] = best.i;
+}
+
+// ------------------------------------------------------------ fused verify
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+    fused_verify_kernel(const __nv_bfloat16* __restrict__ clean, int64_t ldc, const __nv_bfloat16* __restrict__ draft,
+                        int64_t ldd, const int64_t* __restrict__ spec, int V, float inv_temp, uint32_t seed,
+                        uint32_t offset, int32_t* __restrict__ accepted, int64_t* __restrict__ corr) {
+  const int r = blockIdx.x;
+  const __nv_bfloat16* c = clean + (size_t)r * ldc;
+  const __nv_bfloat16* d = draft + (size_t)r * ldd;
+  const int nvec = V / 8;
+  // pass 1: max of both rows, then sums
+  float cm = -INFINITY, dm = -INFINITY;
+  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+    float a[8], b[8];
+    load8(c + k * 8, a);
+    load8(d + k * 8, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cm = fmaxf(cm, a[i]);
+      dm = fmaxf(dm, b[i]);
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    cm = fmaxf(cm, __bfloat162float(c[i]));
+    dm = fmaxf(dm, __bfloat162float(d[i]));
+  }
+  cm = block_max(cm) * inv_temp;
+  dm = block_max(dm) * inv_temp;
+  float cs = 0.f, ds = 0.f;
+  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+    float a[8], b[8];
+    load8(c + k * 8, a);
+    load8(d + k * 8, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cs += __expf(a[i] * inv_temp - cm);
+      ds += __expf(b[i] * inv_temp - dm);
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    cs += __expf(__bfloat162float(c[i]) * inv_temp - cm);
+    ds += __expf(__bfloat162float(d[i]) * inv_temp - dm);
+  }
+  cs = block_sum(cs);
+  ds = block_sum(ds);
+  const int64_t s = spec[r];
+  const float ps = __expf(__bfloat162float(c[s]) * inv_temp - cm) / cs;
+  const float qs = __expf(__bfloat162float(d[s]) * inv_temp - dm) / ds;
+  const float ratio = qs > 0.f ? ps / qs : 0.f;
+  Philox4 ur = philox4x32_10(0u, (uint32_t)r, 2u, 0u, seed, offset);
+  const float u = u01(ur.x);
+  const bool acc = (ratio >= 1.f) || (u < ratio);
+  if (acc) {
+    if (threadIdx.x == 0) {
+      accepted[r] = 1;
+      corr[r] = 0;
+    }
+    return;
+  }
+  // pass 2: Gumbel-max over log(max(p - q, 0))
+  const float cinv = 1.f / cs, dinv = 1.f / ds;
+  ArgBest best{-INFINITY, 0x7fffffff};
+  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+    float a[8], b[8], g[8];
+    load8(c + k * 8, a);
+    load8(d + k * 8, b);
+    gumbel8(seed, offset, r, 3u, k * 8, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float res = __expf(a[i] * inv_temp - cm) * cinv - __expf(b[i] * inv_temp - dm) * dinv;
+      if (res > 0.f) best = better(best, ArgBest{__logf(res) + g[i], k * 8 + i});
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    const float res = __expf(__bfloat162float(c[i]) * inv_temp - cm) * cinv -
+                      __expf(__bfloat162float(d[i]) * inv_temp - dm) * dinv;
+    if (res > 0.f) best = better(best, ArgBest{__logf(res) + gumbel1(seed, offset, r, 3u, i), i});
+  }
+  best = block_best(best);
+  if (threadIdx.x == 0) {
+    accepted[r] = 0;
+    corr[r] = best.i == 0x7fffffff ? s : best.i;
+  }
+}
+
+// ----------------------------------------------------------- top-K + LSE
+// One CTA per draft row.  Each thread keeps a sorted local top-K of its strided
+// slice; the CTA then extracts the global top-K by K rounds of block argmax.
+constexpr int TOPK_MAX = 32;
+constexpr int TOPK_THREADS = 256;
+
+__global__ void __launch_bounds__(TOPK_THREADS)
+    topk_lse_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V, int K, float inv_temp,
+                    int64_t* __restrict__ top_ids, float* __restrict__ top_lp) {
+  __shared__ float cand_v[TOPK_THREADS * 8];
+  __shared__ int cand_i[TOPK_THREADS * 8];
+  const __nv_bfloat16* row = x + (size_t)blockIdx.x * ld;
+  // local top-min(K,8) per thread, kept sorted descending
+  const int L = K < 8 ? K : 8;
+  float lv[8];
+  int li[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lv[i] = -INFINITY;
+    li[i] = 0x7fffffff;
+  }
+  float m = -INFINITY;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float val = __bfloat162float(row[v]) * inv_temp;
+    m = fmaxf(m, val);
+    if (val > lv[L - 1] || (val == lv[L - 1] && v < li[L - 1])) {
+      int pos = L - 1;
+      while (pos > 0 && (val > lv[pos - 1] || (val == lv[pos - 1] && v < li[pos - 1]))) {
+        lv[pos] = lv[pos - 1];
+        li[pos] = li[pos - 1];
+        --pos;
+      }
+      lv[pos] = val;
+      li[pos] = v;
+    }
+  }
+  m = block_max(m);
+  float s = 0.f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) s += __expf(__bfloat162float(row[v]) * inv_temp - m);
+  s = block_sum(s);
+  const float lse = m + __logf(s);
+  // A thread contributes at most L candidates; if K > L a thread could own
+  // more than L of the global top-K, so rescan in that case (K > 8 is rare).
+  if (K > L) {
+    // fallback: K rounds of exclusion argmax over the whole row
+    float last_v = INFINITY;
+    int last_i = -1;
+    for (int k = 0; k < K; ++k) {
+      ArgBest best{-INFINITY, 0x7fffffff};
+      for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float val = __bfloat162float(row[v]) * inv_temp;
+        const bool after = (val < last_v) || (val == last_v && v > last_i);
+        if (after) best = better(best, ArgBest{val, v});
+      }
+      best = block_best(best);
+      if (threadIdx.x == 0) {
+        top_ids[(size_t)blockIdx.x * K + k] = best.i;
+        top_lp[(size_t)blockIdx.x * K + k] = best.v - lse;
+      }
+      last_v = best.v;
+      last_i = best.i;
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    cand_v[threadIdx.x * 8 + i] = lv[i];
+    cand_i[threadIdx.x * 8 + i] = li[i];
+  }
+  __syncthreads();
+  for (int k = 0; k < K; ++k) {
+    ArgBest best{-INFINITY, 0x7fffffff};
+    int slot = -1;
+    for (int j = threadIdx.x; j < TOPK_THREADS * 8; j += blockDim.x) {
+      ArgBest c{cand_v[j], cand_i[j]};
+      ArgBest nb = better(best, c);
+      if (nb.i != best.i || nb.v != best.v) {
+        best = nb;
+        slot = j;
+      }
+    }
+    ArgBest win = block_best(best);
+    if (best.i == win.i && best.v == win.v && slot >= 0 && win.i != 0x7fffffff) {
+      cand_v[slot] = -INFINITY;
+      cand_i[slot] = 0x7fffffff;
+    }
+    if (threadIdx.x == 0) {
+      top_ids[(size_t)blockIdx.x * K + k] = win.i;
+      top_lp[(size_t)blockIdx.x * K + k] = win.v - lse;
+    }
+    __syncthreads();
+  }
+}
+
+// --------------------------------------------------------------- tree build
+// One warp per request.  Node n's next candidate is its lowest-rank unused
+// child among the depth-d top-K list (children are added in rank order), so the
+// global best candidate is the best head over all nodes.  Priority: larger
+// cumulative log-prob, then smaller depth, rank, token id, parent index.
+__global__ void build_tree_kernel(const int64_t* __restrict__ roots, const int64_t* __restrict__ cand_ids,
+                                  const float* __restrict__ cand_lp, int D, int K, int Qn,
+                                  int64_t* __restrict__ tok, int64_t* __restrict__ par, int64_t* __restrict__ dep,
+                                  float* __restrict__ mass, int* __restrict__ count_out) {
+  const int b = blockIdx.x, lane = threadIdx.x;
+  __shared__ int s_ptr[64];
+  __shared__ int s_dep[64];
+  __shared__ float s_mass[64];
+  const int64_t* ids = cand_ids + (size_t)b * D * K;
+  const float* lps = cand_lp + (size_t)b * D * K;
+  int64_t* T = tok + (size_t)b * Qn;
+  int64_t* P = par + (size_t)b * Qn;
+  int64_t* Dp = dep + (size_t)b * Qn;
+  float* Ms = mass + (size_t)b * Qn;
+  if (lane == 0) {
+    T[0] = roots[b];
+    P[0] = -1;
+    Dp[0] = 0;
+    Ms[0] = 0.f;
+  }
+  for (int i = lane; i < 64; i += 32) {
+    s_ptr[i] = 0;
+    s_dep[i] = 0;
+    s_mass[i] = 0.f;
+  }
+  __syncwarp();
+  int n = 1;
+  for (; n < Qn; ++n) {
+    // each lane examines nodes lane and lane + 32
+    float bv = -INFINITY;
+    int bd = 0x7fffffff, br = 0x7fffffff, bnode = -1;
+    int64_t btok = 0x7fffffffffffffffll;
+    for (int node = lane; node < n; node += 32) {
+      const int d = s_dep[node], r = s_ptr[node];
+      if (d >= D || r >= K) continue;
+      const float v = s_mass[node] + lps[d * K + r];
+      const int64_t t = ids[d * K + r];
+      bool take = false;
+      if (bnode < 0 || v > bv) take = true;
+      else if (v == bv) {
+        if (d + 1 < bd) take = true;
+        else if (d + 1 == bd) {
+          if (r < br) take = true;
+          else if (r == br) {
+            if (t < btok) take = true;
+            else if (t == btok && node < bnode) take = true;
+          }
+        }
+      }
+      if (take) {
+        bv = v;
+        bd = d + 1;
+        br = r;
+        btok = t;
+        bnode = node;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffff, bv, o);
+      const int od = __shfl_xor_sync(0xffffffff, bd, o);
+      const int orr = __shfl_xor_sync(0xffffffff, br, o);
+      const long long ot = __shfl_xor_sync(0xffffffff, (long long)btok, o);
+      const int on = __shfl_xor_sync(0xffffffff, bnode, o);
+      bool take = false;
+      if (on >= 0) {
+        if (bnode < 0 || ov > bv) take = true;
+        else if (ov == bv) {
+          if (od < bd) take = true;
+          else if (od == bd) {
+            if (orr < br) take = true;
+            else if (orr == br) {
+              if (ot < btok) take = true;
+              else if (ot == btok && on < bnode) take = true;
+            }
+          }
+        }
+      }
+      if (take) {
+        bv = ov;
+        bd = od;
+        br = orr;
+        btok = ot;
+        bnode = on;
+      }
+    }
+    if (bnode < 0) break;  // candidate set exhausted
+    if (lane == 0) {
+      T[n] = btok;
+      P[n] = bnode;
+      Dp[n] = bd;
+      Ms[n] = bv;
+      s_ptr[bnode] += 1;
+      s_dep[n] = bd;
+      s_mass[n] = bv;
+      s_ptr[n] = 0;
+    }
+    __syncwarp();
+  }
+  if (lane == 0) count_out[b] = n;
+  for (int i = n + lane; i < Qn; i += 32) {  // unused slots: unreachable padding
+    T[i] = 0;
+    P[i] = -2;  // never equals a walk position, never an ancestor
+    Dp[i] = 1;
+    Ms[i] = -INFINITY;
+  }
+}
+
+// --------------------------------------------------------------- tree walk
+__global__ void walk_tree_kernel(const int64_t* __restrict__ tok, const int64_t* __restrict__ par,
+                                 const int64_t* __restrict__ tgt, int Qn, int max_depth, int64_t pad,
+                                 int64_t* __restrict__ committed, int64_t* __restrict__ accepted,
+                                 int64_t* __restrict__ lengths) {
+  const int b = blockIdx.x, lane = threadIdx.x;
+  const int n_cached = max_depth + 1;
+  const int64_t* T = tok + (size_t)b * Qn;
+  const int64_t* P = par + (size_t)b * Qn;
+  const int64_t* G = tgt + (size_t)b * Qn;
+  int64_t* C = committed + (size_t)b * (n_cached + 1);
+  int64_t* A = accepted + (size_t)b * n_cached;
+  for (int i = lane; i <= n_cached; i += 32) C[i] = pad;
+  for (int i = lane; i < n_cached; i += 32) A[i] = -1;
+  __syncwarp();
+  int cur = 0;
+  int64_t len = 1;
+  if (lane == 0) {
+    C[0] = T[0];
+    A[0] = 0;
+  }
+  for (int step = 1; step <= n_cached; ++step) {
+    const int64_t s = G[cur];
+    if (lane == 0) C[step] = s;
+    len = step + 1;
+    if (step > max_depth) break;
+    int child = 0x7fffffff;
+    for (int j = lane; j < Qn; j += 32)
+      if (P[j] == cur && T[j] == s && j < child) child = j;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) child = min(child, __shfl_xor_sync(0xffffffff, child, o));
+    if (child == 0x7fffffff) break;
+    if (lane == 0) A[step] = child;
+    cur = child;
+  }
+  if (lane == 0) lengths[b] = len;
+}
+
+// ------------------------------------------------------------------- host
+void argmax_launch(const at::Tensor& x, at::Tensor& out) {
+  check_dev(x, "logits");
+  check_dev(out, "out");
+  const int rows = x.size(0), V = x.size(1);
+  if (rows == 0) return;
+  TORCH_CHECK(x.stride(0) % 8 == 0, "row stride must be a multiple of 8");
+  argmax_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                           x.stride(0), V, out.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gumbel_sample_launch(const at::Tensor& x, at::Tensor& out, double inv_temp, int64_t seed, int64_t offset) {
+  check_dev(x, "logits");
+  check_dev(out, "out");
+  const int rows = x.size(0), V = x.size(1);
+  if (rows == 0) return;
+  TORCH_CHECK(x.stride(0) % 8 == 0, "row stride must be a multiple of 8");
+  gumbel_sample_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), V, (float)inv_temp, (uint32_t)seed,
+      (uint32_t)offset, out.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void fused_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at::Tensor& spec, double inv_temp,
+                         int64_t seed, int64_t offset, at::Tensor& accepted, at::Tensor& corr) {
+  check_dev(clean, "clean");
+  check_dev(draft, "draft");
+  check_dev(spec, "spec");
+  check_dev(accepted, "accepted");
+  check_dev(corr, "corr");
+  const int rows = clean.size(0), V = clean.size(1);
+  if (rows == 0) return;
+  TORCH_CHECK(clean.stride(0) % 8 == 0 && draft.stride(0) % 8 == 0, "row stride must be a multiple of 8");
+  fused_verify_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(clean.data_ptr()), clean.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(draft.data_ptr()), draft.stride(0), spec.data_ptr<int64_t>(), V,
+      (float)inv_temp, (uint32_t)seed, (uint32_t)offset, accepted.data_ptr<int32_t>(), corr.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void topk_lse_launch(const at::Tensor& x, int K, double inv_temp, at::Tensor& ids, at::Tensor& lp) {
+  check_dev(x, "logits");
+  check_dev(ids, "ids");
+  check_dev(lp, "lp");
+  const int rows = x.size(0), V = x.size(1);
+  TORCH_CHECK(K >= 1 && K <= TOPK_MAX, "candidate top-k must be in [1, 32]");
+  if (rows == 0) return;
+  topk_lse_kernel<<<rows, TOPK_THREADS, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                           x.stride(0), V, K, (float)inv_temp,
+                                                           ids.data_ptr<int64_t>(), lp.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at::Tensor& lp, int Qn, at::Tensor& tok,
+                       at::Tensor& par, at::Tensor& dep, at::Tensor& mass, at::Tensor& count) {
+  check_dev(roots, "roots");
+  check_dev(ids, "ids");
+  check_dev(lp, "lp");
+  check_dev(tok, "tok");
+  check_dev(par, "par");
+  check_dev(dep, "dep");
+  check_dev(mass, "mass");
+  check_dev(count, "count");
+  const int B = ids.size(0), D = ids.size(1), K = ids.size(2);
+  TORCH_CHECK(Qn <= 64, "tree verification supports at most 64 nodes");
+  if (B == 0) return;
+  build_tree_kernel<<<B, 32, 0, cur_stream()>>>(roots.data_ptr<int64_t>(), ids.data_ptr<int64_t>(),
+                                                lp.data_ptr<float>(), D, K, Qn, tok.data_ptr<int64_t>(),
+                                                par.data_ptr<int64_t>(), dep.data_ptr<int64_t>(),
+                                                mass.data_ptr<float>(), count.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void walk_tree_launch(const at::Tensor& tok, const at::Tensor& par, const at::Tensor& tgt, int max_depth, int64_t pad,
+                      at::Tensor& committed, at::Tensor& accepted, at::Tensor& lengths) {
+  check_dev(tok, "tok");
+  check_dev(par, "par");
+  check_dev(tgt, "tgt");
+  check_dev(committed, "committed");
+  check_dev(accepted, "accepted");
+  check_dev(lengths, "lengths");
+  const int B = tok.size(0), Qn = tok.size(1);
+  if (B == 0) return;
+  walk_tree_kernel<<<B, 32, 0, cur_stream()>>>(tok.data_ptr<int64_t>(), par.data_ptr<int64_t>(),
+                                               tgt.data_ptr<int64_t>(), Qn, max_depth, pad,
+                                               committed.data_ptr<int64_t>(), accepted.data_ptr<int64_t>(),
+                                               lengths.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace uno

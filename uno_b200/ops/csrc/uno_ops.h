@@ -1,0 +1,87 @@
+// Host-side declarations shared by the uno_b200 CUDA translation units.
+#pragma once
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAException.h>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <algorithm>
+#include <cstdint>
+
+namespace uno {
+
+// Parameters of the tcgen05 GEMM (gemm_tcgen05.cu) and its fused epilogues.
+struct GemmParams {
+  int M, N, K;
+  int num_m, num_n;
+  __nv_bfloat16* C;
+  int ldc;
+  const __nv_bfloat16* R;  // residual / pre-activation input
+  int ldr;
+  __nv_bfloat16* H;        // LoRA hidden output
+  int ldh;
+  int n_base;
+  float lora_scale;
+  const float* row_mask;
+  // QK-norm / RoPE / KV store
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  const int64_t* slots;
+  const int64_t* positions;
+  const float* cos_sin;
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  float eps;
+  int num_q_heads, num_kv_heads, page_size;
+  int* err;
+};
+void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p,
+                   cudaStream_t stream, int max_ctas);
+int pick_bn(int M, int N, int forced);
+
+struct AttnLaunch {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* o;
+  float* o_part;
+  float* lse_part;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  int num_pages;
+  const int* block_tables;
+  int bt_stride;
+  const int* prefix_lens;
+  const int64_t* suffix_mask;
+  const int* cu_q;
+  const int* cu_k;
+  int B, Q, T, max_q;
+  int hq, hkv, head_dim, page;
+  int num_splits, keys_per_split;
+  float scale;
+  int mode;
+  int* err;
+};
+void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream);
+
+// Device error word (allocated once per device by the bindings).
+int* device_error_flag();
+
+// Every pointer handed to a kernel must live on the current CUDA device: a
+// host or foreign-device tensor is rejected on the host instead of faulting.
+inline void check_dev(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda(), what, " must be a CUDA tensor");
+  int dev;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  TORCH_CHECK(t.get_device() == dev, what, " is on cuda:", t.get_device(), " but the current device is cuda:", dev);
+}
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+#define UNO_CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define UNO_CHECK_BF16(t) TORCH_CHECK((t).scalar_type() == at::kBFloat16, #t " must be bfloat16")
+#define UNO_CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+
+}  // namespace uno

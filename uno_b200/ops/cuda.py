@@ -1,0 +1,313 @@
+"""CUDA implementations of the fused ops (thin wrappers over ``uno_b200._C``).
+
+Weight preparation for the sm_100a path (:func:`prepare_model`):
+
+* ``gate_up_proj`` rows are interleaved in 64-row groups ``[gate_j | up_j]`` so
+  the GEMM epilogue can apply SiLU(gate) * up inside one output tile;
+* a layer with a gated LoRA adapter stores ``[W ; A_cat]`` as one weight
+  (``layer.weight`` becomes a view of its first N rows).  One GEMM then emits
+  the base output and the rank-R hidden ``scale * mask * (x A^T)`` (its
+  epilogue applies the row mask), and a second GEMM with K = R adds
+  ``hidden . B_cat^T`` and runs the layer's real epilogue (plain, SiLU*up or
+  QK-norm + RoPE + paged KV store).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from uno_b200.layers.meta import ForwardMeta, Mode
+from uno_b200.parallel import state as tp
+
+_C = None
+
+EPI_STORE, EPI_SILU, EPI_LORA_SPLIT, EPI_ADD, EPI_ADD_SILU, EPI_QKROPE, EPI_ADD_QKROPE = range(7)
+INTERLEAVE = 64
+
+
+def ext():
+    """Import the compiled extension; raise loudly when it is missing."""
+    global _C
+    if _C is None:
+        try:
+            from uno_b200 import _C as mod
+        except ImportError as e:  # pragma: no cover - depends on the build
+            raise RuntimeError(
+                "uno_b200._C is not built; run `python setup.py build_ext --inplace` "
+                "(CUDA tensors have no fallback path)"
+            ) from e
+        _C = mod
+    return _C
+
+
+def error_flag(reset: bool = False) -> int:
+    return int(ext().error_flag(reset))
+
+
+def _gemm(a, b, epi, *, c=None, r=None, h=None, n_base=0, scale=0.0, row_mask=None, q_out=None,
+          k_cache=None, v_cache=None, slots=None, positions=None, cos_sin=None, q_norm_w=None,
+          k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0):
+    ext().gemm(a, b, epi, bn, c, r, h, n_base, scale, row_mask, q_out, k_cache, v_cache, slots, positions,
+               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, bn: int = 0) -> torch.Tensor:
+    """Plain ``a @ b.T`` on the tcgen05 GEMM (bf16 out)."""
+    out = torch.empty(a.shape[0], b.shape[0], device=a.device, dtype=torch.bfloat16)
+    _gemm(a, b, EPI_STORE, c=out, bn=bn)
+    return out
+
+
+# ------------------------------------------------------------ weight prep
+def interleave_gate_up(w: torch.Tensor, group: int = INTERLEAVE) -> torch.Tensor:
+    """Rows [gate(I); up(I)] -> [g_0..g_63, u_0..u_63, g_64.., u_64.., ...]."""
+    two_i = w.shape[0]
+    inter = two_i // 2
+    if inter % group:
+        raise ValueError(f"intermediate size {inter} must be a multiple of {group}")
+    gate, up = w[:inter], w[inter:]
+    blocks = inter // group
+    stacked = torch.stack([gate.reshape(blocks, group, *w.shape[1:]), up.reshape(blocks, group, *w.shape[1:])], dim=1)
+    return stacked.reshape(two_i, *w.shape[1:]).contiguous()
+
+
+@torch.no_grad()
+def prepare_linear(layer, interleave: bool = False) -> None:
+    if getattr(layer, "_uno_prepared", False):
+        return
+    if layer.bias is not None:
+        raise NotImplementedError("biased linears are not supported on the sm_100a path")
+    w = layer.weight.data
+    if interleave:
+        w = interleave_gate_up(w)
+    if layer.has_lora:
+        if layer.lora_a_cat is None:
+            layer.pack_lora()
+        b_cat = layer.lora_b_cat
+        if interleave:
+            b_cat = interleave_gate_up(b_cat)
+        ext_w = torch.cat([w, layer.lora_a_cat.to(w.dtype)], dim=0).contiguous()
+        layer.weight_ext = ext_w
+        layer.weight.data = ext_w[: w.shape[0]]
+        layer.lora_b_dev = b_cat.to(w.dtype).contiguous()
+    else:
+        layer.weight.data = w.contiguous()
+    layer.interleaved = interleave
+    layer._uno_prepared = True
+
+
+def prepare_model(model) -> None:
+    for layer in model.model.layers:
+        attn, mlp = layer.self_attn, layer.mlp
+        prepare_linear(attn.qkv_proj)
+        prepare_linear(attn.o_proj)
+        prepare_linear(mlp.gate_up_proj, interleave=True)
+        prepare_linear(mlp.down_proj)
+
+
+# ------------------------------------------------------------------ norms
+def rms_norm(x, weight, eps, n_groups=1):
+    y = torch.empty_like(x)
+    ext().rms_norm(x.contiguous(), None, weight, y, float(eps), int(n_groups))
+    return y
+
+
+def add_rms_norm(x, residual, weight, eps, n_groups=1):
+    y = torch.empty_like(x)
+    res = residual.contiguous().clone() if not residual.is_contiguous() else residual
+    ext().rms_norm(x.contiguous(), res, weight, y, float(eps), int(n_groups))
+    return y, res
+
+
+# ----------------------------------------------------------------- linear
+def _row_parallel(layer) -> bool:
+    return layer.tp_dim == 1 and layer.tp_size > 1
+
+
+def _lora_split(x, layer, lora_mask):
+    """One GEMM over [W; A_cat]: base output and masked/scaled LoRA hidden."""
+    M = x.shape[0]
+    N = layer.weight.shape[0]
+    R = layer.lora_rank_total
+    buf = torch.empty(M, N + R, device=x.device, dtype=torch.bfloat16)
+    y, h = buf[:, :N], buf[:, N:]
+    _gemm(x, layer.weight_ext, EPI_LORA_SPLIT, c=y, h=h, n_base=N, scale=layer.lora_scaling,
+          row_mask=lora_mask)
+    if _row_parallel(layer):
+        tp.all_reduce(buf)
+    return y, h
+
+
+def linear(x, layer, lora_mask=None):
+    x = x.contiguous()
+    if lora_mask is not None and layer.has_lora:
+        y, h = _lora_split(x, layer, lora_mask)
+        _gemm(h, layer.lora_b_dev, EPI_ADD, c=y, r=y)
+        return y
+    y = torch.empty(x.shape[0], layer.weight.shape[0], device=x.device, dtype=torch.bfloat16)
+    _gemm(x, layer.weight, EPI_STORE, c=y)
+    if _row_parallel(layer):
+        tp.all_reduce(y)
+    return y
+
+
+def gate_up_silu(x, layer, lora_mask=None):
+    x = x.contiguous()
+    inter = layer.weight.shape[0] // 2
+    act = torch.empty(x.shape[0], inter, device=x.device, dtype=torch.bfloat16)
+    if lora_mask is not None and layer.has_lora:
+        pre, h = _lora_split(x, layer, lora_mask)
+        _gemm(h, layer.lora_b_dev, EPI_ADD_SILU, c=act, r=pre)
+        return act
+    _gemm(x, layer.weight, EPI_SILU, c=act)
+    return act
+
+
+def qkv_rope_store(x, layer, lora_mask, positions, cos_sin, q_norm_w, k_norm_w, eps, num_heads, num_kv_heads,
+                   head_dim, k_cache, v_cache, slot_mapping):
+    x = x.contiguous()
+    T = x.shape[0]
+    q = torch.empty(T, num_heads, head_dim, device=x.device, dtype=torch.bfloat16)
+    page = k_cache.shape[2] if k_cache.numel() else 0
+    kc = k_cache if k_cache.numel() else None
+    vc = v_cache if v_cache.numel() else None
+    slots = slot_mapping if kc is not None else torch.full((T,), -1, dtype=torch.int64, device=x.device)
+    if head_dim != 128:
+        qkv = linear(x, layer, lora_mask)
+        ext().qk_norm_rope_store(qkv, q, k_cache, v_cache, slots, positions, cos_sin, q_norm_w, k_norm_w,
+                                 float(eps), num_heads, num_kv_heads, head_dim, page)
+        return q
+    common = dict(q_out=q, k_cache=kc, v_cache=vc, slots=slots, positions=positions, cos_sin=cos_sin,
+                  q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=float(eps), hq=num_heads, hkv=num_kv_heads, page=page)
+    if lora_mask is not None and layer.has_lora:
+        pre, h = _lora_split(x, layer, lora_mask)
+        _gemm(h, layer.lora_b_dev, EPI_ADD_QKROPE, r=pre, **common)
+    else:
+        _gemm(x, layer.weight, EPI_QKROPE, **common)
+    return q
+
+
+# -------------------------------------------------------------- attention
+_SCRATCH: dict = {}
+
+
+def _scratch(device, numel: int, name: str) -> torch.Tensor:
+    key = (device, name)
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < numel:
+        buf = torch.empty(max(numel, 1), device=device, dtype=torch.float32)
+        _SCRATCH[key] = buf
+    return buf[:numel]
+
+
+def reserve_attention_scratch(device, max_tokens: int, num_heads: int, max_splits: int) -> None:
+    """Pre-size the split-K scratch so graph capture never reallocates it."""
+    _scratch(device, max_splits * max_tokens * num_heads * 128, "o_part")
+    _scratch(device, max_splits * max_tokens * num_heads, "lse")
+
+
+def plan_splits(B: int, hkv: int, qblocks: int, max_kv: int, sms: int = 148):
+    ctas = max(1, B * hkv * qblocks)
+    want = max(1, -(-2 * sms // ctas))
+    max_by_len = max(1, -(-max_kv // 512))
+    splits = min(want, max_by_len, 16)
+    if splits <= 1:
+        return 1, 0
+    kps = -(-max_kv // splits)
+    kps = -(-kps // 64) * 64
+    splits = -(-max_kv // kps)
+    return splits, kps
+
+
+def attention(q, k_cache, v_cache, meta: ForwardMeta, scale):
+    T, hq, d = q.shape
+    o = torch.empty(T, hq * d, device=q.device, dtype=torch.bfloat16)
+    hkv = k_cache.shape[1]
+    if meta.mode is Mode.PREFILL:
+        ext().attention(q, o, k_cache, v_cache, meta.block_tables, None, None, meta.cu_seqlens_q,
+                        meta.cu_seqlens_k, 1, meta.batch_size, 0, meta.max_seqlen_q, float(scale), 1, 0, None, None)
+        return o
+    B, Q = meta.batch_size, meta.seqlen_q
+    group = hq // hkv
+    rows = max(16, -(-Q * group // 16) * 16)
+    qpc = max(1, min(256, rows) // group)
+    qblocks = -(-Q // qpc)
+    max_kv = getattr(meta, "max_kv", 0) or (k_cache.shape[0] * k_cache.shape[2])
+    splits, kps = plan_splits(B, hkv, qblocks, max_kv)
+    o_part = lse = None
+    if splits > 1:
+        o_part = _scratch(q.device, splits * T * hq * 128, "o_part")
+        lse = _scratch(q.device, splits * T * hq, "lse")
+    ext().attention(q, o, k_cache, v_cache, meta.block_tables, meta.prefix_lens, meta.suffix_mask, None, None, 0,
+                    B, Q, Q, float(scale), splits, kps, o_part, lse)
+    return o
+
+
+# ------------------------------------------------------------ embeddings
+def embedding(ids, table, vocab_start=0):
+    out = torch.empty(ids.numel(), table.shape[1], device=ids.device, dtype=table.dtype)
+    ext().embedding(ids.reshape(-1).contiguous(), table, out, int(vocab_start))
+    if tp.tp_size() > 1:
+        tp.all_reduce(out)
+    return out
+
+
+def lm_head(x, weight):
+    return gemm(x.contiguous(), weight)
+
+
+# --------------------------------------------------------------- sampling
+def argmax(logits):
+    out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
+    ext().argmax(logits, out)
+    return out
+
+
+def sample_gumbel(logits, inv_temp, seed, offset):
+    out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
+    ext().gumbel_sample(logits, out, float(inv_temp), int(seed), int(offset))
+    return out
+
+
+def fused_verify(clean, draft, spec, inv_temp, seed, offset):
+    n = clean.shape[0]
+    acc = torch.empty(n, device=clean.device, dtype=torch.int32)
+    corr = torch.empty(n, device=clean.device, dtype=torch.int64)
+    ext().fused_verify(clean, draft, spec.contiguous(), float(inv_temp), int(seed), int(offset), acc, corr)
+    return acc, corr
+
+
+def build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature):
+    from uno_b200.engine.draft_tree import DraftTreeBatch
+
+    B, D, V = draft_logits.shape
+    K = min(int(candidate_top_k), V)
+    rows = draft_logits.reshape(B * D, V)
+    ids = torch.empty(B * D, K, device=rows.device, dtype=torch.int64)
+    lp = torch.empty(B * D, K, device=rows.device, dtype=torch.float32)
+    inv_t = 1.0 / temperature if temperature > 0 else 1.0
+    ext().topk_lse(rows, K, inv_t, ids, lp)
+    tok = torch.empty(B, max_nodes, device=rows.device, dtype=torch.int64)
+    par = torch.empty_like(tok)
+    dep = torch.empty_like(tok)
+    mass = torch.empty(B, max_nodes, device=rows.device, dtype=torch.float32)
+    count = torch.empty(B, device=rows.device, dtype=torch.int32)
+    ext().build_tree(root_tokens.contiguous(), ids.view(B, D, K), lp.view(B, D, K), int(max_nodes), tok, par, dep,
+                     mass, count)
+    return DraftTreeBatch(tok, par, dep, mass)
+
+
+def walk_tree(tokens, parents, targets, max_depth, pad_token_id):
+    B = tokens.shape[0]
+    committed = torch.empty(B, max_depth + 2, device=tokens.device, dtype=torch.int64)
+    accepted = torch.empty(B, max_depth + 1, device=tokens.device, dtype=torch.int64)
+    lengths = torch.empty(B, device=tokens.device, dtype=torch.int64)
+    ext().walk_tree(tokens.contiguous(), parents.contiguous(), targets.contiguous(), int(max_depth),
+                    int(pad_token_id), committed, accepted, lengths)
+    return committed, accepted, lengths
+
+
+def copy_tree_kv(kv_cache, tables, src, dst, page):
+    ext().copy_tree_kv(kv_cache, tables.contiguous(), src.contiguous(), dst.contiguous(), int(page))
