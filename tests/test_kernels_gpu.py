@@ -39,6 +39,23 @@ def test_gemm_store(C, M, N, K, bn):
     assert rel_err(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("splits", [2, 3, 4])
+def test_gemm_split_k(C, splits):
+    torch.manual_seed(splits)
+    M, N, K = 300, 1024, 2048
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    ref = a.float() @ b.float().T
+    for _ in range(3):  # counters must reset between launches
+        out = C.gemm(a, b, splits=splits)
+        assert rel_err(out, ref) < 1e-2
+    # fused epilogue through split-K: residual add
+    r = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    y = r.clone()
+    C._gemm(a, b, C.EPI_ADD, c=y, r=y, splits=splits)
+    assert rel_err(y, ref + r.float()) < 1e-2
+
+
 def test_gemm_silu_interleaved(C):
     torch.manual_seed(0)
     M, K, I = 200, 512, 384
@@ -52,25 +69,32 @@ def test_gemm_silu_interleaved(C):
     assert rel_err(act, ref) < 1e-2
 
 
-def test_gemm_lora_split_and_add(C):
+@pytest.mark.parametrize("splits", [1, 2])
+def test_gemm_lora_hidden_and_k_extension(C, splits):
     torch.manual_seed(1)
-    M, K, N, R = 96, 256, 512, 64
+    M, K, N, R = 96, 1024, 512, 64
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.05
     a = torch.randn(R, K, device=DEV, dtype=torch.bfloat16) * 0.05
     bmat = torch.randn(N, R, device=DEV, dtype=torch.bfloat16) * 0.05
     mask = (torch.arange(M, device=DEV) % 3 != 0).float()
-    wext = torch.cat([w, a]).contiguous()
-    buf = torch.empty(M, N + R, device=DEV, dtype=torch.bfloat16)
-    C._gemm(x, wext, C.EPI_LORA_SPLIT, c=buf[:, :N], h=buf[:, N:], n_base=N, scale=2.0, row_mask=mask)
-    y, h = buf[:, :N], buf[:, N:]
-    ref_y = x.float() @ w.float().T
+    h = torch.empty(M, R, device=DEV, dtype=torch.bfloat16)
+    C._gemm(x, a, C.EPI_ROWSCALE, c=h, scale=2.0, row_mask=mask, splits=splits)
     ref_h = 2.0 * mask[:, None] * (x.float() @ a.float().T)
-    assert rel_err(y, ref_y) < 1e-2
     assert rel_err(h, ref_h) < 1e-2
-    C._gemm(h, bmat, C.EPI_ADD, c=y, r=y)
-    ref = ref_y + h.float() @ bmat.float().T
+    y = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    C._gemm(x, w, C.EPI_STORE, c=y, a2=h, b2=bmat, splits=splits)
+    ref = x.float() @ w.float().T + h.float() @ bmat.float().T
     assert rel_err(y, ref) < 1e-2
+    # SiLU epilogue over the extended K loop (interleaved gate/up rows)
+    I = 256
+    wg = torch.randn(2 * I, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    bg = torch.randn(2 * I, R, device=DEV, dtype=torch.bfloat16) * 0.05
+    act = torch.empty(M, I, device=DEV, dtype=torch.bfloat16)
+    C._gemm(x, C.interleave_gate_up(wg), C.EPI_SILU, c=act, a2=h, b2=C.interleave_gate_up(bg), splits=splits)
+    gu = (x.float() @ wg.float().T + h.float() @ bg.float().T).bfloat16().float()
+    ref_act = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    assert rel_err(act, ref_act) < 1e-2
 
 
 def _ref_qkrope(qkv, positions, cos_sin, qw, kw, hq, hkv, eps):
@@ -107,14 +131,10 @@ def test_gemm_qk_rope_store(C, lora):
                   q_norm_w=qw, k_norm_w=kw, eps=1e-6, hq=hq, hkv=hkv, page=page)
     if lora:
         R = 64
-        a = torch.randn(R, K, device=DEV, dtype=torch.bfloat16) * 0.05
+        h = (torch.randn(T, R, device=DEV) * 0.5).bfloat16()
         bmat = torch.randn(N, R, device=DEV, dtype=torch.bfloat16) * 0.05
-        mask = torch.ones(T, device=DEV)
-        buf = torch.empty(T, N + R, device=DEV, dtype=torch.bfloat16)
-        C._gemm(x, torch.cat([w, a]).contiguous(), C.EPI_LORA_SPLIT, c=buf[:, :N], h=buf[:, N:], n_base=N,
-                scale=1.0, row_mask=mask)
-        C._gemm(buf[:, N:], bmat, C.EPI_ADD_QKROPE, r=buf[:, :N], **common)
-        qkv = (x.float() @ w.float().T).bfloat16().float() + (buf[:, N:].float() @ bmat.float().T)
+        C._gemm(x, w, C.EPI_QKROPE, a2=h, b2=bmat, **common)
+        qkv = x.float() @ w.float().T + h.float() @ bmat.float().T
     else:
         C._gemm(x, w, C.EPI_QKROPE, **common)
         qkv = x.float() @ w.float().T

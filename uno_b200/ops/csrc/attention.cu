@@ -81,7 +81,8 @@ __device__ __forceinline__ uint32_t tile_off(int key, int c) {
   return (uint32_t)((c >> 3) * (ATT_BK * 128) + key * 128 + (((c & 7) ^ (key & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(32 * 17)
+template <int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(32 * 17)
   const int qblk = blockIdx.x, b = blockIdx.y;
   const int h = blockIdx.z % p.hkv, split = blockIdx.z / p.hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_compute = (blockDim.x >> 5) - 1;
+  constexpr int n_compute = NW;
 
   // ---- geometry of this request
   int q_begin, nq, kv_len, prefix;
@@ -374,6 +375,18 @@ __global__ void attention_combine_kernel(const float* __restrict__ o_part, const
 
 CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 
+template <int NW>
+static void launch_attn(dim3 grid, int smem, const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p,
+                        cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(paged_attention_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  paged_attention_kernel<NW><<<grid, 32 * (NW + 1), smem, stream>>>(tk, tv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
   TORCH_CHECK(a.head_dim == ATT_D, "paged attention supports head_dim 128");
   TORCH_CHECK(a.page % ATT_BK == 0, "page size must be a multiple of 64");
@@ -401,9 +414,11 @@ void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = a.err;
   // rows per CTA: cover all (query, head) rows of a decode request when
-  // possible; prefill uses 128-row blocks.
+  // possible (at most 8 compute warps = 128 rows); prefill uses 128-row blocks.
   int rows_needed = (a.mode == MODE_SUFFIX) ? a.Q * p.group : 128;
-  int warps = std::min(16, std::max(1, (rows_needed + 15) / 16));
+  int warps = std::min(8, std::max(1, (rows_needed + 15) / 16));
+  if (warps > 4) warps = 8;
+  else if (warps > 2) warps = 4;
   p.rows_per_cta = warps * 16;
   p.queries_per_cta = std::max(1, p.rows_per_cta / p.group);
   p.rows_per_cta = p.queries_per_cta * p.group;
@@ -414,14 +429,13 @@ void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
   TORCH_CHECK(p.num_splits == 1 || (p.keys_per_split % ATT_BK == 0 && a.o_part && a.lse_part),
               "split attention needs 64-aligned splits and scratch");
   const int smem = 2 * ATT_STAGES * ATT_TILE_BYTES + 1024 + 128;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
   dim3 grid(qblocks, a.B, a.hkv * p.num_splits);
-  paged_attention_kernel<<<grid, 32 * (warps + 1), smem, stream>>>(tk, tv, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  switch (warps) {
+    case 1: launch_attn<1>(grid, smem, tk, tv, p, stream); break;
+    case 2: launch_attn<2>(grid, smem, tk, tv, p, stream); break;
+    case 4: launch_attn<4>(grid, smem, tk, tv, p, stream); break;
+    default: launch_attn<8>(grid, smem, tk, tv, p, stream); break;
+  }
   if (p.num_splits > 1) {
     const int rows = a.T * a.hq;
     attention_combine_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(a.o_part, a.lse_part, a.o, rows,

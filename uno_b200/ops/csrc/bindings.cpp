@@ -26,16 +26,22 @@ void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at:
 void walk_tree_launch(const at::Tensor& tok, const at::Tensor& par, const at::Tensor& tgt, int max_depth, int64_t pad,
                       at::Tensor& committed, at::Tensor& accepted, at::Tensor& lengths);
 
-static int* g_err[64] = {nullptr};
+static DeviceScratch g_scratch[64];
 
-int* device_error_flag() {
+DeviceScratch& device_scratch() {
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
-  if (g_err[dev] == nullptr) {
-    C10_CUDA_CHECK(cudaMalloc(&g_err[dev], sizeof(int)));
-    C10_CUDA_CHECK(cudaMemset(g_err[dev], 0, sizeof(int)));
+  DeviceScratch& s = g_scratch[dev];
+  if (s.err == nullptr) {
+    s.max_counters = 16384;
+    s.ws_floats = (size_t)16 << 20;  // 64 MB of fp32 split-K partials
+    C10_CUDA_CHECK(cudaMalloc(&s.err, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(s.err, 0, sizeof(int)));
+    C10_CUDA_CHECK(cudaMalloc(&s.counters, s.max_counters * sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(s.counters, 0, s.max_counters * sizeof(int)));
+    C10_CUDA_CHECK(cudaMalloc(&s.ws, s.ws_floats * sizeof(float)));
   }
-  return g_err[dev];
+  return s;
 }
 
 static int64_t read_error_flag(bool reset) {
@@ -56,15 +62,15 @@ static T* ptr_or_null(const c10::optional<at::Tensor>& t, const char* what = "te
   return reinterpret_cast<T*>(t->data_ptr());
 }
 
-// Generic GEMM entry: out = epilogue(a[M,K] . b[N,K]^T).
+// Generic GEMM entry: out = epilogue(a[M,K] . b[N,K]^T [+ a2[M,K2] . b2[N,K2]^T]).
 static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t bn, c10::optional<at::Tensor> c,
-                 c10::optional<at::Tensor> r, c10::optional<at::Tensor> h, int64_t n_base, double lora_scale,
-                 c10::optional<at::Tensor> row_mask, c10::optional<at::Tensor> q_out,
+                 c10::optional<at::Tensor> r, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2,
+                 double lora_scale, c10::optional<at::Tensor> row_mask, c10::optional<at::Tensor> q_out,
                  c10::optional<at::Tensor> k_cache, c10::optional<at::Tensor> v_cache,
                  c10::optional<at::Tensor> slots, c10::optional<at::Tensor> positions,
                  c10::optional<at::Tensor> cos_sin, c10::optional<at::Tensor> q_norm_w,
                  c10::optional<at::Tensor> k_norm_w, double eps, int64_t hq, int64_t hkv, int64_t page,
-                 int64_t max_ctas) {
+                 int64_t max_ctas, int64_t splits) {
   check_dev(a, "gemm A");
   check_dev(b, "gemm B");
   UNO_CHECK_BF16(a);
@@ -76,14 +82,23 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   p.N = b.size(0);
   p.K = a.size(1);
   if (p.M == 0) return;
+  const bool ext = a2.has_value() && a2->defined();
+  if (ext) {
+    check_dev(*a2, "gemm A2");
+    TORCH_CHECK(b2.has_value() && b2->defined(), "K extension needs both A2 and B2");
+    check_dev(*b2, "gemm B2");
+    UNO_CHECK_BF16(*a2);
+    UNO_CHECK_BF16(*b2);
+    TORCH_CHECK(a2->dim() == 2 && b2->dim() == 2 && a2->size(0) == p.M && b2->size(0) == p.N &&
+                    a2->size(1) == b2->size(1) && a2->stride(1) == 1 && b2->stride(1) == 1,
+                "gemm: K-extension shape mismatch");
+    p.K2 = a2->size(1);
+  }
   p.C = ptr_or_null<__nv_bfloat16>(c);
   p.ldc = c.has_value() ? c->stride(0) : 0;
   p.R = ptr_or_null<const __nv_bfloat16>(r);
   p.ldr = r.has_value() ? r->stride(0) : 0;
-  p.H = ptr_or_null<__nv_bfloat16>(h);
-  p.ldh = h.has_value() ? h->stride(0) : 0;
-  TORCH_CHECK(p.ldc % 8 == 0 && p.ldr % 8 == 0 && p.ldh % 8 == 0, "output strides must be multiples of 8");
-  p.n_base = n_base;
+  TORCH_CHECK(p.ldc % 8 == 0 && p.ldr % 8 == 0, "output strides must be multiples of 8");
   p.lora_scale = lora_scale;
   p.row_mask = ptr_or_null<const float>(row_mask);
   p.q_out = ptr_or_null<__nv_bfloat16>(q_out);
@@ -98,10 +113,24 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   p.num_q_heads = hq;
   p.num_kv_heads = hkv;
   p.page_size = page;
-  p.err = device_error_flag();
+  if (epi == 5) TORCH_CHECK(p.q_out && p.slots && p.positions && p.cos_sin, "QK-RoPE epilogue arguments missing");
+  if (epi == 2) TORCH_CHECK(p.row_mask != nullptr, "ROWSCALE needs row_mask");
+  if (epi == 3) TORCH_CHECK(p.R != nullptr, "ADD needs a residual");
+  if (epi != 5) TORCH_CHECK(p.C != nullptr, "output tensor missing");
+  DeviceScratch& scratch = device_scratch();
+  p.err = scratch.err;
   int tile = pick_bn(p.M, p.N, (int)bn);
-  if ((epi == 1 || epi == 4 || epi == 5 || epi == 6) && tile == 64) tile = 128;
-  gemm_dispatch((int)epi, tile, a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), p, cur_stream(), (int)max_ctas);
+  if ((epi == 1 || epi == 5) && tile == 64) tile = 128;
+  p.splits = pick_splits(p.M, p.N, p.K + p.K2, tile, (int)splits);
+  const int tiles = ((p.M + 127) / 128) * ((p.N + tile - 1) / tile);
+  if (p.splits > 1 &&
+      (tiles > scratch.max_counters || (size_t)tiles * p.splits * 128 * tile > scratch.ws_floats))
+    p.splits = 1;
+  p.ws = scratch.ws;
+  p.counters = scratch.counters;
+  gemm_dispatch((int)epi, tile, a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                ext ? a2->data_ptr() : nullptr, ext ? a2->stride(0) : 0, ext ? b2->data_ptr() : nullptr,
+                ext ? b2->stride(0) : 0, p, cur_stream(), (int)max_ctas);
 }
 
 static void rms_norm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, at::Tensor& y,

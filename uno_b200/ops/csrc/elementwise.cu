@@ -14,7 +14,7 @@ namespace uno {
 
 // One CTA per row; each thread owns 8 consecutive elements (one 16-byte vector).
 template <bool ADD>
-__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int H,
                                int groups, float eps) {
   const int row = blockIdx.x;
@@ -24,7 +24,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
   float v[8];
   bool active = tid < nvec;
   if (active) {
-    uint4 raw = reinterpret_cast<const uint4*>(x + (size_t)row * H)[tid];
+    uint4 raw = reinterpret_cast<const uint4*>(x + (size_t)row * ldx)[tid];
     const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -110,16 +110,18 @@ void rmsnorm_launch(const at::Tensor& x, const c10::optional<at::Tensor>& residu
   const int rows = x.numel() / H;
   TORCH_CHECK(H % 8 == 0 && H / 8 <= 1024, "hidden size must be a multiple of 8 and <= 8192");
   TORCH_CHECK(groups >= 1 && H % groups == 0 && (H / groups) % 8 == 0, "bad RMSNorm group count");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "x must be [rows, H] with 16-byte rows");
+  TORCH_CHECK(y.is_contiguous() && (!residual.has_value() || residual->is_contiguous()), "y/residual contiguous");
   if (rows == 0) return;
   int threads = ((H / 8 + 31) / 32) * 32;
   if (residual.has_value()) {
     rmsnorm_kernel<true><<<rows, threads, 0, cur_stream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
         reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), H, groups, (float)eps);
   } else {
     rmsnorm_kernel<false><<<rows, threads, 0, cur_stream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr,
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), nullptr,
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), H,
         groups, (float)eps);
   }

@@ -2,229 +2,303 @@
 //
 //   D[M, N] = A[M, K] . B[N, K]^T     (A = activations, B = weights, both K-major)
 //
-// Per CTA (one per SM, persistent over output tiles of 128 x BN):
+// Per CTA (one per SM, persistent over work units = output tile x K split):
 //   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage (128-byte
 //               swizzle) into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from
 //               one elected thread into a double-buffered fp32 TMEM accumulator;
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane
-//               quarter, apply the fused epilogue, store to global memory.
-// The accumulator double buffer lets the epilogue of tile i overlap the
-// main loop of tile i+1.  Tiles are visited M-fastest so the CTAs that run
-// concurrently share weight tiles through L2.
+//               quarter, apply the fused epilogue, and move every global
+//               load/store through a per-warp shared-memory staging tile so
+//               that rows are read and written as contiguous segments.
+// The accumulator double buffer lets the epilogue of tile i overlap the main
+// loop of tile i+1.  Tiles are visited M-fastest so CTAs that run at the same
+// time share weight tiles through L2.
+//
+// Split-K: when there are too few output tiles to fill the SMs, each tile's K
+// range is split across CTAs.  Every split writes its fp32 partial to a global
+// workspace; the last split to finish (per-tile arrival counter) sums the
+// partials and runs the fused epilogue, then resets the counter so the next
+// launch (or CUDA-graph replay) starts from zero.  Launches that share the
+// workspace must not overlap on the GPU (one stream).
+//
+// K extension: a second operand pair (A2 [M, K2], B2 [N, K2]) continues the
+// same K loop after the first, so D = A.B^T + A2.B2^T in one accumulator.  The
+// gated LoRA uses it: A2 = scale * mask * (x . A_lora^T) (computed by a skinny
+// ROWSCALE GEMM) and B2 = B_lora, so the adapter costs R extra K columns and
+// no extra pass over the output.
 //
 // Epilogues (EPI template argument):
 //   STORE      C = bf16(acc)
 //   SILU       gate/up rows interleaved in 64-row groups: out = silu(g) * u
-//   LORA_SPLIT columns < n_base -> C (raw), columns >= n_base -> H = bf16(scale*mask[row]*acc)
+//   ROWSCALE   C = bf16(scale * row_mask[row] * acc)   (LoRA hidden)
 //   ADD        C = bf16(acc + R)          (R may alias C)
-//   ADD_SILU   as SILU with g, u = bf16(acc + R)
-//   QKROPE     per 128-wide head: [+R], bf16 round, optional per-head RMSNorm,
+//   QKROPE     per 128-wide head: bf16 round, optional per-head RMSNorm,
 //              NeoX RoPE; q heads -> Qout, k/v heads -> paged KV cache slots
-//   ADD_QKROPE QKROPE with the residual add
 // Every mbarrier wait is bounded (common.cuh); on timeout the kernel flags the
-// error word and unwinds, freeing its TMEM.
+// error word, lets in-flight copies land and unwinds, freeing its TMEM.
 #include <cudaTypedefs.h>
 
 #include <mutex>
-#include <unordered_map>
 
 #include "common.cuh"
 #include "uno_ops.h"
 
 namespace uno {
 
-enum Epi : int { EPI_STORE = 0, EPI_SILU = 1, EPI_LORA_SPLIT = 2, EPI_ADD = 3, EPI_ADD_SILU = 4, EPI_QKROPE = 5, EPI_ADD_QKROPE = 6 };
+enum Epi : int { EPI_STORE = 0, EPI_SILU = 1, EPI_ROWSCALE = 2, EPI_ADD = 3, EPI_QKROPE = 5 };
 
+template <int EPI>
+constexpr bool is_qkrope() {
+  return EPI == EPI_QKROPE;
+}
 
-template <int BN>
+template <int BN, int EPI>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+  static constexpr int EPI_COLS = is_qkrope<EPI>() ? 128 : 32;
+  static constexpr int PITCH = EPI_COLS * 2 + 16;          // staging row pitch (bytes)
+  static constexpr int EPI_BYTES = 4 * 32 * PITCH;         // 4 epilogue warps x 32 rows
+  static constexpr int RING = 200 * 1024 - EPI_BYTES;
+  static constexpr int STAGES = RING / STAGE_BYTES > 8 ? 8 : RING / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float* v, int valid_cols) {
-  // valid_cols is a multiple of 8 (checked on host); write 16-byte granules.
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (g * 8 < valid_cols) {
-      uint4 w;
-      w.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-      w.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-      w.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-      w.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-      *reinterpret_cast<uint4*>(dst + g * 8) = w;
-    }
-  }
+__device__ __forceinline__ uint64_t shfl64(uint64_t v, int src) {
+  uint32_t lo = __shfl_sync(0xffffffff, (uint32_t)v, src);
+  uint32_t hi = __shfl_sync(0xffffffff, (uint32_t)(v >> 32), src);
+  return ((uint64_t)hi << 32) | lo;
 }
 
-__device__ __forceinline__ void load32_bf16(const __nv_bfloat16* src, float* v, int valid_cols) {
+// ---- per-warp staging tile [32 rows][COLS bf16] with padded rows ----------
+template <int COLS>
+struct Stage {
+  static constexpr int PITCH = COLS * 2 + 16;
+  static constexpr int PPR = COLS / 8;  // 16-byte pieces per row
+
+  // This thread (row = lane) writes n (multiple of 8) values at column c0.
+  __device__ static void row_write(uint8_t* buf, int lane, int c0, const float* v, int n) {
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (g * 8 < valid_cols) {
-      uint4 w = *reinterpret_cast<const uint4*>(src + g * 8);
+    for (int j = 0; j < n / 8; ++j) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(buf + lane * PITCH + c0 * 2 + j * 16) = w;
+    }
+  }
+
+  __device__ static void row_read(const uint8_t* buf, int lane, int c0, float* v, int n) {
+#pragma unroll
+    for (int j = 0; j < n / 8; ++j) {
+      uint4 w = *reinterpret_cast<const uint4*>(buf + lane * PITCH + c0 * 2 + j * 16);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float2 f = __bfloat1622float2(h[i]);
-        v[g * 8 + 2 * i] = f.x;
-        v[g * 8 + 2 * i + 1] = f.y;
+        v[8 * j + 2 * i] = f.x;
+        v[8 * j + 2 * i + 1] = f.y;
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[g * 8 + i] = 0.f;
     }
   }
-}
+
+  // Each lane supplies the global address of its own row (0 = skip); the warp
+  // copies the staged rows out with contiguous 16-byte pieces per row.
+  __device__ static void store(const uint8_t* buf, int lane, uint64_t my_dst, int valid_cols) {
+#pragma unroll
+    for (int k = 0; k < PPR; ++k) {
+      const int pc = k * 32 + lane;
+      const int r = pc / PPR, c = pc % PPR;
+      const uint64_t d = shfl64(my_dst, r);
+      if (d != 0 && c * 8 < valid_cols)
+        *reinterpret_cast<uint4*>(d + c * 16) = *reinterpret_cast<const uint4*>(buf + r * PITCH + c * 16);
+    }
+  }
+
+  __device__ static void load(uint8_t* buf, int lane, uint64_t my_src, int valid_cols) {
+#pragma unroll
+    for (int k = 0; k < PPR; ++k) {
+      const int pc = k * 32 + lane;
+      const int r = pc / PPR, c = pc % PPR;
+      const uint64_t s = shfl64(my_src, r);
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (s != 0 && c * 8 < valid_cols) w = *reinterpret_cast<const uint4*>(s + c * 16);
+      *reinterpret_cast<uint4*>(buf + r * PITCH + c * 16) = w;
+    }
+  }
+};
+
+// Accumulator source: TMEM (single split) or the sum of split-K partials.
+struct AccSrc {
+  uint32_t taddr;      // this warp's TMEM lane quarter + accumulator buffer
+  const float* parts;  // first split partial of this tile (split mode), else null
+  int splits;
+  int bn;
+  int row_in_tile;
+
+  __device__ __forceinline__ void load32(int c, float* v) const {
+    if (parts == nullptr) {
+      tmem_ld32(taddr + c, v);
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float* base = parts + (size_t)s * 128 * bn;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = *reinterpret_cast<const float4*>(base + ((size_t)(c / 4 + q) * 128 + row_in_tile) * 4);
+        v[4 * q] += f.x;
+        v[4 * q + 1] += f.y;
+        v[4 * q + 2] += f.z;
+        v[4 * q + 3] += f.w;
+      }
+    }
+  }
+};
 
 // One 128-wide head of the QK-norm / RoPE / KV-store epilogue.
-template <bool ADD>
-__device__ __forceinline__ void qkrope_head(const GemmParams& p, uint32_t taddr, int row, bool row_ok, int col0) {
+__device__ __forceinline__ void qkrope_head(const GemmParams& p, const AccSrc& src, uint8_t* buf, int lane, int row,
+                                            bool row_ok, int cbase, int col0) {
+  using S = Stage<128>;
   float v[128];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) tmem_ld32(taddr + c * 32, v + c * 32);
-  if (!row_ok) return;
-  if (ADD) {
-    float r[32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      load32_bf16(p.R + (size_t)row * p.ldr + col0 + c * 32, r, 32);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[c * 32 + i] += r[i];
-    }
-  }
+  for (int c = 0; c < 4; ++c) src.load32(cbase + c * 32, v + c * 32);
 #pragma unroll
   for (int i = 0; i < 128; ++i) v[i] = bf16r(v[i]);
   const int head = col0 / 128;
   const int hq = p.num_q_heads, hkv = p.num_kv_heads;
-  const int64_t slot = p.slots[row];
-  if (head < hq + hkv) {
-    const __nv_bfloat16* w = head < hq ? p.q_norm_w : p.k_norm_w;
-    if (w != nullptr) {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
-      const float inv = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
-#pragma unroll
-      for (int i = 0; i < 128; ++i) v[i] = bf16r(v[i] * inv * __bfloat162float(w[i]));
-    }
-    const float* cs = p.cos_sin + (size_t)p.positions[row] * 128;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float c = cs[i], s = cs[64 + i];
-      const float x1 = v[i], x2 = v[64 + i];
-      v[i] = x1 * c - x2 * s;
-      v[64 + i] = x2 * c + x1 * s;
-    }
+  uint64_t dst = 0;
+  if (row_ok) {
+    const int64_t slot = p.slots[row];
     if (head < hq) {
-      __nv_bfloat16* dst = p.q_out + ((size_t)row * hq + head) * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) store32_bf16(dst + c * 32, v + c * 32, 32);
-      return;
+      dst = (uint64_t)(p.q_out + ((size_t)row * hq + head) * 128);
+    } else if (slot >= 0) {
+      const bool is_k = head < hq + hkv;
+      const int kvh = is_k ? head - hq : head - hq - hkv;
+      __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
+      dst = (uint64_t)(cache + (((size_t)(slot / p.page_size) * hkv + kvh) * p.page_size + slot % p.page_size) * 128);
     }
-    if (slot < 0) return;
-    const int kvh = head - hq;
-    __nv_bfloat16* dst = p.k_cache + (((size_t)(slot / p.page_size) * hkv + kvh) * p.page_size + slot % p.page_size) * 128;
+    if (head < hq + hkv) {
+      const __nv_bfloat16* w = head < hq ? p.q_norm_w : p.k_norm_w;
+      if (w != nullptr) {
+        float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) store32_bf16(dst + c * 32, v + c * 32, 32);
-    return;
+        for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
+        const float inv = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] = bf16r(v[i] * inv * __bfloat162float(w[i]));
+      }
+      const float* cs = p.cos_sin + (size_t)p.positions[row] * 128;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float c = cs[i], s = cs[64 + i];
+        const float x1 = v[i], x2 = v[64 + i];
+        v[i] = x1 * c - x2 * s;
+        v[64 + i] = x2 * c + x1 * s;
+      }
+    }
   }
-  if (slot < 0) return;
-  const int kvh = head - hq - hkv;
-  __nv_bfloat16* dst = p.v_cache + (((size_t)(slot / p.page_size) * hkv + kvh) * p.page_size + slot % p.page_size) * 128;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) store32_bf16(dst + c * 32, v + c * 32, 32);
+  S::row_write(buf, lane, 0, v, 128);
+  __syncwarp();
+  S::store(buf, lane, dst, 128);
+  __syncwarp();
 }
 
 template <int BN, int EPI>
-__device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t taddr, int row, int n_blk) {
+__device__ __forceinline__ void run_epilogue(const GemmParams& p, const AccSrc& src, uint8_t* buf, int lane, int row,
+                                             int n_blk) {
   const bool row_ok = row < p.M;
   const int n0 = n_blk * BN;
-  if constexpr (EPI == EPI_QKROPE || EPI == EPI_ADD_QKROPE) {
+  if constexpr (is_qkrope<EPI>()) {
 #pragma unroll 1
-    for (int h = 0; h < BN / 128; ++h) qkrope_head<EPI == EPI_ADD_QKROPE>(p, taddr + h * 128, row, row_ok, n0 + h * 128);
-  } else if constexpr (EPI == EPI_SILU || EPI == EPI_ADD_SILU) {
+    for (int h = 0; h < BN / 128; ++h) {
+      if (n0 + h * 128 >= p.N) break;
+      qkrope_head(p, src, buf, lane, row, row_ok, h * 128, n0 + h * 128);
+    }
+  } else if constexpr (EPI == EPI_SILU) {
+    using S = Stage<32>;
     // Tile columns hold [gate 64 | up 64] pairs; output column block n_blk*BN/2.
 #pragma unroll 1
     for (int pr = 0; pr < BN / 128; ++pr) {
 #pragma unroll 1
       for (int c = 0; c < 64; c += 32) {
-        float g[32], u[32];
-        tmem_ld32(taddr + pr * 128 + c, g);
-        tmem_ld32(taddr + pr * 128 + 64 + c, u);
         const int gcol = n0 + pr * 128 + c;
-        if (!row_ok || gcol >= p.N) continue;
-        if constexpr (EPI == EPI_ADD_SILU) {
-          float r[32];
-          load32_bf16(p.R + (size_t)row * p.ldr + gcol, r, 32);
+        if (gcol >= p.N) break;
+        float g[32], u[32];
+        src.load32(pr * 128 + c, g);
+        src.load32(pr * 128 + 64 + c, u);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) g[i] += r[i];
-          load32_bf16(p.R + (size_t)row * p.ldr + gcol + 64, r, 32);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] += r[i];
-        }
-        float o[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float gg = bf16r(g[i]), uu = bf16r(u[i]);
-          o[i] = silu_f(gg) * uu;
-        }
+        for (int i = 0; i < 32; ++i) g[i] = silu_f(bf16r(g[i])) * bf16r(u[i]);
         const int ocol = (n0 >> 1) + pr * 64 + c;
-        store32_bf16(p.C + (size_t)row * p.ldc + ocol, o, 32);
+        S::row_write(buf, lane, 0, g, 32);
+        __syncwarp();
+        S::store(buf, lane, row_ok ? (uint64_t)(p.C + (size_t)row * p.ldc + ocol) : 0ull, 32);
+        __syncwarp();
       }
     }
   } else {
+    using S = Stage<32>;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(taddr + c, v);
       const int col = n0 + c;
-      if (!row_ok || col >= p.N) continue;
+      if (col >= p.N) break;
       const int valid = min(32, p.N - col);
-      if constexpr (EPI == EPI_STORE) {
-        store32_bf16(p.C + (size_t)row * p.ldc + col, v, valid);
-      } else if constexpr (EPI == EPI_ADD) {
+      float v[32];
+      src.load32(c, v);
+      uint64_t dst = 0;
+      if constexpr (EPI == EPI_ADD) {
         float r[32];
-        load32_bf16(p.R + (size_t)row * p.ldr + col, r, valid);
+        S::load(buf, lane, row_ok ? (uint64_t)(p.R + (size_t)row * p.ldr + col) : 0ull, valid);
+        __syncwarp();
+        S::row_read(buf, lane, 0, r, 32);
+        __syncwarp();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += r[i];
-        store32_bf16(p.C + (size_t)row * p.ldc + col, v, valid);
-      } else if constexpr (EPI == EPI_LORA_SPLIT) {
-        if (col < p.n_base) {
-          store32_bf16(p.C + (size_t)row * p.ldc + col, v, min(valid, p.n_base - col));
-        } else {
-          const float s = p.lora_scale * p.row_mask[row];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= s;
-          store32_bf16(p.H + (size_t)row * p.ldh + (col - p.n_base), v, valid);
-        }
       }
+      const int vcols = valid;
+      if constexpr (EPI == EPI_ROWSCALE) {
+        const float sc = row_ok ? p.lora_scale * p.row_mask[row] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= sc;
+      }
+      if (row_ok) dst = (uint64_t)(p.C + (size_t)row * p.ldc + col);
+      S::row_write(buf, lane, 0, v, 32);
+      __syncwarp();
+      S::store(buf, lane, dst, vcols);
+      __syncwarp();
     }
   }
 }
 
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmParams p) {
+  using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -240,6 +314,10 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.K2 > 0) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   tc_fence_before();
@@ -248,27 +326,54 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = p.num_m * p.num_n;
-  const int k_blocks = (p.K + Cfg::BK - 1) / Cfg::BK;
+  const int splits = p.splits;
+  const int num_units = num_tiles * splits;
+  const int kb_main = (p.K + Cfg::BK - 1) / Cfg::BK;
+  const int k_blocks = kb_main + (p.K2 + Cfg::BK - 1) / Cfg::BK;
+  const int kb_per = (k_blocks + splits - 1) / splits;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int tile = u % num_tiles, ks = u / num_tiles;
         const int m_blk = tile % p.num_m, n_blk = tile / p.num_m;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { *abort_flag = 1; break; }
+        const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            *abort_flag = 1;
+            break;
+          }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, m_blk * Cfg::BM);
-          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * Cfg::BK, n_blk * BN);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (kb < kb_main) {
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, m_blk * Cfg::BM);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * Cfg::BK, n_blk * BN);
+          } else {
+            const int k2 = (kb - kb_main) * Cfg::BK;
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA2, &full[stage], k2, m_blk * Cfg::BM);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB2, &full[stage], k2, n_blk * BN);
+          }
+#pragma unroll
+          for (int s = 0; s < STAGES; ++s)
+            if (s == stage) {
+              issued[s] = true;
+              issued_phase[s] = phase;
+            }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
       }
-      // Drain: make sure every issued load has landed before the CTA may exit.
-      for (int s = 0; s < STAGES; ++s) {
-        // A stage whose load is in flight completes its `full` phase; waiting
-        // for the MMA's release of each stage covers all of them.
-        (void)s;
+      if (*abort_flag) {  // let in-flight copies land before the CTA exits
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&full[s], issued_phase[s], p.err);
       }
     }
   } else if (warp == 1) {
@@ -278,47 +383,105 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) { *abort_flag = 1; break; }
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int ks = u / num_tiles;
+        const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) {
+          *abort_flag = 1;
+          break;
+        }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint64_t adesc = smem_desc_sw128(sA + stage * Cfg::A_BYTES);
           const uint64_t bdesc = smem_desc_sw128(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom
-            tc_mma_bf16(d, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc, (kb | k) != 0);
+            tc_mma_bf16(d, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc, (kb > kb0 || k > 0));
           }
           tc_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        if (!ok) { *abort_flag = 1; break; }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
         tc_commit(&tfull[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
       }
     }
   } else {
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t* buf = sEpi + (warp - 2) * 32 * Cfg::PITCH;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const int tile = u % num_tiles, ks = u / num_tiles;
       const int m_blk = tile % p.num_m, n_blk = tile / p.num_m;
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, p.err);
       ok = __shfl_sync(0xffffffff, ok, 0);
-      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      if (!ok || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      run_epilogue<BN, EPI>(p, taddr, m_blk * 128 + row_in_tile, n_blk);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      const int row = m_blk * 128 + row_in_tile;
+      if (splits == 1) {
+        AccSrc src{taddr, nullptr, 1, BN, row_in_tile};
+        run_epilogue<BN, EPI>(p, src, buf, lane, row, n_blk);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      } else {
+        // write this split's fp32 partial ([BN/4][128 rows][4] layout: coalesced per warp)
+        float* mine = p.ws + ((size_t)tile * splits + ks) * 128 * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(mine + ((size_t)(c / 4 + q) * 128 + row_in_tile) * 4) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(p.counters + tile, 1);
+          *last_flag = (old == splits - 1);
+        }
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          AccSrc src{0u, p.ws + (size_t)tile * splits * 128 * BN, splits, BN, row_in_tile};
+          run_epilogue<BN, EPI>(p, src, buf, lane, row, n_blk);
+          epi_bar();
+          if (threadIdx.x == 64) p.counters[tile] = 0;  // ready for the next launch
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
     }
   }
   tc_fence_before();
@@ -360,7 +523,7 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t 
   return m;
 }
 
-static int num_sms() {
+int num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev;
@@ -371,63 +534,75 @@ static int num_sms() {
 }
 
 template <int BN, int EPI>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t stream, int max_ctas) {
-  using Cfg = GemmCfg<BN>;
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                   GemmParams& p, cudaStream_t stream, int max_ctas) {
+  using Cfg = GemmCfg<BN, EPI>;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     configured = true;
   }
-  p.num_m = (p.M + 127) / 128;
-  p.num_n = (p.N + BN - 1) / BN;
-  int tiles = p.num_m * p.num_n;
-  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_bf16_kernel<BN, EPI><<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, p);
+  const int units = p.num_m * p.num_n * p.splits;
+  const int grid = std::min(units, max_ctas > 0 ? max_ctas : num_sms());
+  gemm_bf16_kernel<BN, EPI><<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, ta2, tb2, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 int pick_bn(int M, int N, int forced) {
   if (forced) return forced;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  return 256;
+}
+
+// K splits for a (M, N, K) problem with tile width bn: only when the output
+// tiles leave most SMs idle and each split keeps a long enough K loop.
+int pick_splits(int M, int N, int K, int bn, int forced) {
+  if (forced > 0) return forced;
   const int sms = num_sms();
-  const int num_m = (M + 127) / 128;
-  // Largest tile whose wave count keeps most SMs busy.
-  for (int bn : {256, 128}) {
-    int tiles = num_m * ((N + bn - 1) / bn);
-    if (tiles >= (sms * 3) / 4) return bn;
-  }
-  return 64;
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int kb = (K + 63) / 64;
+  if (tiles * 5 >= sms * 3 || kb < 16) return 1;
+  int s = std::min({4, std::max(1, sms / tiles), kb / 8});
+  return std::max(1, s);
 }
 
 template <int EPI>
-static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p,
-                        cudaStream_t stream, int max_ctas) {
+static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2, int64_t lda2,
+                        const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas) {
   CUtensorMap ta = make_tmap_bf16(a, p.M, p.K, lda, 128);
+  CUtensorMap ta2 = p.K2 > 0 ? make_tmap_bf16(a2, p.M, p.K2, lda2, 128) : ta;
+  p.num_m = (p.M + 127) / 128;
+  p.num_n = (p.N + bn - 1) / bn;
   if (bn == 256) {
     CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 256);
-    launch<256, EPI>(ta, tb, p, stream, max_ctas);
+    CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 256) : tb;
+    launch<256, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
   } else if (bn == 128) {
     CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 128);
-    launch<128, EPI>(ta, tb, p, stream, max_ctas);
+    CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 128) : tb;
+    launch<128, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
   } else {
-    if constexpr (EPI == EPI_SILU || EPI == EPI_ADD_SILU || EPI == EPI_QKROPE || EPI == EPI_ADD_QKROPE) {
+    if constexpr (EPI == EPI_SILU || is_qkrope<EPI>()) {
       TORCH_CHECK(false, "this epilogue needs a 128 or 256 column tile");
     } else {
       CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 64);
-      launch<64, EPI>(ta, tb, p, stream, max_ctas);
+      CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 64) : tb;
+      launch<64, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
     }
   }
 }
 
-void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p,
-                   cudaStream_t stream, int max_ctas) {
+void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,
+                   int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas) {
+  TORCH_CHECK(p.K2 == 0 || p.K % 64 == 0, "the K extension needs the main K to be a multiple of 64");
   switch (epi) {
-    case EPI_STORE: dispatch_bn<EPI_STORE>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_SILU: dispatch_bn<EPI_SILU>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_LORA_SPLIT: dispatch_bn<EPI_LORA_SPLIT>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_ADD: dispatch_bn<EPI_ADD>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_ADD_SILU: dispatch_bn<EPI_ADD_SILU>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_QKROPE: dispatch_bn<EPI_QKROPE>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
-    case EPI_ADD_QKROPE: dispatch_bn<EPI_ADD_QKROPE>(bn, a, lda, b, ldb, p, stream, max_ctas); break;
+    case EPI_STORE: dispatch_bn<EPI_STORE>(bn, a, lda, b, ldb, a2, lda2, b2, ldb2, p, stream, max_ctas); break;
+    case EPI_SILU: dispatch_bn<EPI_SILU>(bn, a, lda, b, ldb, a2, lda2, b2, ldb2, p, stream, max_ctas); break;
+    case EPI_ROWSCALE: dispatch_bn<EPI_ROWSCALE>(bn, a, lda, b, ldb, a2, lda2, b2, ldb2, p, stream, max_ctas); break;
+    case EPI_ADD: dispatch_bn<EPI_ADD>(bn, a, lda, b, ldb, a2, lda2, b2, ldb2, p, stream, max_ctas); break;
+    case EPI_QKROPE: dispatch_bn<EPI_QKROPE>(bn, a, lda, b, ldb, a2, lda2, b2, ldb2, p, stream, max_ctas); break;
     default: TORCH_CHECK(false, "unknown epilogue ", epi);
   }
 }

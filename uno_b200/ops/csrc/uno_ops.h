@@ -19,11 +19,9 @@ struct GemmParams {
   int num_m, num_n;
   __nv_bfloat16* C;
   int ldc;
-  const __nv_bfloat16* R;  // residual / pre-activation input
+  const __nv_bfloat16* R;  // residual input (ADD)
   int ldr;
-  __nv_bfloat16* H;        // LoRA hidden output
-  int ldh;
-  int n_base;
+  int K2;                  // K extension length (0 = none)
   float lora_scale;
   const float* row_mask;
   // QK-norm / RoPE / KV store
@@ -38,10 +36,27 @@ struct GemmParams {
   float eps;
   int num_q_heads, num_kv_heads, page_size;
   int* err;
+  // split-K: number of K splits, fp32 partial workspace, per-tile arrival counters
+  int splits;
+  float* ws;
+  int* counters;
 };
-void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p,
-                   cudaStream_t stream, int max_ctas);
+void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,
+                   int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas);
 int pick_bn(int M, int N, int forced);
+int pick_splits(int M, int N, int K, int bn, int forced);
+int num_sms();
+
+// Per-device scratch shared by the GEMM split-K path (fp32 partials and
+// self-resetting tile counters) and the device error word.
+struct DeviceScratch {
+  int* err;
+  int* counters;
+  float* ws;
+  size_t ws_floats;
+  int max_counters;
+};
+DeviceScratch& device_scratch();
 
 struct AttnLaunch {
   const __nv_bfloat16* q;
@@ -67,7 +82,7 @@ struct AttnLaunch {
 void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream);
 
 // Device error word (allocated once per device by the bindings).
-int* device_error_flag();
+inline int* device_error_flag() { return device_scratch().err; }
 
 // Every pointer handed to a kernel must live on the current CUDA device: a
 // host or foreign-device tensor is rejected on the host instead of faulting.

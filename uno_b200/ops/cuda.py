@@ -4,12 +4,12 @@ Weight preparation for the sm_100a path (:func:`prepare_model`):
 
 * ``gate_up_proj`` rows are interleaved in 64-row groups ``[gate_j | up_j]`` so
   the GEMM epilogue can apply SiLU(gate) * up inside one output tile;
-* a layer with a gated LoRA adapter stores ``[W ; A_cat]`` as one weight
-  (``layer.weight`` becomes a view of its first N rows).  One GEMM then emits
-  the base output and the rank-R hidden ``scale * mask * (x A^T)`` (its
-  epilogue applies the row mask), and a second GEMM with K = R adds
-  ``hidden . B_cat^T`` and runs the layer's real epilogue (plain, SiLU*up or
-  QK-norm + RoPE + paged KV store).
+* a gated LoRA layer keeps ``A_cat [R, K]`` and ``B_cat [N, R]`` (B rows in
+  the same interleaved order as W).  A skinny split-K GEMM computes the hidden
+  ``h = scale * mask * (x A_cat^T)`` (ROWSCALE epilogue), and the base GEMM runs
+  its K loop over ``[x | h] . [W | B_cat]^T`` (K extension) with the layer's
+  real epilogue (plain, SiLU*up or QK-norm + RoPE + paged KV store), so the
+  adapter adds R columns of K and no extra pass over the output.
 """
 
 from __future__ import annotations
@@ -23,7 +23,7 @@ from uno_b200.parallel import state as tp
 
 _C = None
 
-EPI_STORE, EPI_SILU, EPI_LORA_SPLIT, EPI_ADD, EPI_ADD_SILU, EPI_QKROPE, EPI_ADD_QKROPE = range(7)
+EPI_STORE, EPI_SILU, EPI_ROWSCALE, EPI_ADD, EPI_QKROPE = 0, 1, 2, 3, 5
 INTERLEAVE = 64
 
 
@@ -46,17 +46,17 @@ def error_flag(reset: bool = False) -> int:
     return int(ext().error_flag(reset))
 
 
-def _gemm(a, b, epi, *, c=None, r=None, h=None, n_base=0, scale=0.0, row_mask=None, q_out=None,
+def _gemm(a, b, epi, *, c=None, r=None, a2=None, b2=None, scale=0.0, row_mask=None, q_out=None,
           k_cache=None, v_cache=None, slots=None, positions=None, cos_sin=None, q_norm_w=None,
-          k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0):
-    ext().gemm(a, b, epi, bn, c, r, h, n_base, scale, row_mask, q_out, k_cache, v_cache, slots, positions,
-               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas)
+          k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0, splits=0):
+    ext().gemm(a, b, epi, bn, c, r, a2, b2, scale, row_mask, q_out, k_cache, v_cache, slots, positions,
+               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas, splits)
 
 
-def gemm(a: torch.Tensor, b: torch.Tensor, bn: int = 0) -> torch.Tensor:
+def gemm(a: torch.Tensor, b: torch.Tensor, bn: int = 0, splits: int = 0) -> torch.Tensor:
     """Plain ``a @ b.T`` on the tcgen05 GEMM (bf16 out)."""
     out = torch.empty(a.shape[0], b.shape[0], device=a.device, dtype=torch.bfloat16)
-    _gemm(a, b, EPI_STORE, c=out, bn=bn)
+    _gemm(a, b, EPI_STORE, c=out, bn=bn, splits=splits)
     return out
 
 
@@ -82,18 +82,15 @@ def prepare_linear(layer, interleave: bool = False) -> None:
     w = layer.weight.data
     if interleave:
         w = interleave_gate_up(w)
+    layer.weight.data = w.contiguous()
     if layer.has_lora:
         if layer.lora_a_cat is None:
             layer.pack_lora()
         b_cat = layer.lora_b_cat
         if interleave:
             b_cat = interleave_gate_up(b_cat)
-        ext_w = torch.cat([w, layer.lora_a_cat.to(w.dtype)], dim=0).contiguous()
-        layer.weight_ext = ext_w
-        layer.weight.data = ext_w[: w.shape[0]]
+        layer.lora_a_dev = layer.lora_a_cat.to(w.dtype).contiguous()
         layer.lora_b_dev = b_cat.to(w.dtype).contiguous()
-    else:
-        layer.weight.data = w.contiguous()
     layer.interleaved = interleave
     layer._uno_prepared = True
 
@@ -108,17 +105,26 @@ def prepare_model(model) -> None:
 
 
 # ------------------------------------------------------------------ norms
+def _rows(x):
+    """2-D row view with unit column stride (row stride may be padded)."""
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    return x2 if x2.stride(-1) == 1 else x2.contiguous()
+
+
 def rms_norm(x, weight, eps, n_groups=1):
-    y = torch.empty_like(x)
-    ext().rms_norm(x.contiguous(), None, weight, y, float(eps), int(n_groups))
-    return y
+    x2 = _rows(x)
+    y = torch.empty(x2.shape, device=x.device, dtype=x.dtype)
+    ext().rms_norm(x2, None, weight, y, float(eps), int(n_groups))
+    return y.view(x.shape)
 
 
 def add_rms_norm(x, residual, weight, eps, n_groups=1):
-    y = torch.empty_like(x)
-    res = residual.contiguous().clone() if not residual.is_contiguous() else residual
-    ext().rms_norm(x.contiguous(), res, weight, y, float(eps), int(n_groups))
-    return y, res
+    """Returns (normed, new_residual); the residual buffer is updated in place."""
+    x2 = _rows(x)
+    y = torch.empty(x2.shape, device=x.device, dtype=x.dtype)
+    res = residual if residual.is_contiguous() else residual.contiguous()
+    ext().rms_norm(x2, res, weight, y, float(eps), int(n_groups))
+    return y.view(x.shape), res
 
 
 # ----------------------------------------------------------------- linear
@@ -126,48 +132,48 @@ def _row_parallel(layer) -> bool:
     return layer.tp_dim == 1 and layer.tp_size > 1
 
 
-def _lora_split(x, layer, lora_mask):
-    """One GEMM over [W; A_cat]: base output and masked/scaled LoRA hidden."""
-    M = x.shape[0]
-    N = layer.weight.shape[0]
-    R = layer.lora_rank_total
-    buf = torch.empty(M, N + R, device=x.device, dtype=torch.bfloat16)
-    y, h = buf[:, :N], buf[:, N:]
-    _gemm(x, layer.weight_ext, EPI_LORA_SPLIT, c=y, h=h, n_base=N, scale=layer.lora_scaling,
-          row_mask=lora_mask)
+def lora_hidden(x, layer, lora_mask):
+    """``scale * mask * (x A_cat^T)`` [M, R] (all-reduced for row-parallel layers)."""
+    h = torch.empty(x.shape[0], layer.lora_rank_total, device=x.device, dtype=torch.bfloat16)
+    _gemm(x, layer.lora_a_dev, EPI_ROWSCALE, c=h, scale=layer.lora_scaling, row_mask=lora_mask)
     if _row_parallel(layer):
-        tp.all_reduce(buf)
-    return y, h
+        tp.all_reduce(h)
+    return h
+
+
+def _lora_ext(x, layer, lora_mask):
+    """K-extension operands (a2, b2) for the base GEMM, or (None, None)."""
+    if lora_mask is None or not layer.has_lora:
+        return None, None
+    h = lora_hidden(x, layer, lora_mask)
+    if _row_parallel(layer) and layer.tp_rank != 0:
+        # the adapter term is replicated; exactly one rank adds it before the sum
+        return None, None
+    return h, layer.lora_b_dev
 
 
 def linear(x, layer, lora_mask=None):
-    x = x.contiguous()
-    if lora_mask is not None and layer.has_lora:
-        y, h = _lora_split(x, layer, lora_mask)
-        _gemm(h, layer.lora_b_dev, EPI_ADD, c=y, r=y)
-        return y
+    x = _rows(x)
+    a2, b2 = _lora_ext(x, layer, lora_mask)
     y = torch.empty(x.shape[0], layer.weight.shape[0], device=x.device, dtype=torch.bfloat16)
-    _gemm(x, layer.weight, EPI_STORE, c=y)
+    _gemm(x, layer.weight, EPI_STORE, c=y, a2=a2, b2=b2)
     if _row_parallel(layer):
         tp.all_reduce(y)
     return y
 
 
 def gate_up_silu(x, layer, lora_mask=None):
-    x = x.contiguous()
+    x = _rows(x)
+    a2, b2 = _lora_ext(x, layer, lora_mask)
     inter = layer.weight.shape[0] // 2
     act = torch.empty(x.shape[0], inter, device=x.device, dtype=torch.bfloat16)
-    if lora_mask is not None and layer.has_lora:
-        pre, h = _lora_split(x, layer, lora_mask)
-        _gemm(h, layer.lora_b_dev, EPI_ADD_SILU, c=act, r=pre)
-        return act
-    _gemm(x, layer.weight, EPI_SILU, c=act)
+    _gemm(x, layer.weight, EPI_SILU, c=act, a2=a2, b2=b2)
     return act
 
 
 def qkv_rope_store(x, layer, lora_mask, positions, cos_sin, q_norm_w, k_norm_w, eps, num_heads, num_kv_heads,
                    head_dim, k_cache, v_cache, slot_mapping):
-    x = x.contiguous()
+    x = _rows(x)
     T = x.shape[0]
     q = torch.empty(T, num_heads, head_dim, device=x.device, dtype=torch.bfloat16)
     page = k_cache.shape[2] if k_cache.numel() else 0
@@ -179,13 +185,10 @@ def qkv_rope_store(x, layer, lora_mask, positions, cos_sin, q_norm_w, k_norm_w, 
         ext().qk_norm_rope_store(qkv, q, k_cache, v_cache, slots, positions, cos_sin, q_norm_w, k_norm_w,
                                  float(eps), num_heads, num_kv_heads, head_dim, page)
         return q
-    common = dict(q_out=q, k_cache=kc, v_cache=vc, slots=slots, positions=positions, cos_sin=cos_sin,
-                  q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=float(eps), hq=num_heads, hkv=num_kv_heads, page=page)
-    if lora_mask is not None and layer.has_lora:
-        pre, h = _lora_split(x, layer, lora_mask)
-        _gemm(h, layer.lora_b_dev, EPI_ADD_QKROPE, r=pre, **common)
-    else:
-        _gemm(x, layer.weight, EPI_QKROPE, **common)
+    a2, b2 = _lora_ext(x, layer, lora_mask)
+    _gemm(x, layer.weight, EPI_QKROPE, a2=a2, b2=b2, q_out=q, k_cache=kc, v_cache=vc, slots=slots,
+          positions=positions, cos_sin=cos_sin, q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=float(eps),
+          hq=num_heads, hkv=num_kv_heads, page=page)
     return q
 
 
