@@ -81,8 +81,8 @@ __device__ __forceinline__ uint32_t tile_off(int key, int c) {
   return (uint32_t)((c >> 3) * (ATT_BK * 128) + key * 128 + (((c & 7) ^ (key & 7)) << 4));
 }
 
-template <int NW>
-__global__ void __launch_bounds__(32 * (NW + 1), 1)
+template <int NWR, int KS>
+__global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -95,7 +95,9 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
   const int qblk = blockIdx.x, b = blockIdx.y;
   const int h = blockIdx.z % p.hkv, split = blockIdx.z / p.hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int n_compute = NW;
+  constexpr int n_compute = NWR * KS;
+  constexpr int KPW = ATT_BK / KS;  // keys of each tile handled by one warp
+  constexpr int NT = KPW / 8;       // 8-key n-tiles per warp
 
   // ---- geometry of this request
   int q_begin, nq, kv_len, prefix;
@@ -162,10 +164,12 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
     return;
   }
 
-  // ---- compute warps: 16 rows each
+  // ---- compute warps: 16 rows x KPW keys of every tile each
   const int cw = warp - 1;
+  const int rg = cw % NWR, kss = cw / NWR;
   const int g = lane >> 2, tq = lane & 3;
-  const int row_base = cw * 16;  // row index within CTA
+  const int row_base = rg * 16;  // row index within CTA
+  const int kofs = kss * KPW;    // first key of this warp inside a tile
   // rows g and g+8 of this warp
   int qi[2], qh[2];
   bool row_valid[2];
@@ -213,18 +217,18 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
     const uint32_t kb = sK_base + stage * ATT_TILE_BYTES;
     const uint32_t vb = sV_base + stage * ATT_TILE_BYTES;
     const int k0 = k_lo + t * ATT_BK;
-    // ---- S = Q K^T  (16 rows x 64 keys)
-    float s[8][4];
+    // ---- S = Q K^T  (16 rows x KPW keys)
+    float s[NT][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < NT / 2; ++np) {
         // matrices: (keys np*16+0..7, chunk 2ks), (same keys, chunk 2ks+1),
         //           (keys np*16+8..15, chunk 2ks), (.., chunk 2ks+1)
         const int mtx = lane >> 3, r8 = lane & 7;
-        const int key = np * 16 + (mtx >> 1) * 8 + r8;
+        const int key = kofs + np * 16 + (mtx >> 1) * 8 + r8;
         const int chunk = ks * 2 + (mtx & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(kb + tile_off(key, chunk), b0, b1, b2, b3);
@@ -235,11 +239,11 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
     // ---- mask + online softmax
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < NT; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = e >> 1;
-        const int key = k0 + n * 8 + tq * 2 + (e & 1);
+        const int key = k0 + kofs + n * 8 + tq * 2 + (e & 1);
         bool vis = row_valid[r] && key < k_hi;
         if (vis) {
           if (p.mode == MODE_SUFFIX) {
@@ -264,9 +268,9 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
       m_run[r] = m_new;
     }
     float rs[2] = {0.f, 0.f};
-    uint32_t pa[4][4];  // P as A fragments for 4 k-steps of 16 keys
+    uint32_t pa[NT / 2][4];  // P as A fragments for the k-steps of 16 keys
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < NT; ++n) {
       float e4[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -291,13 +295,13 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
     }
     // ---- O += P V
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+    for (int ks = 0; ks < NT / 2; ++ks) {
 #pragma unroll
       for (int dp = 0; dp < 8; ++dp) {
         // matrices: (keys ks*16+0..7, dim chunk 2dp), (keys +8..15, chunk 2dp),
         //           (keys 0..7, chunk 2dp+1), (keys 8..15, chunk 2dp+1) -- transposed
         const int mtx = lane >> 3, r8 = lane & 7;
-        const int key = ks * 16 + (mtx & 1) * 8 + r8;
+        const int key = kofs + ks * 16 + (mtx & 1) * 8 + r8;
         const int chunk = dp * 2 + (mtx >> 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(vb + tile_off(key, chunk), b0, b1, b2, b3);
@@ -315,6 +319,46 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
   for (int r = 0; r < 2; ++r) {
     l_run[r] += __shfl_xor_sync(0xffffffff, l_run[r], 1);
     l_run[r] += __shfl_xor_sync(0xffffffff, l_run[r], 2);
+  }
+  if constexpr (KS > 1) {
+    // Merge the KS key-split partial states of each row group through shared
+    // memory (the K/V ring is idle now: every issued tile was consumed).
+    constexpr int PER_THREAD = 68;  // m[2], l[2], o[16][4]
+    float* part = reinterpret_cast<float*>(smem) + (size_t)(cw * 32 + lane) * PER_THREAD;
+    asm volatile("bar.sync 1, %0;" ::"r"(n_compute * 32) : "memory");
+    if (kss > 0) {
+      part[0] = m_run[0];
+      part[1] = m_run[1];
+      part[2] = l_run[0];
+      part[3] = l_run[1];
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) part[4 + n * 4 + e] = o[n][e];
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(n_compute * 32) : "memory");
+    if (kss > 0) return;
+#pragma unroll
+    for (int k = 1; k < KS; ++k) {
+      const float* q = reinterpret_cast<const float*>(smem) + (size_t)(((k * NWR + rg) * 32) + lane) * PER_THREAD;
+      float cm[2], co[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float mo = q[r];
+        const float mn = fmaxf(m_run[r], mo);
+        cm[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - mn);
+        co[r] = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+        l_run[r] = l_run[r] * cm[r] + q[2 + r] * co[r];
+        m_run[r] = mn;
+      }
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] = o[n][0] * cm[0] + q[4 + n * 4 + 0] * co[0];
+        o[n][1] = o[n][1] * cm[0] + q[4 + n * 4 + 1] * co[0];
+        o[n][2] = o[n][2] * cm[1] + q[4 + n * 4 + 2] * co[1];
+        o[n][3] = o[n][3] * cm[1] + q[4 + n * 4 + 3] * co[1];
+      }
+    }
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -375,15 +419,16 @@ __global__ void attention_combine_kernel(const float* __restrict__ o_part, const
 
 CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 
-template <int NW>
+template <int NWR, int KS>
 static void launch_attn(dim3 grid, int smem, const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p,
                         cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(paged_attention_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(paged_attention_kernel<NWR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  paged_attention_kernel<NW><<<grid, 32 * (NW + 1), smem, stream>>>(tk, tv, p);
+  paged_attention_kernel<NWR, KS><<<grid, 32 * (NWR * KS + 1), smem, stream>>>(tk, tv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -416,10 +461,14 @@ void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
   // rows per CTA: cover all (query, head) rows of a decode request when
   // possible (at most 8 compute warps = 128 rows); prefill uses 128-row blocks.
   int rows_needed = (a.mode == MODE_SUFFIX) ? a.Q * p.group : 128;
-  int warps = std::min(8, std::max(1, (rows_needed + 15) / 16));
-  if (warps > 4) warps = 8;
-  else if (warps > 2) warps = 4;
-  p.rows_per_cta = warps * 16;
+  // Row warps cover the (query, head) rows; small row sets split every 64-key
+  // tile across KS warps as well so each SM keeps enough warps in flight.
+  int nwr, ks;
+  if (rows_needed <= 16) { nwr = 1; ks = 4; }
+  else if (rows_needed <= 32) { nwr = 2; ks = 4; }
+  else if (rows_needed <= 64) { nwr = 4; ks = 2; }
+  else { nwr = 8; ks = 1; }
+  p.rows_per_cta = nwr * 16;
   p.queries_per_cta = std::max(1, p.rows_per_cta / p.group);
   p.rows_per_cta = p.queries_per_cta * p.group;
   int qblocks = (a.mode == MODE_SUFFIX) ? (a.Q + p.queries_per_cta - 1) / p.queries_per_cta
@@ -430,12 +479,10 @@ void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
               "split attention needs 64-aligned splits and scratch");
   const int smem = 2 * ATT_STAGES * ATT_TILE_BYTES + 1024 + 128;
   dim3 grid(qblocks, a.B, a.hkv * p.num_splits);
-  switch (warps) {
-    case 1: launch_attn<1>(grid, smem, tk, tv, p, stream); break;
-    case 2: launch_attn<2>(grid, smem, tk, tv, p, stream); break;
-    case 4: launch_attn<4>(grid, smem, tk, tv, p, stream); break;
-    default: launch_attn<8>(grid, smem, tk, tv, p, stream); break;
-  }
+  if (nwr == 1) launch_attn<1, 4>(grid, smem, tk, tv, p, stream);
+  else if (nwr == 2) launch_attn<2, 4>(grid, smem, tk, tv, p, stream);
+  else if (nwr == 4) launch_attn<4, 2>(grid, smem, tk, tv, p, stream);
+  else launch_attn<8, 1>(grid, smem, tk, tv, p, stream);
   if (p.num_splits > 1) {
     const int rows = a.T * a.hq;
     attention_combine_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(a.o_part, a.lse_part, a.o, rows,

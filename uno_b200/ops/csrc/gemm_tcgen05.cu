@@ -551,8 +551,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
 
 int pick_bn(int M, int N, int forced) {
   if (forced) return forced;
-  if (N <= 64) return 64;
-  if (N <= 128) return 128;
+  if (N <= 256) return 64;  // skinny outputs (LoRA hidden): more tiles, cheap split-K reduction
   return 256;
 }
 
@@ -564,7 +563,9 @@ int pick_splits(int M, int N, int K, int bn, int forced) {
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   const int kb = (K + 63) / 64;
   if (tiles * 5 >= sms * 3 || kb < 16) return 1;
-  int s = std::min({4, std::max(1, sms / tiles), kb / 8});
+  // Few tiles: up to 16 splits of >= 4 k-blocks for skinny outputs, else 4.
+  const int cap = bn <= 64 ? 16 : 4;
+  int s = std::min({cap, std::max(1, sms / tiles), kb / (bn <= 64 ? 4 : 8)});
   return std::max(1, s);
 }
 
