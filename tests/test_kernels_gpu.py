@@ -320,3 +320,17 @@ def test_copy_tree_kv(C):
 
     for s, d in [(60, 60), (62, 61), (65, 62), (70, 63)]:
         assert torch.equal(at(cache, d), at(orig, s))
+
+
+def test_sampling_on_strided_rows_matches_contiguous(C):
+    torch.manual_seed(9)
+    x = torch.randn(6, 5, 4096, device=DEV).bfloat16()
+    view = x[:, 1:, :]  # [6, 4, V] strided rows, as the decoder passes draft rows
+    flat = view.reshape(-1, 4096).contiguous()
+    assert torch.equal(C.argmax(view), C.argmax(flat))
+    assert torch.equal(C.sample_gumbel(view, 1.0, 3, 11), C.sample_gumbel(flat, 1.0, 3, 11))
+    other = x[:, :4, :]
+    spec = torch.randint(0, 4096, (24,), device=DEV)
+    a1, c1 = C.fused_verify(other, view, spec, 1.0, 5, 2)
+    a2, c2 = C.fused_verify(other.reshape(-1, 4096).contiguous(), flat, spec, 1.0, 5, 2)
+    assert torch.equal(a1, a2) and torch.equal(c1, c2)

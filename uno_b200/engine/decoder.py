@@ -118,7 +118,10 @@ class TwoPassDecoder:
             clean, _ = self.sampler.sample(logits[:, 0, :], sp)
             proposal[:, 0] = clean
             if L > 1:
-                spec, q_sparse = self.sampler.sample(logits[:, 1:, :].reshape(-1, logits.shape[-1]), sp)
+                spec_rows = logits[:, 1:, :]
+                if not (spec_rows.is_cuda and not sp.filtered(logits.shape[-1])):
+                    spec_rows = spec_rows.reshape(-1, logits.shape[-1])
+                spec, q_sparse = self.sampler.sample(spec_rows, sp)
                 proposal[:, 1:] = spec.view(B, L - 1)
         else:
             proposal = torch.zeros((B, L), dtype=torch.int64, device=logits.device)
@@ -144,8 +147,10 @@ class TwoPassDecoder:
             corr = target
         else:
             V = logits.shape[-1]
-            clean = logits[:, : L - 1, :].reshape(-1, V)
-            draft = draft_logits[:, : L - 1, :].reshape(-1, V)
+            clean = logits[:, : L - 1, :]
+            draft = draft_logits[:, : L - 1, :]
+            if not clean.is_cuda or sp.filtered(V):
+                clean, draft = clean.reshape(-1, V), draft.reshape(-1, V)
             spec = proposal[:, 1:].reshape(-1)
             if sp.filtered(V):
                 if q_sparse is None:
@@ -162,7 +167,8 @@ class TwoPassDecoder:
         from uno_b200.engine.sampling import argmax
 
         shape = logits.shape
-        return argmax(logits.reshape(-1, shape[-1])).view(shape[:-1])
+        rows = logits if logits.is_cuda else logits.reshape(-1, shape[-1])
+        return argmax(rows).view(shape[:-1])
 
     def build_payload(self, proposal, accepted, corr, lookahead, sp: SamplingParams):
         """``[B, L+2]`` int64: committed tokens (L+1 slots) then the length."""

@@ -24,6 +24,15 @@ namespace uno {
 
 constexpr int SAMPLE_THREADS = 512;
 
+// Logit rows may be a strided [groups, rows_per_group, V] view (for example the
+// draft rows 1..L-1 of every request in a [B, L, V] block): row r lives at
+// (r / rpg) * gstride + (r % rpg) * ld elements from the base pointer.
+struct RowMap {
+  int rpg;
+  int64_t gstride, ld;
+  __device__ __forceinline__ int64_t off(int r) const { return (int64_t)(r / rpg) * gstride + (int64_t)(r % rpg) * ld; }
+};
+
 struct ArgBest {
   float v;
   int i;
@@ -127,9 +136,9 @@ __device__ __forceinline__ float gumbel1(uint32_t seed, uint32_t offset, uint32_
 }
 
 // ------------------------------------------------------------------ argmax
-__global__ void __launch_bounds__(SAMPLE_THREADS) argmax_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V,
+__global__ void __launch_bounds__(SAMPLE_THREADS) argmax_kernel(const __nv_bfloat16* __restrict__ x, RowMap rm, int V,
                                                                int64_t* __restrict__ out) {
-  const __nv_bfloat16* row = x + (size_t)blockIdx.x * ld;
+  const __nv_bfloat16* row = x + rm.off(blockIdx.x);
   ArgBest best{-INFINITY, 0x7fffffff};
   const int nvec = V / 8;
   for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
@@ -145,9 +154,9 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) argmax_kernel(const __nv_bfloa
 
 // ---------------------------------------------------------- gumbel sample
 __global__ void __launch_bounds__(SAMPLE_THREADS)
-    gumbel_sample_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V, float inv_temp, uint32_t seed,
+    gumbel_sample_kernel(const __nv_bfloat16* __restrict__ x, RowMap rm, int V, float inv_temp, uint32_t seed,
                          uint32_t offset, int64_t* __restrict__ out) {
-  const __nv_bfloat16* row = x + (size_t)blockIdx.x * ld;
+  const __nv_bfloat16* row = x + rm.off(blockIdx.x);
   ArgBest best{-INFINITY, 0x7fffffff};
   const int nvec = V / 8;
   for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
@@ -165,12 +174,12 @@ __global__ void __launch_bounds__(SAMPLE_THREADS)
 
 // ------------------------------------------------------------ fused verify
 __global__ void __launch_bounds__(SAMPLE_THREADS)
-    fused_verify_kernel(const __nv_bfloat16* __restrict__ clean, int64_t ldc, const __nv_bfloat16* __restrict__ draft,
-                        int64_t ldd, const int64_t* __restrict__ spec, int V, float inv_temp, uint32_t seed,
+    fused_verify_kernel(const __nv_bfloat16* __restrict__ clean, RowMap cm_, const __nv_bfloat16* __restrict__ draft,
+                        RowMap dm_, const int64_t* __restrict__ spec, int V, float inv_temp, uint32_t seed,
                         uint32_t offset, int32_t* __restrict__ accepted, int64_t* __restrict__ corr) {
   const int r = blockIdx.x;
-  const __nv_bfloat16* c = clean + (size_t)r * ldc;
-  const __nv_bfloat16* d = draft + (size_t)r * ldd;
+  const __nv_bfloat16* c = clean + cm_.off(r);
+  const __nv_bfloat16* d = draft + dm_.off(r);
   const int nvec = V / 8;
   // pass 1: max of both rows, then sums
   float cm = -INFINITY, dm = -INFINITY;
@@ -493,26 +502,52 @@ __global__ void walk_tree_kernel(const int64_t* __restrict__ tok, const int64_t*
 }
 
 // ------------------------------------------------------------------- host
+// 2-D [rows, V] or 3-D [groups, rpg, V] logits with unit stride along V.
+static RowMap row_map(const at::Tensor& x, int& rows, int& V) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "logits must be bfloat16");
+  TORCH_CHECK(x.stride(-1) == 1, "logits must be contiguous along the vocabulary");
+  RowMap m{};
+  if (x.dim() == 2) {
+    rows = x.size(0);
+    V = x.size(1);
+    m.rpg = std::max<int>(1, rows);
+    m.gstride = 0;
+    m.ld = x.stride(0);
+  } else {
+    TORCH_CHECK(x.dim() == 3, "logits must be 2-D or 3-D");
+    rows = x.size(0) * x.size(1);
+    V = x.size(2);
+    m.rpg = std::max<int>(1, x.size(1));
+    m.gstride = x.stride(0);
+    m.ld = x.stride(1);
+  }
+  TORCH_CHECK(m.ld % 8 == 0 && m.gstride % 8 == 0, "logit row strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "logits must be 16-byte aligned");
+  return m;
+}
+
 void argmax_launch(const at::Tensor& x, at::Tensor& out) {
   check_dev(x, "logits");
   check_dev(out, "out");
-  const int rows = x.size(0), V = x.size(1);
+  int rows, V;
+  RowMap m = row_map(x, rows, V);
+  TORCH_CHECK(out.numel() == rows, "argmax output size");
   if (rows == 0) return;
-  TORCH_CHECK(x.stride(0) % 8 == 0, "row stride must be a multiple of 8");
-  argmax_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                                                           x.stride(0), V, out.data_ptr<int64_t>());
+  argmax_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), m, V,
+                                                           out.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void gumbel_sample_launch(const at::Tensor& x, at::Tensor& out, double inv_temp, int64_t seed, int64_t offset) {
   check_dev(x, "logits");
   check_dev(out, "out");
-  const int rows = x.size(0), V = x.size(1);
+  int rows, V;
+  RowMap m = row_map(x, rows, V);
+  TORCH_CHECK(out.numel() == rows, "sample output size");
   if (rows == 0) return;
-  TORCH_CHECK(x.stride(0) % 8 == 0, "row stride must be a multiple of 8");
-  gumbel_sample_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), V, (float)inv_temp, (uint32_t)seed,
-      (uint32_t)offset, out.data_ptr<int64_t>());
+  gumbel_sample_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                                  m, V, (float)inv_temp, (uint32_t)seed,
+                                                                  (uint32_t)offset, out.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -523,13 +558,15 @@ void fused_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const
   check_dev(spec, "spec");
   check_dev(accepted, "accepted");
   check_dev(corr, "corr");
-  const int rows = clean.size(0), V = clean.size(1);
+  int rows, V, rows2, V2;
+  RowMap cm = row_map(clean, rows, V);
+  RowMap dm = row_map(draft, rows2, V2);
+  TORCH_CHECK(rows == rows2 && V == V2 && spec.numel() == rows, "verify shapes");
   if (rows == 0) return;
-  TORCH_CHECK(clean.stride(0) % 8 == 0 && draft.stride(0) % 8 == 0, "row stride must be a multiple of 8");
   fused_verify_kernel<<<rows, SAMPLE_THREADS, 0, cur_stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(clean.data_ptr()), clean.stride(0),
-      reinterpret_cast<const __nv_bfloat16*>(draft.data_ptr()), draft.stride(0), spec.data_ptr<int64_t>(), V,
-      (float)inv_temp, (uint32_t)seed, (uint32_t)offset, accepted.data_ptr<int32_t>(), corr.data_ptr<int64_t>());
+      reinterpret_cast<const __nv_bfloat16*>(clean.data_ptr()), cm,
+      reinterpret_cast<const __nv_bfloat16*>(draft.data_ptr()), dm, spec.data_ptr<int64_t>(), V, (float)inv_temp,
+      (uint32_t)seed, (uint32_t)offset, accepted.data_ptr<int32_t>(), corr.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -262,23 +262,29 @@ def lm_head(x, weight):
 
 
 # --------------------------------------------------------------- sampling
+def _n_rows(x):
+    return x.shape[0] if x.dim() == 2 else x.shape[0] * x.shape[1]
+
+
 def argmax(logits):
-    out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
+    """Greedy tokens for 2-D [N, V] or strided 3-D [B, R, V] logits (no copy)."""
+    out = torch.empty(_n_rows(logits), device=logits.device, dtype=torch.int64)
     ext().argmax(logits, out)
     return out
 
 
 def sample_gumbel(logits, inv_temp, seed, offset):
-    out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
+    out = torch.empty(_n_rows(logits), device=logits.device, dtype=torch.int64)
     ext().gumbel_sample(logits, out, float(inv_temp), int(seed), int(offset))
     return out
 
 
 def fused_verify(clean, draft, spec, inv_temp, seed, offset):
-    n = clean.shape[0]
+    n = _n_rows(clean)
     acc = torch.empty(n, device=clean.device, dtype=torch.int32)
     corr = torch.empty(n, device=clean.device, dtype=torch.int64)
-    ext().fused_verify(clean, draft, spec.contiguous(), float(inv_temp), int(seed), int(offset), acc, corr)
+    ext().fused_verify(clean, draft, spec.reshape(-1).contiguous(), float(inv_temp), int(seed), int(offset), acc,
+                       corr)
     return acc, corr
 
 
