@@ -133,6 +133,14 @@ class ModelRunner:
                     "Insufficient GPU memory for KV cache allocation "
                     f"({per_page / 1e6:.2f} MB per page); increase gpu_memory_utilization"
                 )
+            if self.world_size > 1:
+                # Rank 0 schedules pages for every rank: all caches must hold the
+                # same page count, so agree on the smallest one.
+                import torch.distributed as dist
+
+                n = torch.tensor([config.num_kvcache_blocks], device=self.device)
+                dist.all_reduce(n, op=dist.ReduceOp.MIN)
+                config.num_kvcache_blocks = int(n.item())
         kvh = cfg.num_key_value_heads // self.world_size
         self.kv_cache = torch.zeros(
             cfg.num_hidden_layers, 2, config.num_kvcache_blocks, kvh, self.page, cfg.head_dim,
