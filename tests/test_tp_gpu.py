@@ -1,0 +1,46 @@
+"""Tensor parallelism on real GPUs: fused NVLink collectives vs NCCL vs TP=1."""
+
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(world: int, comm: str, eager: bool = False) -> dict:
+    env = dict(os.environ, UNO_TP_COMM=comm, NCCL_NVLS_ENABLE="0", TP_TEST_EAGER="1" if eager else "0",
+               TORCH_DISTRIBUTED_TIMEOUT_MINUTES="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "tp_worker.py")]
+    out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    line = [l for l in out.stdout.splitlines() if l.startswith("{")][-1]
+    return json.loads(line)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2])
+def test_fused_tp_matches_nccl_and_single_gpu(world):
+    one = _run(1, "fused")
+    nccl = _run(world, "nccl")
+    fused = _run(world, "fused")
+    fused_eager = _run(world, "fused", eager=True)
+    assert fused["err"] == 0 and nccl["err"] == 0
+    for res in (nccl, fused, fused_eager):
+        for a, b in zip(one["greedy"], res["greedy"]):
+            assert a[:4] == b[:4]  # greedy prefix agrees (bf16 reduction order may flip late near-ties)
+        assert all(len(t) >= 24 for t in res["sampled"])
+    assert fused["greedy"] == fused_eager["greedy"]  # graphs replay the same kernels

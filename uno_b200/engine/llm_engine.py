@@ -97,7 +97,7 @@ class LLMEngine:
 
         self.rank = int(os.environ.get("RANK", 0)) if config.distributed_init == "env" else 0
         self.control = init_distributed(config, self.rank, port)
-        self.model_runner = ModelRunner(config, self.rank)
+        self.model_runner = ModelRunner(config, self.rank, self.control)
         if self.control is not None:
             import torch.distributed as dist
 

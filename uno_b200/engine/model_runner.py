@@ -48,9 +48,11 @@ def sglang_batch_ladder(max_bs: int) -> list[int]:
 
 
 class ModelRunner:
-    def __init__(self, config, rank: int = 0):
+    def __init__(self, config, rank: int = 0, control=None):
         self.config = config
         self.rank = rank
+        self.control = control
+        self.tp_comm = None
         self.world_size = config.tensor_parallel_size
         self.page = config.kvcache_block_size
         cfg = config.hf_config
@@ -85,6 +87,16 @@ class ModelRunner:
             from uno_b200.ops import cuda as cuda_ops
 
             cuda_ops.prepare_model(self.model)
+            if self.world_size > 1 and os.environ.get("UNO_TP_COMM", "fused") != "nccl":
+                # Row-parallel outputs travel over NVLink peer memory with the
+                # reduction fused into residual-add + RMSNorm (no NCCL all-reduce).
+                from uno_b200.parallel.symm import FusedTPComm
+
+                max_q = max(config.max_diffusion_block_size, config.tree_verify_size or 0)
+                max_tokens = max(config.max_num_batched_tokens, config.max_num_seqs * max_q)
+                self.tp_comm = FusedTPComm(rank, self.world_size, control.group if control is not None else None,
+                                           max_tokens, cfg.hidden_size, self.device)
+                cuda_ops.set_tp_comm(self.tp_comm)
 
         self.sampler = Sampler(config.seed)
         self.allocate_kv_cache()
@@ -447,3 +459,13 @@ class ModelRunner:
         self.release_graphs()
         if self.device.type == "cuda":
             torch.cuda.synchronize()
+            if self.tp_comm is not None:
+                from uno_b200.ops import cuda as cuda_ops
+
+                cuda_ops.set_tp_comm(None)
+                if self.control is not None:
+                    import torch.distributed as dist
+
+                    dist.barrier(group=self.control.group)  # no peer still reads our workspace
+                self.tp_comm.close()
+                self.tp_comm = None

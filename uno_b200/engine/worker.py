@@ -78,7 +78,7 @@ def worker_main(config, rank: int, port: int, ready=None) -> None:
     control = None
     try:
         control = init_distributed(config, rank, port)
-        runner = ModelRunner(config, rank)
+        runner = ModelRunner(config, rank, control)
         dist.barrier(group=control.group)
         follower_loop(runner, control)
     except BaseException:
@@ -115,6 +115,6 @@ def serve_follower(model, tokenizer_path=None, **kwargs) -> None:
     if config.device == "cuda":
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     control = init_distributed(config, rank)
-    runner = ModelRunner(config, rank)
+    runner = ModelRunner(config, rank, control)
     dist.barrier(group=control.group)
     follower_loop(runner, control)

@@ -36,6 +36,10 @@ class RMSNorm(nn.Module):
             return ops.rms_norm(x, self.weight, self.eps, self.n_groups)
         return ops.add_rms_norm(x, residual, self.weight, self.eps, self.n_groups)
 
+    def first(self, x):
+        """Normalise the start of the residual stream: returns (normed, residual)."""
+        return ops.rms_norm_first(x, self.weight, self.eps, self.n_groups)
+
 
 class VocabParallelEmbedding(nn.Module):
     def __init__(self, num_embeddings: int, embedding_dim: int):
@@ -125,7 +129,7 @@ class DecoderLayer(nn.Module):
 
     def forward(self, x, residual, meta, cos_sin):
         if residual is None:
-            x, residual = self.input_layernorm(x), x
+            x, residual = self.input_layernorm.first(x)
         else:
             x, residual = self.input_layernorm(x, residual)
         x = self.self_attn(x, meta, cos_sin)

@@ -24,8 +24,15 @@ def rms_norm(x, weight, eps, n_groups=1):
     return ref.rms_norm(x, weight, eps, n_groups)
 
 
+def rms_norm_first(x, weight, eps, n_groups=1):
+    """Norm that starts the residual stream: returns (normed, residual)."""
+    if not isinstance(x, torch.Tensor) or x.is_cuda:
+        return _cuda().rms_norm_first(x, weight, eps, n_groups)
+    return ref.rms_norm(x, weight, eps, n_groups), x
+
+
 def add_rms_norm(x, residual, weight, eps, n_groups=1):
-    if x.is_cuda:
+    if not isinstance(x, torch.Tensor) or x.is_cuda:
         return _cuda().add_rms_norm(x, residual, weight, eps, n_groups)
     return ref.add_rms_norm(x, residual, weight, eps, n_groups)
 

@@ -23,6 +23,14 @@ void fused_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const
 void topk_lse_launch(const at::Tensor& x, int K, double inv_temp, at::Tensor& ids, at::Tensor& lp);
 void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at::Tensor& lp, int Qn, at::Tensor& tok,
                        at::Tensor& par, at::Tensor& dep, at::Tensor& mass, at::Tensor& count);
+void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t H,
+                               int64_t recv_off, int64_t gather_off, at::Tensor& residual, bool add_residual,
+                               const at::Tensor& weight, int64_t groups, double eps);
+void embedding_scatter_launch(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& ids,
+                              const at::Tensor& table, int64_t start, int64_t recv_off, int64_t gather_off);
+std::vector<int64_t> symm_alloc(int64_t nbytes);
+int64_t symm_open(const std::vector<int64_t>& handle_bytes);
+void symm_close(int64_t ptr, bool owned);
 void walk_tree_launch(const at::Tensor& tok, const at::Tensor& par, const at::Tensor& tgt, int max_depth, int64_t pad,
                       at::Tensor& committed, at::Tensor& accepted, at::Tensor& lengths);
 
@@ -70,7 +78,8 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
                  c10::optional<at::Tensor> slots, c10::optional<at::Tensor> positions,
                  c10::optional<at::Tensor> cos_sin, c10::optional<at::Tensor> q_norm_w,
                  c10::optional<at::Tensor> k_norm_w, double eps, int64_t hq, int64_t hkv, int64_t page,
-                 int64_t max_ctas, int64_t splits) {
+                 int64_t max_ctas, int64_t splits, std::vector<int64_t> rs_peers, int64_t rs_rank,
+                 int64_t rs_recv_off) {
   check_dev(a, "gemm A");
   check_dev(b, "gemm B");
   UNO_CHECK_BF16(a);
@@ -116,7 +125,18 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   if (epi == 5) TORCH_CHECK(p.q_out && p.slots && p.positions && p.cos_sin, "QK-RoPE epilogue arguments missing");
   if (epi == 2) TORCH_CHECK(p.row_mask != nullptr, "ROWSCALE needs row_mask");
   if (epi == 3) TORCH_CHECK(p.R != nullptr, "ADD needs a residual");
-  if (epi != 5) TORCH_CHECK(p.C != nullptr, "output tensor missing");
+  if (!rs_peers.empty()) {
+    TORCH_CHECK(epi == 0 && rs_peers.size() <= 8, "reduce-scatter send needs the STORE epilogue and <= 8 ranks");
+    const int tp = (int)rs_peers.size();
+    for (int j = 0; j < tp; ++j) p.rs_peers[j] = reinterpret_cast<uint8_t*>(rs_peers[j]);
+    p.rs_enable = 1;
+    p.rs_rank = (int)rs_rank;
+    p.rs_R = (p.M + tp - 1) / tp;
+    p.rs_recv_off = (int)rs_recv_off;
+    TORCH_CHECK((p.N * 2) % 16 == 0, "row width must be 16-byte aligned");
+  } else if (epi != 5) {
+    TORCH_CHECK(p.C != nullptr, "output tensor missing");
+  }
   DeviceScratch& scratch = device_scratch();
   p.err = scratch.err;
   int tile = pick_bn(p.M, p.N, (int)bn);
@@ -200,5 +220,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_lse", &uno::topk_lse_launch);
   m.def("build_tree", &uno::build_tree_launch);
   m.def("walk_tree", &uno::walk_tree_launch);
+  m.def("reduce_norm_gather", &uno::reduce_norm_gather_launch);
+  m.def("embedding_scatter", &uno::embedding_scatter_launch);
+  m.def("symm_alloc", &uno::symm_alloc);
+  m.def("symm_open", &uno::symm_open);
+  m.def("symm_close", &uno::symm_close);
   m.def("error_flag", &uno::read_error_flag, py::arg("reset") = false);
 }

@@ -194,16 +194,32 @@ __device__ __forceinline__ void qkrope_head(const GemmParams& p, const AccSrc& s
 #pragma unroll
         for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
         const float inv = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
+        const uint4* w4 = reinterpret_cast<const uint4*>(w);
 #pragma unroll
-        for (int i = 0; i < 128; ++i) v[i] = bf16r(v[i] * inv * __bfloat162float(w[i]));
+        for (int j = 0; j < 16; ++j) {
+          const uint4 ww = __ldg(w4 + j);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&ww);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h2[e]);
+            v[8 * j + 2 * e] = bf16r(v[8 * j + 2 * e] * inv * f.x);
+            v[8 * j + 2 * e + 1] = bf16r(v[8 * j + 2 * e + 1] * inv * f.y);
+          }
+        }
       }
-      const float* cs = p.cos_sin + (size_t)p.positions[row] * 128;
+      // NeoX rotation with the [cos | sin] row of this position (float4 loads)
+      const float4* cs4 = reinterpret_cast<const float4*>(p.cos_sin + (size_t)p.positions[row] * 128);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float c = cs[i], s = cs[64 + i];
-        const float x1 = v[i], x2 = v[64 + i];
-        v[i] = x1 * c - x2 * s;
-        v[64 + i] = x2 * c + x1 * s;
+      for (int j = 0; j < 16; ++j) {
+        const float4 c = __ldg(cs4 + j), sn = __ldg(cs4 + 16 + j);
+        const float cc[4] = {c.x, c.y, c.z, c.w}, ss4[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * j + e;
+          const float x1 = v[i], x2 = v[64 + i];
+          v[i] = x1 * cc[e] - x2 * ss4[e];
+          v[64 + i] = x2 * cc[e] + x1 * ss4[e];
+        }
       }
     }
   }
@@ -270,7 +286,16 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, const AccSrc& 
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= sc;
       }
-      if (row_ok) dst = (uint64_t)(p.C + (size_t)row * p.ldc + col);
+      if (row_ok) {
+        if (EPI == EPI_STORE && p.rs_enable) {
+          // reduce-scatter send: partial row -> owner's receive slot (NVLink P2P store)
+          const int owner = row / p.rs_R, lr = row - owner * p.rs_R;
+          dst = (uint64_t)(p.rs_peers[owner] + p.rs_recv_off +
+                           (((size_t)p.rs_rank * p.rs_R + lr) * p.N + col) * 2);
+        } else {
+          dst = (uint64_t)(p.C + (size_t)row * p.ldc + col);
+        }
+      }
       S::row_write(buf, lane, 0, v, 32);
       __syncwarp();
       S::store(buf, lane, dst, vcols);
@@ -484,6 +509,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
+  if (EPI == EPI_STORE && p.rs_enable) __threadfence_system();  // peer stores visible before the reduce
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

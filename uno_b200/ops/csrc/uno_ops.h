@@ -40,6 +40,10 @@ struct GemmParams {
   int splits;
   float* ws;
   int* counters;
+  // reduce-scatter send (row-parallel TP): row r goes to rank r / rs_R, slot
+  // rs_rank, at byte offset rs_recv_off of that rank's symmetric workspace
+  uint8_t* rs_peers[8];
+  int rs_enable, rs_rank, rs_R, rs_recv_off;
 };
 void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,
                    int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas);

@@ -22,6 +22,23 @@ from uno_b200.layers.meta import ForwardMeta, Mode
 from uno_b200.parallel import state as tp
 
 _C = None
+# Fused tensor-parallel collectives (uno_b200.parallel.symm.FusedTPComm) or None.
+_COMM = None
+
+
+def set_tp_comm(comm) -> None:
+    global _COMM
+    _COMM = comm
+
+
+class PendingRS:
+    """Marker: row-parallel partials were sent to the owners' receive slots and
+    the next (add+)RMSNorm must run the fused reduce-norm-gather kernel."""
+
+    __slots__ = ("T",)
+
+    def __init__(self, T: int):
+        self.T = int(T)
 
 EPI_STORE, EPI_SILU, EPI_ROWSCALE, EPI_ADD, EPI_QKROPE = 0, 1, 2, 3, 5
 INTERLEAVE = 64
@@ -48,9 +65,10 @@ def error_flag(reset: bool = False) -> int:
 
 def _gemm(a, b, epi, *, c=None, r=None, a2=None, b2=None, scale=0.0, row_mask=None, q_out=None,
           k_cache=None, v_cache=None, slots=None, positions=None, cos_sin=None, q_norm_w=None,
-          k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0, splits=0):
+          k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0, splits=0, rs=None):
+    peers, rank, off = ([], 0, 0) if rs is None else rs
     ext().gemm(a, b, epi, bn, c, r, a2, b2, scale, row_mask, q_out, k_cache, v_cache, slots, positions,
-               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas, splits)
+               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas, splits, peers, rank, off)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, bn: int = 0, splits: int = 0) -> torch.Tensor:
@@ -118,8 +136,17 @@ def rms_norm(x, weight, eps, n_groups=1):
     return y.view(x.shape)
 
 
+def rms_norm_first(x, weight, eps, n_groups=1):
+    """First norm of the residual stream: returns (normed, residual)."""
+    if isinstance(x, PendingRS):
+        return _COMM.reduce_norm(x.T, None, weight, eps, n_groups)
+    return rms_norm(x, weight, eps, n_groups), x
+
+
 def add_rms_norm(x, residual, weight, eps, n_groups=1):
     """Returns (normed, new_residual); the residual buffer is updated in place."""
+    if isinstance(x, PendingRS):
+        return _COMM.reduce_norm(x.T, residual, weight, eps, n_groups)
     x2 = _rows(x)
     y = torch.empty(x2.shape, device=x.device, dtype=x.dtype)
     res = residual if residual.is_contiguous() else residual.contiguous()
@@ -133,11 +160,14 @@ def _row_parallel(layer) -> bool:
 
 
 def lora_hidden(x, layer, lora_mask):
-    """``scale * mask * (x A_cat^T)`` [M, R] (all-reduced for row-parallel layers)."""
+    """``scale * mask * (x A_cat^T)`` [M, R].
+
+    For a row-parallel layer this is the rank's partial hidden (its K shard);
+    every rank adds ``h_r . B^T`` to its partial output, and the reduction of
+    the outputs sums the partial hiddens as well, so no extra collective runs.
+    """
     h = torch.empty(x.shape[0], layer.lora_rank_total, device=x.device, dtype=torch.bfloat16)
     _gemm(x, layer.lora_a_dev, EPI_ROWSCALE, c=h, scale=layer.lora_scaling, row_mask=lora_mask)
-    if _row_parallel(layer):
-        tp.all_reduce(h)
     return h
 
 
@@ -145,16 +175,16 @@ def _lora_ext(x, layer, lora_mask):
     """K-extension operands (a2, b2) for the base GEMM, or (None, None)."""
     if lora_mask is None or not layer.has_lora:
         return None, None
-    h = lora_hidden(x, layer, lora_mask)
-    if _row_parallel(layer) and layer.tp_rank != 0:
-        # the adapter term is replicated; exactly one rank adds it before the sum
-        return None, None
-    return h, layer.lora_b_dev
+    return lora_hidden(x, layer, lora_mask), layer.lora_b_dev
 
 
 def linear(x, layer, lora_mask=None):
     x = _rows(x)
     a2, b2 = _lora_ext(x, layer, lora_mask)
+    if _COMM is not None and _row_parallel(layer):
+        # fused reduce-scatter: partial rows go straight to their owners
+        _gemm(x, layer.weight, EPI_STORE, a2=a2, b2=b2, rs=_COMM.rs_args(x.shape[0]))
+        return PendingRS(x.shape[0])
     y = torch.empty(x.shape[0], layer.weight.shape[0], device=x.device, dtype=torch.bfloat16)
     _gemm(x, layer.weight, EPI_STORE, c=y, a2=a2, b2=b2)
     if _row_parallel(layer):
@@ -250,6 +280,9 @@ def attention(q, k_cache, v_cache, meta: ForwardMeta, scale):
 
 # ------------------------------------------------------------ embeddings
 def embedding(ids, table, vocab_start=0):
+    if _COMM is not None:
+        _COMM.embedding_scatter(ids, table, vocab_start)
+        return PendingRS(ids.numel())
     out = torch.empty(ids.numel(), table.shape[1], device=ids.device, dtype=table.dtype)
     ext().embedding(ids.reshape(-1).contiguous(), table, out, int(vocab_start))
     if tp.tp_size() > 1:
