@@ -56,9 +56,10 @@ def test_gemm_split_k(C, splits):
     assert rel_err(y, ref + r.float()) < 1e-2
 
 
-def test_gemm_silu_interleaved(C):
+@pytest.mark.parametrize("M", [200, 300, 512])
+def test_gemm_silu_interleaved(C, M):
     torch.manual_seed(0)
-    M, K, I = 200, 512, 384
+    K, I = 512, 384
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(2 * I, K, device=DEV, dtype=torch.bfloat16) * 0.05
     wi = C.interleave_gate_up(w)
@@ -70,9 +71,10 @@ def test_gemm_silu_interleaved(C):
 
 
 @pytest.mark.parametrize("splits", [1, 2])
-def test_gemm_lora_hidden_and_k_extension(C, splits):
+@pytest.mark.parametrize("M", [96, 384])
+def test_gemm_lora_hidden_and_k_extension(C, splits, M):
     torch.manual_seed(1)
-    M, K, N, R = 96, 1024, 512, 64
+    K, N, R = 1024, 512, 64
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.05
     a = torch.randn(R, K, device=DEV, dtype=torch.bfloat16) * 0.05
@@ -110,11 +112,12 @@ def _ref_qkrope(qkv, positions, cos_sin, qw, kw, hq, hkv, eps):
 
 
 @pytest.mark.parametrize("lora", [False, True])
-def test_gemm_qk_rope_store(C, lora):
+@pytest.mark.parametrize("T", [70, 300])
+def test_gemm_qk_rope_store(C, lora, T):
     from uno_b200.layers.rotary import cos_sin_cache
 
     torch.manual_seed(2)
-    T, K, hq, hkv, page, pages = 70, 512, 4, 2, 64, 8
+    K, hq, hkv, page, pages = 512, 4, 2, 64, 8
     N = (hq + 2 * hkv) * 128
     x = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.05

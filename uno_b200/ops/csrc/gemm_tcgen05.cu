@@ -518,6 +518,244 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+// Two CTAs of a cluster compute one 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 rows of A and
+// half (128 rows) of the B tile, so every SM streams 32 KB per 64-deep k-block
+// instead of 48 KB for the same tensor work.  The leader CTA (cluster rank 0)
+// owns the stage-full and accumulator-empty barriers and issues every MMA; the
+// peer's TMA loads report their bytes to the leader's barrier (cta_group::2
+// load form), and MMA completion is committed to both CTAs' barriers.  Each CTA
+// runs the epilogue on its own 128 accumulator rows.
+template <int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                          GemmParams p) {
+  constexpr int BN = 256;
+  using Cfg = GemmCfg<128, EPI>;  // per-CTA stage = 128x64 A + 128x64 B
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int TMEM_COLS = 2 * BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::EPI_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.K2 > 0) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m2 = (p.M + 255) / 256;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m2 * num_n;
+  const int splits = p.splits;
+  const int num_units = num_tiles * splits;
+  const int kb_main = (p.K + Cfg::BK - 1) / Cfg::BK;
+  const int k_blocks = kb_main + (p.K2 + Cfg::BK - 1) / Cfg::BK;
+  const int kb_per = (k_blocks + splits - 1) / splits;
+  const int cid = (int)cluster_id_x(), ncl = (int)num_clusters_x();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      for (int u = cid; u < num_units && !*abort_flag; u += ncl) {
+        const int tile = u % num_tiles, ks = u / num_tiles;
+        const int m2 = tile % num_m2, n_blk = tile / num_m2;
+        const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
+        const int arow = m2 * 256 + (int)rank * 128;
+        const int brow = n_blk * BN + (int)rank * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          if (kb < kb_main) {
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, lead_full, kb * Cfg::BK, arow);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, lead_full, kb * Cfg::BK, brow);
+          } else {
+            const int k2 = (kb - kb_main) * Cfg::BK;
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA2, lead_full, k2, arow);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB2, lead_full, k2, brow);
+          }
+#pragma unroll
+          for (int s = 0; s < STAGES; ++s)
+            if (s == stage) {
+              issued[s] = true;
+              issued_phase[s] = phase;
+            }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag && leader) {  // let in-flight copies land before the CTA exits
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&full[s], issued_phase[s], p.err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_bf16(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = cid; u < num_units && !*abort_flag; u += ncl) {
+        const int ks = u / num_tiles;
+        const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc_sw128(sA + stage * Cfg::A_BYTES);
+          const uint64_t bdesc = smem_desc_sw128(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k)
+            tc_mma_bf16_pair(d, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc, (kb > kb0 || k > 0));
+          const uint32_t e_addr = smem_u32(&empty[stage]);
+          tc_commit_pair(mapa_shared(e_addr, 0));
+          tc_commit_pair(mapa_shared(e_addr, 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t f_addr = smem_u32(&tfull[acc]);
+        tc_commit_pair(mapa_shared(f_addr, 0));
+        tc_commit_pair(mapa_shared(f_addr, 1));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    uint8_t* buf = sEpi + (warp - 2) * 32 * Cfg::PITCH;
+    const int num_m128 = num_m2 * 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = cid; u < num_units; u += ncl) {
+      const int tile = u % num_tiles, ks = u / num_tiles;
+      const int m2 = tile % num_m2, n_blk = tile / num_m2;
+      const int m_blk = m2 * 2 + (int)rank;  // this CTA's 128-row block
+      const int ctile = m_blk + num_m128 * n_blk;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, p.err);
+      ok = __shfl_sync(0xffffffff, ok, 0);
+      if (!ok || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int row = m_blk * 128 + row_in_tile;
+      const uint32_t lead_tempty = mapa_shared(smem_u32(&tempty[acc]), 0);
+      if (splits == 1) {
+        AccSrc src{taddr, nullptr, 1, BN, row_in_tile};
+        run_epilogue<BN, EPI>(p, src, buf, lane, row, n_blk);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_tempty);
+      } else {
+        float* mine = p.ws + ((size_t)ctile * splits + ks) * 128 * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(mine + ((size_t)(c / 4 + q) * 128 + row_in_tile) * 4) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_tempty);
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(p.counters + ctile, 1);
+          *last_flag = (old == splits - 1);
+        }
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          AccSrc src{0u, p.ws + (size_t)ctile * splits * 128 * BN, splits, BN, row_in_tile};
+          run_epilogue<BN, EPI>(p, src, buf, lane, row, n_blk);
+          epi_bar();
+          if (threadIdx.x == 64) p.counters[ctile] = 0;
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  if (EPI == EPI_STORE && p.rs_enable) __threadfence_system();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer is done with the leader's barriers and TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -575,6 +813,42 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                        GemmParams& p, cudaStream_t stream, int max_ctas) {
+  using Cfg = GemmCfg<128, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    configured = true;
+  }
+  const int units = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.splits;
+  const int pairs = std::max(1, std::min(units, (max_ctas > 0 ? max_ctas : num_sms()) / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel<EPI>, ta, tb, ta2, tb2, p));
+}
+
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("UNO_GEMM_PAIR");
+    v = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 int pick_bn(int M, int N, int forced) {
   if (forced) return forced;
   if (N <= 256) return 64;  // skinny outputs (LoRA hidden): more tiles, cheap split-K reduction
@@ -602,7 +876,13 @@ static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64
   CUtensorMap ta2 = p.K2 > 0 ? make_tmap_bf16(a2, p.M, p.K2, lda2, 128) : ta;
   p.num_m = (p.M + 127) / 128;
   p.num_n = (p.N + bn - 1) / bn;
-  if (bn == 256) {
+  if (bn == 256 && p.M >= 256 && pair_enabled()) {
+    // CTA-pair path: 128-row boxes for both operands (each CTA stages half of B)
+    CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 128);
+    CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 128) : tb;
+    p.num_m = ((p.M + 255) / 256) * 2;
+    launch_pair<EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
+  } else if (bn == 256) {
     CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 256);
     CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 256) : tb;
     launch<256, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
