@@ -140,7 +140,7 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   DeviceScratch& scratch = device_scratch();
   p.err = scratch.err;
   int tile = pick_bn(p.M, p.N, (int)bn);
-  if ((epi == 1 || epi == 5) && tile == 64) tile = 128;
+  if ((epi == 1 || epi == 5) && tile < 128) tile = 128;
   p.splits = pick_splits(p.M, p.N, p.K + p.K2, tile, (int)splits);
   const int tiles = ((p.M + 127) / 128) * ((p.N + tile - 1) / tile);
   if (p.splits > 1 &&

@@ -851,7 +851,7 @@ static bool pair_enabled() {
 
 int pick_bn(int M, int N, int forced) {
   if (forced) return forced;
-  if (N <= 256) return 64;  // skinny outputs (LoRA hidden): more tiles, cheap split-K reduction
+  if (N <= 256) return 32;  // skinny outputs (LoRA hidden): many small tiles, cheap split-K reduction
   return 256;
 }
 
@@ -864,7 +864,7 @@ int pick_splits(int M, int N, int K, int bn, int forced) {
   const int kb = (K + 63) / 64;
   if (tiles * 5 >= sms * 3 || kb < 16) return 1;
   // Few tiles: up to 16 splits of >= 4 k-blocks for skinny outputs, else 4.
-  const int cap = bn <= 64 ? 16 : 4;
+  const int cap = bn <= 64 ? 8 : 4;
   int s = std::min({cap, std::max(1, sms / tiles), kb / (bn <= 64 ? 4 : 8)});
   return std::max(1, s);
 }
@@ -893,10 +893,15 @@ static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64
   } else {
     if constexpr (EPI == EPI_SILU || is_qkrope<EPI>()) {
       TORCH_CHECK(false, "this epilogue needs a 128 or 256 column tile");
-    } else {
+    } else if (bn == 64) {
       CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 64);
       CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 64) : tb;
       launch<64, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
+    } else {
+      TORCH_CHECK(bn == 32, "unsupported tile width ", bn);
+      CUtensorMap tb = make_tmap_bf16(b, p.N, p.K, ldb, 32);
+      CUtensorMap tb2 = p.K2 > 0 ? make_tmap_bf16(b2, p.N, p.K2, ldb2, 32) : tb;
+      launch<32, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
     }
   }
 }
