@@ -9,7 +9,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("uno_b200", "ops", "csrc")
 SOURCES = [
     os.path.join(CSRC, name)
-    for name in ("bindings.cpp", "gemm_tcgen05.cu", "attention.cu", "elementwise.cu", "sampling.cu", "comm.cu")
+    for name in ("bindings.cpp", "gemm_tcgen05.cu", "gemm_noalloc.cu", "attention.cu", "elementwise.cu",
+                 "sampling.cu", "comm.cu")
 ]
 
 NVCC_FLAGS = [

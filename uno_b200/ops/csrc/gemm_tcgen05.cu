@@ -863,7 +863,7 @@ int pick_splits(int M, int N, int K, int bn, int forced) {
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   const int kb = (K + 63) / 64;
   if (tiles * 5 >= sms * 3 || kb < 16) return 1;
-  // Few tiles: up to 16 splits of >= 4 k-blocks for skinny outputs, else 4.
+  // Few tiles: up to 8 splits of >= 4 k-blocks for skinny outputs, else 4.
   const int cap = bn <= 64 ? 8 : 4;
   int s = std::min({cap, std::max(1, sms / tiles), kb / (bn <= 64 ? 4 : 8)});
   return std::max(1, s);
