@@ -35,7 +35,9 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "Uno-Qwen3-8B Psi-Spec output tok/s at TP=1/2/4/8; per-request tok/s; TPF"
-BASELINE_TOKS = None  # BASELINE.json publishes no number (chart estimate only)
+# The reference publishes one throughput figure: about 5,200 tok/s for Uno (Psi-Spec), read
+# off its results chart (hardware unspecified).
+BASELINE_TOKS = 5200.0
 VOCAB = 151936
 MASK_ID = 151669
 
