@@ -99,7 +99,13 @@ class Config:
             self.model_source = str(self.model)
             path = os.path.expanduser(str(self.model))
             if not os.path.isdir(path):
-                raise FileNotFoundError(f"Model path does not exist: {path}")
+                from uno_b200.utils.hub import resolve_hf_snapshot
+
+                try:
+                    path = resolve_hf_snapshot(self.model, revision=self.model_revision, cache_dir=self.hf_cache_dir,
+                                               local_files_only=self.hf_local_files_only, artifact_name="model")
+                except ValueError as exc:
+                    raise FileNotFoundError(f"Model path does not exist: {path}") from exc
             # Pick the latest ``checkpoint-N`` sub-directory when present
             # (reference ``config.py:91-101``).
             ckpts = [d for d in os.listdir(path) if d.startswith("checkpoint-")
@@ -174,7 +180,15 @@ class Config:
         if self.gated_lora_path is not None:
             self.gated_lora_source = self.gated_lora_path
             if not os.path.isdir(self.gated_lora_path):
-                raise FileNotFoundError(f"gated LoRA adapter not found: {self.gated_lora_path}")
+                from uno_b200.utils.hub import ADAPTER_ALLOW_PATTERNS, resolve_hf_snapshot
+
+                try:
+                    self.gated_lora_path = resolve_hf_snapshot(
+                        self.gated_lora_path, revision=self.gated_lora_revision, cache_dir=self.hf_cache_dir,
+                        local_files_only=self.hf_local_files_only, allow_patterns=ADAPTER_ALLOW_PATTERNS,
+                        artifact_name="gated LoRA adapter")
+                except ValueError as exc:
+                    raise FileNotFoundError(f"gated LoRA adapter not found: {self.gated_lora_path}") from exc
         if self.device not in {"cuda", "cpu"}:
             raise ValueError("device must be 'cuda' or 'cpu'")
         if self.device == "cpu" or os.environ.get("NANO_VLLM_FORCE_FLOAT32", "0") == "1":
