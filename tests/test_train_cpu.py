@@ -1,0 +1,236 @@
+"""Conditional-LoRA diffusion training on CPU (BASELINE config 1 training step)."""
+
+import json
+import os
+
+import pytest
+import torch
+
+from uno_b200.train import (IGNORE_INDEX, BlockCurriculumPlan, LoraSettings, TrainableLoRA, UnoObjectiveConfig,
+                            UnoTrainer, build_uno_batch, shift_labels_for_next_token)
+from uno_b200.train.layout import visibility
+from uno_b200.train.losses import fused_head_loss, reference_losses
+
+
+# ------------------------------------------------------------------ layout
+def test_layout_places_noisy_then_clean_per_packed_sequence():
+    ids = torch.tensor([[10, 11, 12, 13, 20, 21]])
+    labels = torch.tensor([[IGNORE_INDEX, 11, 12, 13, 20, 21]])
+    pos = torch.tensor([[0, 1, 2, 3, 0, 1]])  # two packed sequences of 4 and 2 tokens
+    ub = build_uno_batch(ids, labels, pos, block_size=2, mask_token_id=100, generator=torch.Generator().manual_seed(0))
+    # layout: [noisy(seq0) 4][clean(seq0) 4][noisy(seq1) 2][clean(seq1) 2]
+    assert ub.noisy.tolist() == [[True] * 4 + [False] * 4 + [True] * 2 + [False] * 2]
+    assert ub.positions.tolist() == [[0, 1, 2, 3, 0, 1, 2, 3, 0, 1, 0, 1]]
+    assert ub.ids[0, 4:8].tolist() == [10, 11, 12, 13] and ub.ids[0, 10:].tolist() == [20, 21]
+    # unsupervised tokens are never noised; noise ids lie in [1, mask)
+    assert not bool(ub.noised[0, 0])
+    noisy_ids = ub.ids[0, ub.noisy_index[0]]
+    assert bool(((noisy_ids == ids[0]) | ub.noised[0]).all())
+    assert bool(((noisy_ids >= 1) & (noisy_ids < 100) | ~ub.noised[0]).all())
+    assert ub.p_mask.numel() == int(ub.noised.sum())
+    hidden = torch.arange(12.0)[None, :, None]
+    n, c = ub.gather_regions(hidden)
+    assert n[0, :, 0].tolist() == [0, 1, 2, 3, 8, 9] and c[0, :, 0].tolist() == [4, 5, 6, 7, 10, 11]
+
+
+def test_visibility_rules():
+    seg = torch.tensor([[0] * 8])
+    pos = torch.tensor([[0, 1, 2, 3, 0, 1, 2, 3]])
+    noisy = torch.tensor([[True] * 4 + [False] * 4])
+    vis = visibility(seg, pos, noisy, block_size=2)[0]
+    # noisy token at position 2 (block 1): noisy 2,3 of its block; clean positions 0,1 only
+    assert vis[2].tolist() == [False, False, True, True, True, True, False, False]
+    # noisy token at position 0: only its own block's noisy tokens
+    assert vis[0].tolist() == [True, True, False, False, False, False, False, False]
+    # clean token at position 2: clean 0..2
+    assert vis[6].tolist() == [False, False, False, False, True, True, True, False]
+    # packed sequences never see each other
+    seg2 = torch.tensor([[0, 0, 1, 1]])
+    vis2 = visibility(seg2, torch.tensor([[0, 1, 0, 1]]), torch.tensor([[False] * 4]), 2)[0]
+    assert not bool(vis2[2, 0]) and not bool(vis2[3, 1])
+
+
+def test_shift_labels_masks_packed_boundaries():
+    labels = torch.tensor([[1, 2, 3, 4, 5]])
+    pos = torch.tensor([[0, 1, 2, 0, 1]])
+    assert shift_labels_for_next_token(labels, pos).tolist() == [[2, 3, IGNORE_INDEX, 5, IGNORE_INDEX]]
+
+
+# ------------------------------------------------------------------ losses
+@pytest.mark.parametrize("weights,teacher_ce", [((1.0, 0.0, 0.0), True), ((0.0, 1.0, 0.0), True),
+                                                ((0.3, 0.5, 0.7), True), ((0.0, 0.0, 1.0), False)])
+def test_fused_head_loss_matches_autograd(weights, teacher_ce):
+    torch.manual_seed(0)
+    N, H, V = 23, 16, 97
+    W = torch.randn(V, H)
+    sh = torch.randn(N, H, requires_grad=True)
+    th = torch.randn(N, H)
+    dist_mask = torch.rand(N) < 0.8
+    ce_mask = dist_mask & (torch.rand(N) < 0.6)
+    p = torch.rand(N) * 0.9 + 0.1
+    tgt = torch.randint(0, V, (N,))
+    tv_w, kl_w, ce_w = weights
+    count = int(dist_mask.sum())
+    loss = fused_head_loss(sh, th, W, dist_mask=dist_mask, ce_mask=ce_mask, ce_target=tgt, ce_scale=1 / p,
+                           tv_weight=tv_w, kl_weight=kl_w, ce_weight=ce_w, teacher_ce=teacher_ce,
+                           normalizer=count, chunk=7)
+    loss.backward()
+    g_fused = sh.grad.clone()
+    sh2 = sh.detach().clone().requires_grad_(True)
+    s, t = sh2 @ W.t(), th @ W.t()
+    tv, kl = reference_losses(s[dist_mask], t[dist_mask], count)
+    y = t.argmax(-1) if teacher_ce else tgt
+    ce = (torch.nn.functional.cross_entropy(s[ce_mask], y[ce_mask], reduction="none") / p[ce_mask]).sum() / count
+    ref = tv_w * tv + kl_w * kl + ce_w * ce
+    ref.backward()
+    assert torch.allclose(loss, ref, rtol=1e-4, atol=1e-5)
+    assert torch.allclose(g_fused, sh2.grad, rtol=1e-3, atol=1e-5)
+
+
+# -------------------------------------------------------------- training
+def _tiny_setup(rank=8, seed=0):
+    from uno_b200.models.decoder import build_model
+    from uno_b200.models.presets import resolve_preset
+    from uno_b200.utils.loader import dummy_init
+
+    cfg = resolve_preset("tiny-qwen3")
+    model = build_model(cfg)
+    dummy_init(model, seed=seed)
+    lora = TrainableLoRA(cfg, LoraSettings(rank=rank, alpha=16), seed=seed)
+    return cfg, model, lora
+
+
+def _batch(B=2, S=128, vocab=4096, seed=0):
+    from uno_b200.train.data import synthetic_batches
+
+    return next(synthetic_batches(B, S, vocab, seed=seed))
+
+
+def test_config1_training_step_updates_lora_only():
+    cfg, model, lora = _tiny_setup()
+    base_before = {k: v.clone() for k, v in model.state_dict().items()}
+    plan = BlockCurriculumPlan.fixed([4], 3, 128, 2)
+    tr = UnoTrainer(model, lora, objective=UnoObjectiveConfig(ce_weight=0.5, kl_weight=0.5, tv_weight=1.0),
+                    curriculum=plan, mask_token_id=cfg.mask_token_id, lr=1e-2)
+    m = tr.train_step([_batch()])
+    assert m["step"] == 1 and m["block_size"] == 4 and m["tokens"] == 256 and m["noised_tokens"] > 0
+    assert torch.isfinite(torch.tensor(m["loss"])) and m["grad_norm"] > 0
+    assert any(float(b.detach().abs().sum()) > 0 for b in lora.B.values())  # B starts at zero
+    for k, v in model.state_dict().items():
+        assert torch.equal(v, base_before[k]), k
+
+
+def test_training_reduces_loss_on_a_fixed_batch():
+    cfg, model, lora = _tiny_setup(seed=1)
+    plan = BlockCurriculumPlan.fixed([4], 12, 64, 2)
+    tr = UnoTrainer(model, lora, objective=UnoObjectiveConfig(), curriculum=plan, mask_token_id=cfg.mask_token_id,
+                    lr=3e-3, seed=5)
+    batch = _batch(2, 64, seed=3)
+    losses = []
+    for _ in range(12):
+        tr.generator.manual_seed(123)  # same noise every step
+        losses.append(tr.train_step([batch])["loss"])
+    assert losses[-1] < 0.7 * losses[0]
+
+
+def test_curriculum_checkpoint_and_resume(tmp_path):
+    cfg, model, lora = _tiny_setup()
+    plan = BlockCurriculumPlan.fixed([2, 4], 1, 32, 1)
+    obj = UnoObjectiveConfig()
+    tr = UnoTrainer(model, lora, objective=obj, curriculum=plan, mask_token_id=cfg.mask_token_id, lr=1e-2,
+                    output_dir=str(tmp_path))
+    b = _batch(1, 32)
+    assert tr.train_step([b])["block_size"] == 2
+    ckpt = tmp_path / "checkpoint-1"
+    state = json.loads((ckpt / "uno_curriculum_state.json").read_text())
+    assert state["reason"] == "completed_block_size_2" and state["curriculum_sha256"] == plan.sha256()
+    assert (ckpt / "adapter_config.json").is_file()
+    # resume into a fresh trainer: same LoRA, continues at stage 2
+    _, model2, lora2 = _tiny_setup(seed=9)
+    tr2 = UnoTrainer(model2, lora2, objective=obj, curriculum=plan, mask_token_id=cfg.mask_token_id, lr=1e-2)
+    tr2.resume(ckpt)
+    assert tr2.step == 1
+    for k in lora.A:
+        assert torch.equal(lora.A[k], lora2.A[k]) and torch.equal(lora.B[k], lora2.B[k])
+    assert tr2.curriculum.stage_for_step(tr2.step).block_size == 4
+    other = BlockCurriculumPlan.fixed([2, 8], 1, 32, 1)
+    tr3 = UnoTrainer(model2, lora2, objective=obj, curriculum=other, mask_token_id=cfg.mask_token_id)
+    with pytest.raises(ValueError, match="curriculum"):
+        tr3.resume(ckpt)
+
+
+def test_trained_adapter_serves_in_the_inference_engine(tmp_path):
+    from uno_b200 import LLM, SamplingParams
+
+    cfg, model, lora = _tiny_setup()
+    plan = BlockCurriculumPlan.fixed([4], 1, 32, 1)
+    UnoTrainer(model, lora, objective=UnoObjectiveConfig(), curriculum=plan, mask_token_id=cfg.mask_token_id,
+               lr=1e-2).train_step([_batch(1, 32)])
+    path = str(tmp_path / "adapter")
+    lora.save(path, "preset:tiny-qwen3")
+    llm = LLM("preset:tiny-qwen3", device="cpu", max_num_seqs=2, max_model_len=128, kvcache_block_size=64,
+              gated_lora_path=path, max_diffusion_block_size=4)
+    out = llm.generate([[5, 6, 7]], SamplingParams(temperature=0.0, max_tokens=8, diffusion_block_size=4,
+                                                   mask_token_id=cfg.mask_token_id, ignore_eos=True),
+                       use_tqdm=False)
+    llm.exit()
+    assert len(out[0]["token_ids"]) >= 8
+
+
+def test_curriculum_yaml_rules(tmp_path):
+    y = tmp_path / "c.yaml"
+    y.write_text("tokens_per_step: 64\nsequence_length: 32\nglobal_batch_size: 2\nseed: 1\n"
+                 "stages:\n  - block_size: 2\n    tokens: 128\n  - block_size: 4\n    tokens: 200\n")
+    plan = BlockCurriculumPlan.from_yaml(y)
+    assert [(s.block_size, s.start_step, s.end_step) for s in plan.stages] == [(2, 0, 2), (4, 2, 5)]
+    assert plan.stage_for_step(1).block_size == 2 and plan.stage_for_step(2).block_size == 4
+    assert plan.checkpoint_reasons == {2: "completed_block_size_2", 5: "completed_block_size_4"}
+    y.write_text("tokens_per_step: 64\nsequence_length: 32\nglobal_batch_size: 2\nseed: 1\n"
+                 "stages:\n  - block_size: 4\n    tokens: 128\n  - block_size: 2\n    tokens: 200\n")
+    with pytest.raises(ValueError, match="increasing"):
+        BlockCurriculumPlan.from_yaml(y)
+
+
+def _dp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg, model, lora = _tiny_setup()
+    plan = BlockCurriculumPlan.fixed([4], 2, 32, 2)
+    tr = UnoTrainer(model, lora, objective=UnoObjectiveConfig(), curriculum=plan, mask_token_id=cfg.mask_token_id,
+                    lr=1e-2, process_group=dist.group.WORLD, seed=3)
+    tr.train_step([_batch(1, 32, seed=rank)])  # different data per rank
+    torch.save({k: v.detach().clone() for k, v in lora.state_dict().items()}, os.path.join(out, f"r{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_data_parallel_ranks_stay_in_sync(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_dp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    a, b = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_training_cli_stops_and_resumes_at_a_stage_boundary(tmp_path, capsys):
+    from uno_b200.train.__main__ import main
+
+    out = str(tmp_path / "run")
+    common = ["--model", "preset:tiny-qwen3", "--output-dir", out, "--device", "cpu", "--block-sizes", "4,8",
+              "--steps-per-stage", "2", "--seq-len", "32", "--global-batch", "2", "--micro-batch", "1",
+              "--lora-rank", "8"]
+    first = main(common + ["--max-steps", "2"])
+    assert [m["step"] for m in first] == [1, 2]
+    assert os.path.isfile(os.path.join(out, "checkpoint-2", "uno_curriculum_state.json"))
+    rest = main(common + ["--resume", os.path.join(out, "checkpoint-2")])
+    assert [m["step"] for m in rest] == [3, 4] and all(m["block_size"] == 8 for m in rest)
+    assert os.path.isfile(os.path.join(out, "final_adapter", "adapter_model.safetensors"))
+    # a different objective does not match the run manifest
+    with pytest.raises(ValueError, match="does not match"):
+        main(common + ["--resume", os.path.join(out, "checkpoint-2"), "--kl-weight", "1.0"])

@@ -1,0 +1,137 @@
+"""Training CLI: ``python -m uno_b200.train --model DIR|preset:NAME --output-dir OUT ...``.
+
+Single process, or one process per GPU under ``torchrun`` (data parallel: the
+frozen base is replicated, LoRA gradients are averaged across ranks).
+Data is synthetic Zipf token ids (``--data synthetic``) or a JSONL file of
+pre-tokenised ``{"input_ids", "labels"}`` rows.  The curriculum comes from a
+YAML file (``--curriculum``) or from ``--block-sizes`` / ``--steps-per-stage``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def build_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--model", required=True)
+    p.add_argument("--output-dir", required=True)
+    p.add_argument("--curriculum")
+    p.add_argument("--block-sizes", default="4,8,16")
+    p.add_argument("--steps-per-stage", type=int, default=1)
+    p.add_argument("--seq-len", type=int, default=128)
+    p.add_argument("--global-batch", type=int, default=2)
+    p.add_argument("--micro-batch", type=int, default=1)
+    p.add_argument("--data", default="synthetic")
+    p.add_argument("--prompt-len", type=int, default=0)
+    p.add_argument("--lr", type=float, default=1e-4)
+    p.add_argument("--warmup-steps", type=int, default=0)
+    p.add_argument("--weight-decay", type=float, default=0.0)
+    p.add_argument("--max-grad-norm", type=float, default=1.0)
+    p.add_argument("--lora-rank", type=int, default=64)
+    p.add_argument("--lora-alpha", type=int, default=None)
+    p.add_argument("--lora-target", default="all")
+    p.add_argument("--tv-weight", type=float, default=1.0)
+    p.add_argument("--kl-weight", type=float, default=0.0)
+    p.add_argument("--ce-weight", type=float, default=0.0)
+    p.add_argument("--ce-target", choices=("teacher", "ground_truth"), default="teacher")
+    p.add_argument("--mask-token-id", type=int)
+    p.add_argument("--device", choices=("cuda", "cpu"), default="cuda")
+    p.add_argument("--checkpoint-layers", action="store_true")
+    p.add_argument("--resume")
+    p.add_argument("--max-steps", type=int, help="stop after this many optimizer steps (default: curriculum end)")
+    p.add_argument("--seed", type=int, default=0)
+    return p
+
+
+def main(argv: list[str] | None = None) -> list[dict]:
+    args = build_parser().parse_args(argv)
+    from uno_b200.models.decoder import build_model
+    from uno_b200.models.presets import resolve_preset
+    from uno_b200.train import BlockCurriculumPlan, LoraSettings, TrainableLoRA, UnoObjectiveConfig, UnoTrainer
+    from uno_b200.train.config import manifest_digest, validate_resume_manifest, write_run_manifest
+    from uno_b200.train.data import batches_from_rows, data_manifest, load_jsonl, pack_rows, synthetic_batches
+    from uno_b200.utils.hf_compat import load_model_config
+    from uno_b200.utils.loader import dummy_init, load_model
+
+    world, rank, group = 1, 0, None
+    if "WORLD_SIZE" in os.environ and int(os.environ["WORLD_SIZE"]) > 1:
+        backend = "nccl" if args.device == "cuda" else "gloo"
+        dist.init_process_group(backend)
+        world, rank, group = dist.get_world_size(), dist.get_rank(), dist.group.WORLD
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))) if args.device == "cuda" else torch.device("cpu")
+    if device.type == "cuda":
+        torch.cuda.set_device(device)
+
+    if args.model.startswith("preset:"):
+        cfg, model_dir = resolve_preset(args.model[len("preset:"):]), None
+    else:
+        model_dir = args.model
+        cfg = load_model_config(model_dir)
+    dtype = torch.float32 if device.type == "cpu" else torch.bfloat16
+    torch.set_default_dtype(dtype)
+    with torch.device(device):
+        model = build_model(cfg)
+    torch.set_default_dtype(torch.float32)
+    if model_dir is None:
+        dummy_init(model, seed=args.seed)
+    else:
+        load_model(model, model_dir)
+    mask_id = args.mask_token_id if args.mask_token_id is not None else cfg.mask_token_id
+    if mask_id is None:
+        raise SystemExit("the model config has no mask_token_id; pass --mask-token-id")
+
+    if args.curriculum:
+        plan = BlockCurriculumPlan.from_yaml(args.curriculum)
+    else:
+        plan = BlockCurriculumPlan.fixed([int(b) for b in args.block_sizes.split(",")], args.steps_per_stage,
+                                         args.seq_len, args.global_batch, args.seed)
+    accumulation = plan.global_batch_size // (world * args.micro_batch)
+    plan.validate_runtime(world_size=world, per_device_batch=args.micro_batch, accumulation=accumulation)
+    settings = LoraSettings(target=args.lora_target, rank=args.lora_rank, alpha=args.lora_alpha)
+    objective = UnoObjectiveConfig(ce_target=args.ce_target, ce_weight=args.ce_weight, kl_weight=args.kl_weight,
+                                   tv_weight=args.tv_weight)
+    lora = TrainableLoRA(cfg, settings, device=device, seed=args.seed)
+    if args.data == "synthetic":
+        batches = synthetic_batches(args.micro_batch, plan.sequence_length, cfg.vocab_size, prompt_len=args.prompt_len,
+                                    seed=args.seed * 7919 + rank)
+        data_info = {"kind": "synthetic-zipf-1.1", "seed": args.seed}
+    else:
+        batches = batches_from_rows(pack_rows(load_jsonl(args.data), plan.sequence_length), args.micro_batch,
+                                    seed=args.seed * 7919 + rank)
+        data_info = data_manifest([args.data])
+    compat = {"model": args.model, "curriculum_sha256": plan.sha256(), "lora": vars(settings) | {"alpha": settings.resolved_alpha},
+              "objective": vars(objective), "mask_token_id": int(mask_id), "data": data_info,
+              "micro_batch": args.micro_batch, "world_size": world}
+    out = args.output_dir
+    os.makedirs(out, exist_ok=True)
+    trainer = UnoTrainer(model, lora, objective=objective, curriculum=plan, mask_token_id=mask_id, lr=args.lr,
+                         warmup_steps=args.warmup_steps, weight_decay=args.weight_decay,
+                         max_grad_norm=args.max_grad_norm, output_dir=out, checkpoint_layers=args.checkpoint_layers,
+                         seed=args.seed, process_group=group, base_model_name=args.model)
+    if args.resume:
+        validate_resume_manifest(out, compat)
+        trainer.resume(args.resume)
+    elif rank == 0:
+        write_run_manifest(out, compat, {"compatibility_sha256_short": manifest_digest(compat)[:12]})
+    last = min(plan.max_steps, args.max_steps or plan.max_steps)
+    history = []
+    while trainer.step < last:
+        metrics = trainer.train_step([next(batches) for _ in range(accumulation)])
+        history.append(metrics)
+        if rank == 0:
+            print(json.dumps(metrics), flush=True)
+    if rank == 0:
+        lora.save(os.path.join(out, "final_adapter"), args.model)
+    if group is not None:
+        dist.destroy_process_group()
+    return history
+
+
+if __name__ == "__main__":
+    main()

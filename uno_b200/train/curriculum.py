@@ -1,0 +1,130 @@
+"""Block-size curriculum: YAML stages -> optimizer-step ranges.
+
+Format and rules of ``training/curriculum.py:21-171``: a YAML mapping with
+``tokens_per_step`` (= ``sequence_length * global_batch_size``), ``seed``,
+optional ``total_tokens`` and ``stages`` (strictly increasing ``block_size``
+with a ``tokens`` budget each).  A stage ends at step
+``floor(cumulative_tokens / tokens_per_step)``; every stage end is a
+checkpoint boundary (``completed_block_size_{B}``); the plan's sha256 (of its
+canonical manifest) pins a resume to the same curriculum.
+"""
+
+from __future__ import annotations
+
+import bisect
+import hashlib
+import json
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Any
+
+
+@dataclass(frozen=True)
+class CurriculumStage:
+    block_size: int
+    token_budget: int
+    start_step: int
+    end_step: int
+
+
+def _int(m: dict[str, Any], key: str, positive: bool = True) -> int:
+    v = m.get(key)
+    if not isinstance(v, int) or isinstance(v, bool):
+        raise ValueError(f"{key} must be an integer.")
+    if positive and v <= 0:
+        raise ValueError(f"{key} must be positive.")
+    return v
+
+
+class BlockCurriculumPlan:
+    def __init__(self, *, tokens_per_step: int, sequence_length: int, global_batch_size: int, seed: int,
+                 stages: list[CurriculumStage], source_path: Path | None = None) -> None:
+        if not stages:
+            raise ValueError("Curriculum stages must be a non-empty list.")
+        self.source_path = source_path
+        self.tokens_per_step = tokens_per_step
+        self.sequence_length = sequence_length
+        self.global_batch_size = global_batch_size
+        self.seed = seed
+        self.stages = tuple(stages)
+        self._ends = tuple(s.end_step for s in stages)
+        self.checkpoint_reasons = {s.end_step: f"completed_block_size_{s.block_size}" for s in stages}
+
+    @classmethod
+    def from_mapping(cls, raw: dict[str, Any], source_path: Path | None = None) -> "BlockCurriculumPlan":
+        if not isinstance(raw, dict):
+            raise ValueError("Curriculum YAML must contain a mapping.")
+        if raw.get("replay") not in (None, {}, False):
+            raise ValueError("Smaller-block replay is not supported.")
+        tps = _int(raw, "tokens_per_step")
+        seq = _int(raw, "sequence_length")
+        gbs = _int(raw, "global_batch_size")
+        seed = _int(raw, "seed", positive=False)
+        if tps != seq * gbs:
+            raise ValueError("tokens_per_step must equal sequence_length * global_batch_size.")
+        items = raw.get("stages")
+        if not isinstance(items, list) or not items:
+            raise ValueError("Curriculum stages must be a non-empty list.")
+        stages, total, prev_end, prev_block = [], 0, 0, 0
+        for i, item in enumerate(items):
+            if not isinstance(item, dict):
+                raise ValueError(f"Curriculum stage {i} must be a mapping.")
+            block = _int(item, "block_size")
+            budget = _int(item, "tokens")
+            if block <= prev_block:
+                raise ValueError("Curriculum block sizes must be strictly increasing.")
+            total += budget
+            end = total // tps
+            if end <= prev_end:
+                raise ValueError(f"Curriculum stage B={block} is shorter than one step.")
+            stages.append(CurriculumStage(block, budget, prev_end, end))
+            prev_end, prev_block = end, block
+        if raw.get("total_tokens") is not None and raw["total_tokens"] != total:
+            raise ValueError("total_tokens does not match the sum of stage token budgets.")
+        return cls(tokens_per_step=tps, sequence_length=seq, global_batch_size=gbs, seed=seed, stages=stages,
+                   source_path=source_path)
+
+    @classmethod
+    def from_yaml(cls, path: str | Path) -> "BlockCurriculumPlan":
+        import yaml
+
+        p = Path(path).expanduser().resolve()
+        if not p.is_file():
+            raise FileNotFoundError(f"Curriculum file not found: {p}")
+        return cls.from_mapping(yaml.safe_load(p.read_text()), p)
+
+    @classmethod
+    def fixed(cls, block_sizes: list[int], steps_per_stage: int, sequence_length: int, global_batch_size: int,
+              seed: int = 0) -> "BlockCurriculumPlan":
+        tps = sequence_length * global_batch_size
+        return cls.from_mapping({"tokens_per_step": tps, "sequence_length": sequence_length,
+                                 "global_batch_size": global_batch_size, "seed": seed,
+                                 "stages": [{"block_size": b, "tokens": steps_per_stage * tps} for b in block_sizes]})
+
+    @property
+    def max_steps(self) -> int:
+        return self.stages[-1].end_step
+
+    @property
+    def total_tokens(self) -> int:
+        return sum(s.token_budget for s in self.stages)
+
+    def stage_for_step(self, step: int) -> CurriculumStage:
+        if not 0 <= step < self.max_steps:
+            raise ValueError(f"Optimizer step {step} is outside [0, {self.max_steps}).")
+        return self.stages[bisect.bisect_right(self._ends, step)]
+
+    def validate_runtime(self, *, world_size: int, per_device_batch: int, accumulation: int) -> None:
+        got = world_size * per_device_batch * accumulation
+        if got != self.global_batch_size:
+            raise ValueError(f"Curriculum global batch mismatch: runtime={got}, expected={self.global_batch_size}.")
+
+    def manifest(self) -> dict[str, Any]:
+        return {"version": 1, "tokens_per_step": self.tokens_per_step, "sequence_length": self.sequence_length,
+                "global_batch_size": self.global_batch_size, "seed": self.seed, "total_tokens": self.total_tokens,
+                "max_steps": self.max_steps, "replay_smaller_blocks": False,
+                "stages": [{"block_size": s.block_size, "token_budget": s.token_budget, "start_step": s.start_step,
+                            "end_step": s.end_step} for s in self.stages]}
+
+    def sha256(self) -> str:
+        return hashlib.sha256(json.dumps(self.manifest(), sort_keys=True, separators=(",", ":")).encode()).hexdigest()

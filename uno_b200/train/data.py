@@ -1,0 +1,93 @@
+"""Training data: synthetic Zipf batches, packed JSONL token rows, manifests.
+
+* :func:`synthetic_batches` -- random token ids drawn Zipf(a) over a fixed
+  permutation of the vocabulary (the benchmark configs' "Zipf(1.1) random token
+  ids"), optionally with an unsupervised prompt prefix;
+* :func:`pack_rows` -- packs pre-tokenised ``{"input_ids", "labels"}`` rows
+  into fixed-length sequences whose positions restart at every packed
+  example, right-padded with IGNORE labels (collation of
+  ``training/data.py:55-118``);
+* :func:`data_manifest` -- sha256 of the data files, pinned in the run
+  manifest (``training/data.py:139-206``).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from pathlib import Path
+from typing import Iterator
+
+import numpy as np
+import torch
+
+from uno_b200.train.config import IGNORE_INDEX
+
+
+def synthetic_batches(batch_size: int, seq_len: int, vocab_size: int, *, zipf_a: float = 1.1,
+                      prompt_len: int = 0, seed: int = 0, low: int = 1) -> Iterator[dict[str, torch.Tensor]]:
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(np.arange(low, vocab_size))
+    while True:
+        ranks = np.minimum(rng.zipf(zipf_a, size=(batch_size, seq_len)) - 1, len(perm) - 1)
+        ids = torch.from_numpy(perm[ranks]).long()
+        labels = ids.clone()
+        if prompt_len:
+            labels[:, :prompt_len] = IGNORE_INDEX
+        yield {"input_ids": ids, "labels": labels,
+               "position_ids": torch.arange(seq_len).expand(batch_size, seq_len).clone()}
+
+
+def pack_rows(rows: list[dict], seq_len: int, pad_id: int = 0) -> list[dict[str, torch.Tensor]]:
+    """Greedy first-fit packing of token rows into ``seq_len`` sequences."""
+    out, cur_ids, cur_lab, cur_pos = [], [], [], []
+
+    def flush():
+        if not cur_ids:
+            return
+        n = len(cur_ids)
+        ids = cur_ids + [pad_id] * (seq_len - n)
+        lab = cur_lab + [IGNORE_INDEX] * (seq_len - n)
+        last = cur_pos[-1] if cur_pos else -1
+        pos = cur_pos + list(range(last + 1, last + 1 + seq_len - n))
+        out.append({"input_ids": torch.tensor(ids), "labels": torch.tensor(lab), "position_ids": torch.tensor(pos)})
+        cur_ids.clear(), cur_lab.clear(), cur_pos.clear()
+
+    for row in rows:
+        ids = list(row["input_ids"])[:seq_len]
+        lab = list(row.get("labels", ids))[:seq_len]
+        if len(ids) != len(lab):
+            raise ValueError("input_ids and labels must have the same length")
+        if len(cur_ids) + len(ids) > seq_len:
+            flush()
+        cur_ids.extend(ids)
+        cur_lab.extend(lab)
+        cur_pos.extend(range(len(ids)))
+    flush()
+    return out
+
+
+def load_jsonl(path: str | Path) -> list[dict]:
+    with open(path, encoding="utf-8") as fh:
+        return [json.loads(line) for line in fh if line.strip()]
+
+
+def batches_from_rows(packed: list[dict[str, torch.Tensor]], batch_size: int, seed: int = 0
+                      ) -> Iterator[dict[str, torch.Tensor]]:
+    g = torch.Generator().manual_seed(seed)
+    while True:
+        order = torch.randperm(len(packed), generator=g).tolist()
+        for i in range(0, len(order) - batch_size + 1, batch_size):
+            items = [packed[j] for j in order[i:i + batch_size]]
+            yield {k: torch.stack([it[k] for it in items]) for k in items[0]}
+
+
+def data_manifest(paths: list[str | Path]) -> dict:
+    files = []
+    for p in sorted(str(x) for x in paths):
+        h = hashlib.sha256()
+        with open(p, "rb") as fh:
+            for chunk in iter(lambda: fh.read(1 << 20), b""):
+                h.update(chunk)
+        files.append({"path": Path(p).name, "sha256": h.hexdigest(), "bytes": Path(p).stat().st_size})
+    return {"version": 1, "files": files}

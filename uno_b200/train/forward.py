@@ -1,0 +1,97 @@
+"""Differentiable forward of the frozen decoder plus trainable gated LoRA.
+
+Runs the same layer math as the inference model (pre-norm residual blocks,
+QKV with optional QK-norm, NeoX RoPE, GQA attention, SiLU-gated MLP, final
+norm) over the concatenated noisy/clean Uno layout with an explicit
+visibility mask, and adds the LoRA branch of every projection on rows whose
+router mask is set.  Base weights are read from the inference model's
+modules (no copy) and receive no gradient; activations of each layer can be
+recomputed in backward (per-layer checkpointing, as the reference
+checkpoints the modules that hold trainable parameters,
+``training/checkpointing.py:12-52``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch.utils.checkpoint import checkpoint
+
+from uno_b200.ops import reference as R
+from uno_b200.train.lora import TrainableLoRA
+
+
+def _proj(x, weight, bias, lora, li, name, mask):
+    """Base projection (frozen) plus the gated LoRA delta of projection ``name``."""
+    y = F.linear(x, weight, bias)
+    if lora is not None and lora.has(li, name):
+        y = y + lora.delta(li, name, x, mask).to(y.dtype)
+    return y
+
+
+def _layer(x, layer, li, lora, mask, positions, cos_sin, attn_mask, cfg):
+    B, T, H = x.shape
+    attn = layer.self_attn
+    hq, hkv, hd = attn.num_heads, attn.num_kv_heads, attn.head_dim
+    ln1 = layer.input_layernorm
+    h = R.rms_norm(x, ln1.weight, ln1.eps, ln1.n_groups)
+    qkv_w, qkv_b = attn.qkv_proj.weight, attn.qkv_proj.bias
+    q_end, k_end = hq * hd, (hq + hkv) * hd
+    qkv = F.linear(h, qkv_w, qkv_b)
+    if lora is not None:
+        parts = []
+        for name, lo, hi in (("q_proj", 0, q_end), ("k_proj", q_end, k_end), ("v_proj", k_end, qkv.shape[-1])):
+            seg = qkv[..., lo:hi]
+            if lora.has(li, name):
+                seg = seg + lora.delta(li, name, h, mask).to(seg.dtype)
+            parts.append(seg)
+        q, k, v = parts
+    else:
+        q, k, v = qkv[..., :q_end], qkv[..., q_end:k_end], qkv[..., k_end:]
+    q = q.reshape(B, T, hq, hd)
+    k = k.reshape(B, T, hkv, hd)
+    v = v.reshape(B, T, hkv, hd)
+    if attn.qk_norm:
+        q = R.head_rms_norm(q, attn.q_norm.weight, attn.eps)
+        k = R.head_rms_norm(k, attn.k_norm.weight, attn.eps)
+    pos = positions.reshape(-1)
+    q = R.apply_rope(q.reshape(B * T, hq, hd), pos, cos_sin).reshape(B, T, hq, hd)
+    k = R.apply_rope(k.reshape(B * T, hkv, hd), pos, cos_sin).reshape(B, T, hkv, hd)
+    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                       attn_mask=attn_mask[:, None], scale=attn.scale, enable_gqa=hq != hkv)
+    o = o.transpose(1, 2).reshape(B, T, hq * hd)
+    o = _proj(o, attn.o_proj.weight, None, lora, li, "o_proj", mask)
+    x = x + o
+    ln2 = layer.post_attention_layernorm
+    h = R.rms_norm(x, ln2.weight, ln2.eps, ln2.n_groups)
+    mlp = layer.mlp
+    inter = mlp.gate_up_proj.weight.shape[0] // 2
+    gu = F.linear(h, mlp.gate_up_proj.weight)
+    if lora is not None:
+        g, u = gu[..., :inter], gu[..., inter:]
+        if lora.has(li, "gate_proj"):
+            g = g + lora.delta(li, "gate_proj", h, mask).to(g.dtype)
+        if lora.has(li, "up_proj"):
+            u = u + lora.delta(li, "up_proj", h, mask).to(u.dtype)
+    else:
+        g, u = gu[..., :inter], gu[..., inter:]
+    a = F.silu(g) * u
+    d = _proj(a, mlp.down_proj.weight, None, lora, li, "down_proj", mask)
+    return x + d
+
+
+def uno_hidden_states(model, lora: TrainableLoRA | None, ids: torch.Tensor, positions: torch.Tensor,
+                      attn_mask: torch.Tensor, lora_rows: torch.Tensor | None,
+                      checkpoint_layers: bool = False) -> torch.Tensor:
+    """Final-norm hidden states ``[B, T, H]`` for the Uno layout."""
+    dec = model.model
+    x = F.embedding(ids, dec.embed_tokens.weight)
+    cos_sin = model.cos_sin_cache
+    for li, layer in enumerate(dec.layers):
+        if checkpoint_layers and torch.is_grad_enabled():
+            x = checkpoint(_layer, x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config,
+                           use_reentrant=False)
+        else:
+            x = _layer(x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config)
+    norm = dec.norm
+    return R.rms_norm(x, norm.weight, norm.eps, norm.n_groups)
