@@ -238,34 +238,65 @@ __global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
     }
     // ---- mask + online softmax
     float mx[2] = {-INFINITY, -INFINITY};
+    // tiles every row sees in full (prefix keys, or causal keys below every row's limit) skip the mask
+    const bool tile_visible = row_valid[0] && row_valid[1] && k0 + ATT_BK <= k_hi &&
+                              (p.mode == MODE_SUFFIX ? k0 + ATT_BK <= prefix
+                                                     : k0 + ATT_BK - 1 <= min(qlimit[0], qlimit[1]));
+    if (__all_sync(0xffffffff, tile_visible)) {
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = e >> 1;
-        const int key = k0 + kofs + n * 8 + tq * 2 + (e & 1);
-        bool vis = row_valid[r] && key < k_hi;
-        if (vis) {
-          if (p.mode == MODE_SUFFIX) {
-            const int j = key - prefix;
-            vis = (j < 0) || ((smask[r] >> j) & 1);
-          } else {
-            vis = key <= qlimit[r];
-          }
+        for (int e = 0; e < 4; ++e) {
+          s[n][e] *= p.scale_log2;
+          mx[e >> 1] = fmaxf(mx[e >> 1], s[n][e]);
         }
-        const float v = vis ? s[n][e] * p.scale_log2 : -INFINITY;
-        s[n][e] = v;
-        mx[r] = fmaxf(mx[r], v);
+    } else {
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = e >> 1;
+          const int key = k0 + kofs + n * 8 + tq * 2 + (e & 1);
+          bool vis = row_valid[r] && key < k_hi;
+          if (vis) {
+            if (p.mode == MODE_SUFFIX) {
+              const int j = key - prefix;
+              vis = (j < 0) || ((smask[r] >> j) & 1);
+            } else {
+              vis = key <= qlimit[r];
+            }
+          }
+          const float v = vis ? s[n][e] * p.scale_log2 : -INFINITY;
+          s[n][e] = v;
+          mx[r] = fmaxf(mx[r], v);
+        }
       }
     }
-    float corr[2];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffff, mx[r], 1));
       mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffff, mx[r], 2));
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      corr[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
-      m_run[r] = m_new;
+    }
+    // Lazy rescale: the running max only moves when a score exceeds it by
+    // more than 2^8 (so exp2 arguments stay <= 8, far inside fp32/bf16
+    // range); after the first tiles the O rescale below is rarely taken.
+    const bool raise = (mx[0] > m_run[0] + 8.f) || (mx[1] > m_run[1] + 8.f);
+    if (__any_sync(0xffffffff, raise)) {
+      float corr[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float m_new = fmaxf(m_run[r], mx[r]);
+        corr[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
+        m_run[r] = m_new;
+        l_run[r] *= corr[r];
+      }
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
     }
     float rs[2] = {0.f, 0.f};
     uint32_t pa[NT / 2][4];  // P as A fragments for the k-steps of 16 keys
@@ -275,7 +306,7 @@ __global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = e >> 1;
-        const float v = (m_run[r] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[r]);
+        const float v = (s[n][e] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[r]);
         e4[e] = v;
         rs[r] += v;
       }
@@ -285,14 +316,7 @@ __global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
       pa[ks][hi * 2 + 1] = pack_bf16x2(e4[2], e4[3]);
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= corr[0];
-      o[n][1] *= corr[0];
-      o[n][2] *= corr[1];
-      o[n][3] *= corr[1];
-    }
+    for (int r = 0; r < 2; ++r) l_run[r] += rs[r];
     // ---- O += P V
 #pragma unroll
     for (int ks = 0; ks < NT / 2; ++ks) {
