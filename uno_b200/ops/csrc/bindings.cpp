@@ -139,9 +139,8 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   }
   DeviceScratch& scratch = device_scratch();
   p.err = scratch.err;
-  int tile = pick_bn(p.M, p.N, (int)bn);
-  if ((epi == 1 || epi == 5) && tile < 128) tile = 128;
-  p.splits = pick_splits(p.M, p.N, p.K + p.K2, tile, (int)splits);
+  int tile = 0;
+  pick_tile(p.M, p.N, p.K + p.K2, (int)epi, (int)bn, (int)splits, &tile, &p.splits);
   const int tiles = ((p.M + 127) / 128) * ((p.N + tile - 1) / tile);
   if (p.splits > 1 &&
       (tiles > scratch.max_counters || (size_t)tiles * p.splits * 128 * tile > scratch.ws_floats))

@@ -139,8 +139,8 @@ __attribute__((visibility("default"))) int uno_gemm_splitk_noalloc(const void* a
     p.C = reinterpret_cast<__nv_bfloat16*>(out);
     p.ldc = ldo;
     p.err = d.err;
-    const int bn = uno::pick_bn(M, N, 0);
-    p.splits = uno::pick_splits(M, N, K, bn, splits);
+    int bn = 0;
+    uno::pick_tile(M, N, K, 0 /* STORE */, 0, splits, &bn, &p.splits);
     if (p.splits > 1) {
       // 128-row tiles, or 256-row CTA pairs counted as two tiles
       const long long m_tiles = std::max((M + 127) / 128, ((M + 255) / 256) * 2);

@@ -869,6 +869,35 @@ int pick_splits(int M, int N, int K, int bn, int forced) {
   return std::max(1, s);
 }
 
+// Tile width and K splits for one GEMM.  A single row of 128-row tiles
+// (M <= 128: small-batch decode, tree verification) is bound by streaming
+// the weights, so it takes narrow tiles -- 64 columns when K <= 4096 and the
+// epilogue allows, else 128 -- and enough K splits for about 128 CTAs.
+void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, int* bn, int* splits) {
+  const bool wide_epi = (epi == EPI_SILU || epi == EPI_QKROPE);  // head / gate-up aligned tiles
+  int tile;
+  if (forced_bn) {
+    tile = forced_bn;
+  } else if (M <= 128 && N > 256) {
+    tile = (!wide_epi && K <= 4096) ? 64 : 128;
+  } else {
+    tile = pick_bn(M, N, 0);
+  }
+  if (wide_epi && tile < 128) tile = 128;
+  int s;
+  if (forced_splits > 0) {
+    s = forced_splits;
+  } else if (!forced_bn && M <= 128 && N > 256) {
+    const int tiles = (N + tile - 1) / tile;
+    const int kb = (K + 63) / 64;
+    s = std::max(1, std::min({4, (128 + tiles / 2) / tiles, kb / 16}));
+  } else {
+    s = pick_splits(M, N, K, tile, 0);
+  }
+  *bn = tile;
+  *splits = s;
+}
+
 template <int EPI>
 static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2, int64_t lda2,
                         const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas) {

@@ -49,6 +49,7 @@ void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, i
                    int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas);
 int pick_bn(int M, int N, int forced);
 int pick_splits(int M, int N, int K, int bn, int forced);
+void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, int* bn, int* splits);
 int num_sms();
 
 // Per-device scratch shared by the GEMM split-K path (fp32 partials and
