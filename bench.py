@@ -269,6 +269,14 @@ def count_launches(llm):
 
 
 def run_reference(args):
+    if args.sampler == "tree":
+        # The reference tree sampler requires attention_backend fa3 or fa4 (its config.py:134-138):
+        # FA3 (flash_attn_interface / sgl_kernel) is Hopper-only and FA4 comes with SGLang; neither
+        # is installed on this image.
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "reference tree sampler needs FA3 "
+                              "(sm90-only) or FA4 via SGLang; neither is installed"}), flush=True)
+        return
     from bench_reference import run  # the reference arm lives beside bench.py
 
     run(args)
