@@ -1,0 +1,206 @@
+"""Evaluation stack on CPU: parsers, graders, protocol guard, runner with resume, pull suite."""
+
+import json
+import multiprocessing as mp
+import os
+import socket
+import threading
+
+import pytest
+
+from uno_b200.eval import benchmarks, graders, parsers
+
+
+def test_registry_and_aliases():
+    assert len(benchmarks.list_benchmarks()) == 13
+    assert benchmarks.get_benchmark("AA-LCR").task == "aa_lcr"
+    assert benchmarks.get_benchmark("gpqa-diamond").temperature == 0.6
+    with pytest.raises(KeyError, match="Unknown benchmark"):
+        benchmarks.get_benchmark("nope")
+
+
+def test_parsers():
+    assert parsers.last_boxed(r"so \boxed{\frac{1}{2}} then \boxed{x^{2}+1}") == "x^{2}+1"
+    assert parsers.last_boxed("no box") is None
+    assert parsers.extract_mc_answer("<think>maybe A</think>The answer is (C).") == "C"
+    assert parsers.extract_mc_answer(r"... \boxed{\text{B}}") == "B"
+    assert parsers.extract_mc_answer("Reasoning...\nD") == "D"
+    code = "text\n```python\ndef f(x):\n    return x + 1\n```\nmore"
+    assert parsers.extract_code(code) == "def f(x):\n    return x + 1"
+    with pytest.raises(ValueError):
+        parsers.parse_generation("nope", "x")
+
+
+@pytest.mark.parametrize("pred,truth,ok", [
+    (r"\frac{1}{2}", "0.5", True), ("1,000", "1000", True), (r"\dfrac{\sqrt{2}}{2}", r"\frac{\sqrt{2}}{2}", True),
+    ("x = 3", "3", True), ("2\\pi", "6.283185307", True), ("7", "8", False), ("", "1", False),
+])
+def test_math_equivalence(pred, truth, ok):
+    assert graders.math_equal(pred, truth) is ok
+
+
+def test_grade_math_and_mc():
+    assert graders.grade_math(r"<think>hmm</think> result \boxed{42}", 42)["correct"]
+    assert graders.grade_multiple_choice("b", "B")["correct"]
+    assert not graders.grade_multiple_choice(None, "B")["correct"]
+
+
+def test_code_sandbox():
+    ok = graders.grade_code("def add(a, b):\n    return a + b", {"test_list": ["assert add(1, 2) == 3"]})
+    bad = graders.grade_code("def add(a, b):\n    return a - b", {"test_list": ["assert add(1, 2) == 3"]})
+    he = graders.grade_code("def inc(x):\n    return x + 1", {"prompt": "", "entry_point": "inc",
+                                                            "test": "def check(f):\n    assert f(1) == 2"})
+    slow = graders.run_code_sandboxed("while True:\n    pass\n", timeout=1.0)
+    env = graders.run_code_sandboxed("import os, sys\nsys.exit(0 if 'HF_TOKEN' not in os.environ else 1)\n")
+    assert ok["correct"] and not bad["correct"] and he["correct"]
+    assert slow["status"] == "timeout" and env["passed"]
+
+
+def test_llm_judge_with_fake_transport():
+    seen = {}
+
+    def transport(payload):
+        seen.update(payload)
+        return "CORRECT"
+
+    res = graders.grade_with_judge("q?", "a", "<think>x</think>final", model="judge-1", transport=transport)
+    assert res["correct"] and seen["model"] == "judge-1" and "final" in seen["messages"][0]["content"]
+
+
+# ------------------------------------------------------------- runner
+def _chat_model_dir(tmp_path):
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    from uno_b200.utils.hf_compat import model_config_from_dict, save_model_config
+
+    words = ["<unk>", "<eos>", "system", "user", "assistant", ":", "what", "is", "two", "plus", "three", "\n"]
+    words += [f"w{i}" for i in range(100)]
+    tok = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    fast = PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="<unk>", eos_token="<eos>")
+    fast.chat_template = ("{% for m in messages %}{{ m['role'] }} : {{ m['content'] }} {% endfor %}"
+                          "{% if add_generation_prompt %}assistant : {% endif %}")
+    d = tmp_path / "model"
+    fast.save_pretrained(str(d))
+    save_model_config(model_config_from_dict(dict(
+        model_type="qwen3", vocab_size=4096, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=32, eos_token_id=1, mask_token_id=4095,
+        torch_dtype="float32")), str(d))
+    return d
+
+
+def _dataset(tmp_path):
+    p = tmp_path / "toy.jsonl"
+    rows = [{"id": "q1", "chat_input": [{"role": "user", "content": "what is two plus three"}], "answer": "5"},
+            {"id": "q2", "chat_input": [{"role": "user", "content": "what is two"}], "answer": "2"}]
+    p.write_text("".join(json.dumps(r) + "\n" for r in rows))
+    return p
+
+
+def test_eval_runner_generates_resumes_and_scores(tmp_path):
+    from uno_b200.eval.run import main
+
+    model = _chat_model_dir(tmp_path)
+    data = _dataset(tmp_path)
+    out = tmp_path / "toy-generations.jsonl"
+    common = ["--model", str(model), "--data", str(data), "--output", str(out), "--device", "cpu",
+              "--load-format", "dummy", "--num-samples", "2", "--max-tokens", "12", "--max-model-len", "128",
+              "--diffusion-block-size", "4", "--temperature", "1.0", "--seed", "0"]
+    s1 = main(common)
+    rows = [json.loads(x) for x in out.read_text().splitlines()]
+    assert s1["generated"] == 4 and len(rows) == 4
+    assert [(r["id"], r["sample"]) for r in rows] == [("q1", 0), ("q1", 1), ("q2", 0), ("q2", 1)]
+    assert s1["decoder_tokens_per_sequence_forward"] > 0 and s1["scores"]["rows"] == 4
+    assert (tmp_path / "scores.json").is_file() and (tmp_path / "grades.jsonl").is_file()
+    s2 = main(common)  # resume: nothing left to generate
+    assert s2["generated"] == 0 and s2["resumed"] == 4 and len(out.read_text().splitlines()) == 4
+
+
+def test_protocol_overrides_need_an_arm(tmp_path):
+    from uno_b200.eval.run import main
+
+    model = _chat_model_dir(tmp_path)
+    data = _dataset(tmp_path)
+    args = ["--benchmark", "math500", "--model", str(model), "--data", str(data), "--device", "cpu",
+            "--load-format", "dummy", "--output", str(tmp_path / "m.jsonl"), "--no-grade"]
+    with pytest.raises(ValueError, match="protocol-arm"):
+        main(args)  # the toy file is not the pinned math500 artifact
+    s = main(args + ["--protocol-arm", "toy", "--skip-row-count-check", "--max-tokens", "4",
+                     "--max-model-len", "128", "--diffusion-block-size", "4"])
+    assert set(s["overrides"]) >= {"data", "max_tokens", "max_model_len"} and s["protocol_arm"] == "toy"
+
+
+# ---------------------------------------------------------- pull suite
+def _fake_generate(jobs):
+    return [f"gen {j['id']} {j['sample']}" for j in jobs]
+
+
+def _worker(port, manifest, box):
+    from uno_b200.eval.pull_suite import run_worker
+
+    try:
+        box.put(("ok", run_worker(("127.0.0.1", port), b"k", manifest, _fake_generate, batch=3,
+                                  connect_deadline=30)))
+    except Exception as exc:  # report to the parent
+        box.put(("err", repr(exc)))
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_pull_suite_distributes_resumes_and_guards_manifest(tmp_path):
+    from uno_b200.eval.pull_suite import completed_keys, run_coordinator
+
+    ctx = mp.get_context("fork")
+    manifest = {"model": "toy", "protocol": "p1"}
+    jobs = [{"benchmark": "toy", "id": f"q{i}", "sample": s, "ground_truth": str(i)} for i in range(7) for s in (0, 1)]
+    results = tmp_path / "results.jsonl"
+    # two jobs finished in an earlier, interrupted run
+    results.write_text("".join(json.dumps({**jobs[k], "generation": "old"}) + "\n" for k in (0, 5)))
+    port = _port()
+    box = ctx.Queue()
+    summary = {}
+
+    def coord():
+        summary.update(run_coordinator(jobs, results, manifest, ("127.0.0.1", port), b"k", num_workers=2,
+                                       timeout=60))
+
+    t = threading.Thread(target=coord)
+    t.start()
+    workers = [ctx.Process(target=_worker, args=(port, manifest, box)) for _ in range(2)]
+    for w in workers:
+        w.start()
+    for w in workers:
+        w.join(60)
+    t.join(60)
+    outcomes = [box.get(timeout=5) for _ in workers]
+    assert all(o[0] == "ok" for o in outcomes), outcomes
+    assert summary["resumed"] == 2 and summary["completed"] == 12
+    assert sum(o[1] for o in outcomes) == 12
+    lines = [json.loads(x) for x in results.read_text().splitlines()]
+    assert len(lines) == 14 and len(completed_keys(results)) == 14
+
+    # a worker with a different manifest is refused
+    port2 = _port()
+    seen = {}
+
+    def coord2():
+        try:
+            run_coordinator(jobs[:1], tmp_path / "r2.jsonl", manifest, ("127.0.0.1", port2), b"k", num_workers=1,
+                            timeout=8)
+        except TimeoutError as exc:  # its only worker was refused, so the job never finishes
+            seen["timeout"] = str(exc)
+
+    t2 = threading.Thread(target=coord2)
+    t2.start()
+    bad = ctx.Process(target=_worker, args=(port2, {"model": "other"}, box))
+    bad.start()
+    bad.join(30)
+    kind, msg = box.get(timeout=5)
+    assert kind == "err" and "manifest mismatch" in msg
+    t2.join(30)
+    assert "1 jobs unfinished" in seen.get("timeout", "")

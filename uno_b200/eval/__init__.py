@@ -1,1 +1,1 @@
-
+"""Evaluation: protocol registry, runner with resume, parsers, graders, scoring, pull suite."""

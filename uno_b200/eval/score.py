@@ -1,0 +1,84 @@
+"""Grade a generations file and score it (``evaluation/score_generations.py``).
+
+Routing by task: multiple-choice parsers grade letters; ``humaneval`` /
+``mbpp`` (and any ``code_completion`` parser) run the sandboxed code grader;
+benchmarks with a judge use the LLM judge when a transport is given (else the
+rows are reported as ungraded); ``ifeval`` is reported as unsupported;
+everything else is graded as math (boxed answer equivalence).  Scores are
+the mean correctness over all samples, the per-question mean, and the
+generation throughput (TPS, TPF) copied from the generation summary.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+from typing import Any, Callable
+
+from uno_b200.eval.benchmarks import get_benchmark
+from uno_b200.eval.data import first_field, read_jsonl, ID_FIELDS
+from uno_b200.eval.graders import grade_code, grade_math, grade_multiple_choice, grade_with_judge
+from uno_b200.eval.parsers import parse_generation
+
+
+def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: Callable | None = None,
+              judge_model: str | None = None, timeout: float = 10.0) -> dict[str, Any]:
+    gen = row.get("generation", "")
+    truth = row.get("ground_truth")
+    if task == "ifeval":
+        return {"correct": None, "status": "unsupported grader"}
+    if parser == "mc_answer":
+        return grade_multiple_choice(parse_generation("mc_answer", gen), truth)
+    if parser == "code_completion" or task in ("humaneval", "mbpp"):
+        if record is None:
+            return {"correct": None, "status": "missing source record"}
+        return grade_code(parse_generation("code_completion", gen), record, timeout)
+    if judge_model is not None:
+        if judge is None:
+            return {"correct": None, "status": "ungraded: no judge endpoint"}
+        question = row.get("question") or (record or {}).get("question", "")
+        return grade_with_judge(question, truth, gen, model=judge_model, transport=judge)
+    return grade_math(gen, truth)
+
+
+def score_file(generations: str | Path, *, benchmark: str | None = None, data: str | Path | None = None,
+               parser: str | None = None, grades_out: str | Path | None = None,
+               scores_out: str | Path | None = None, summary: str | Path | None = None,
+               judge: Callable | None = None) -> dict[str, Any]:
+    rows = read_jsonl(generations)
+    bench = get_benchmark(benchmark) if benchmark else None
+    task = bench.task if bench else "math"
+    parser = parser or (bench.parser if bench else "passthrough")
+    records = {}
+    if data is not None:
+        for i, rec in enumerate(read_jsonl(data)):
+            rid = first_field(rec, ID_FIELDS)
+            records[str(rid if rid is not None else i)] = rec
+    grades = []
+    for row in rows:
+        g = grade_row(row, records.get(str(row.get("id"))), task=task, parser=parser, judge=judge,
+                      judge_model=bench.judge if bench else None, timeout=bench.grader_timeout if bench else 10.0)
+        grades.append({"id": row.get("id"), "sample": row.get("sample"), **g})
+    graded = [g for g in grades if g["correct"] is not None]
+    per_q: dict[str, list[bool]] = {}
+    for g in graded:
+        per_q.setdefault(str(g["id"]), []).append(bool(g["correct"]))
+    scores: dict[str, Any] = {
+        "benchmark": bench.name if bench else None,
+        "rows": len(rows),
+        "graded": len(graded),
+        "accuracy": sum(bool(g["correct"]) for g in graded) / len(graded) if graded else None,
+        "question_accuracy": (sum(sum(v) / len(v) for v in per_q.values()) / len(per_q)) if per_q else None,
+    }
+    if summary is not None and Path(summary).is_file():
+        s = json.loads(Path(summary).read_text())
+        for key in ("output_tokens_per_second", "decoder_tokens_per_sequence_forward", "total_output_tokens"):
+            if key in s:
+                scores[key] = s[key]
+    if grades_out is not None:
+        with open(grades_out, "w", encoding="utf-8") as fh:
+            for g in grades:
+                fh.write(json.dumps(g) + "\n")
+    if scores_out is not None:
+        Path(scores_out).write_text(json.dumps(scores, indent=2) + "\n")
+    return scores
