@@ -875,22 +875,34 @@ int pick_splits(int M, int N, int K, int bn, int forced) {
 // epilogue allows, else 128 -- and enough K splits for about 128 CTAs.
 void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, int* bn, int* splits) {
   const bool wide_epi = (epi == EPI_SILU || epi == EPI_QKROPE);  // head / gate-up aligned tiles
+  // More rows: 128x128 single-SM tiles without a K split while they fit in
+  // one wave of SMs (the partial-sum reduction costs more than it saves
+  // there); K splits only when those tiles are few; CTA pairs with 256x256
+  // tiles for the large GEMMs.
+  const int sms = num_sms();
+  const int t128 = ((M + 127) / 128) * ((N + 127) / 128);
+  const bool narrow_rows = M <= 128 && N > 256;
+  const bool mid = M > 128 && N > 256 && t128 <= sms;
   int tile;
   if (forced_bn) {
     tile = forced_bn;
-  } else if (M <= 128 && N > 256) {
+  } else if (narrow_rows) {
     tile = (!wide_epi && K <= 4096) ? 64 : 128;
+  } else if (mid) {
+    tile = 128;
   } else {
     tile = pick_bn(M, N, 0);
   }
   if (wide_epi && tile < 128) tile = 128;
   int s;
+  const int kb = (K + 63) / 64;
   if (forced_splits > 0) {
     s = forced_splits;
-  } else if (!forced_bn && M <= 128 && N > 256) {
+  } else if (!forced_bn && narrow_rows) {
     const int tiles = (N + tile - 1) / tile;
-    const int kb = (K + 63) / 64;
     s = std::max(1, std::min({4, (128 + tiles / 2) / tiles, kb / 16}));
+  } else if (!forced_bn && mid) {
+    s = t128 * 2 >= sms ? 1 : std::max(1, std::min({4, (128 + t128 / 2) / t128, kb / 16}));
   } else {
     s = pick_splits(M, N, K, tile, 0);
   }

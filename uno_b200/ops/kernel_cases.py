@@ -7,7 +7,7 @@ launches of the case, then one launch inside the NVTX range ``capture`` (for
 host launch cost excluded) and prints one JSON line per kernel.  Inputs are random; the
 decode-attention KV cache (~240 MB) is larger than the L2.
 
-Cases: ``layer-gemms`` (gate_up + SiLU, o_proj, LoRA hidden), ``decode-attention``.
+Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden), ``decode-attention``.
 """
 
 from __future__ import annotations
@@ -27,13 +27,20 @@ def _layer_gemms():
     act = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
     w_o = torch.randn(H, H, device="cuda").bfloat16() * 0.02
     y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    w_qkv = torch.randn(6144, H, device="cuda").bfloat16() * 0.02
+    qkv = torch.empty(M, 6144, device="cuda", dtype=torch.bfloat16)
+    a_i = torch.randn(M, I, device="cuda").bfloat16()
+    w_d = torch.randn(H, I, device="cuda").bfloat16() * 0.02
     a_l = torch.randn(192, H, device="cuda").bfloat16() * 0.02
     h_l = torch.empty(M, 192, device="cuda", dtype=torch.bfloat16)
     mask = torch.ones(M, device="cuda")
     return {
         "gate_up_silu 512x24576x4096": (lambda: C._gemm(x, w_gu, C.EPI_SILU, c=act), 2 * M * 2 * I * H,
                                         2 * I * H * 2),
+        "qkv (plain store) 512x6144x4096": (lambda: C._gemm(x, w_qkv, C.EPI_STORE, c=qkv), 2 * M * 6144 * H,
+                                            6144 * H * 2),
         "o_proj 512x4096x4096": (lambda: C._gemm(x, w_o, C.EPI_STORE, c=y), 2 * M * H * H, H * H * 2),
+        "down 512x4096x12288": (lambda: C._gemm(a_i, w_d, C.EPI_STORE, c=y), 2 * M * H * I, H * I * 2),
         "lora_hidden 512x192x4096": (lambda: C._gemm(x, a_l, C.EPI_ROWSCALE, c=h_l, scale=2.0, row_mask=mask),
                                      2 * M * 192 * H, (M + 192) * H * 2),
     }
