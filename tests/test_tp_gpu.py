@@ -38,9 +38,15 @@ def test_fused_tp_matches_nccl_and_single_gpu(world):
     nccl = _run(world, "nccl")
     fused = _run(world, "fused")
     fused_eager = _run(world, "fused", eager=True)
-    assert fused["err"] == 0 and nccl["err"] == 0
-    for res in (nccl, fused, fused_eager):
-        for a, b in zip(one["greedy"], res["greedy"]):
-            assert a[:4] == b[:4]  # greedy prefix agrees (bf16 reduction order may flip late near-ties)
+    assert fused["err"] == 0 and nccl["err"] == 0 and fused_eager["err"] == 0
+    ref = torch.tensor(one["logits"])
+    scale = ref.abs().max().item()
+    for name, res in (("nccl", nccl), ("fused", fused), ("fused_eager", fused_eager)):
+        got = torch.tensor(res["logits"])
+        err = (got - ref).abs().max().item()
+        # bf16 activations with a different reduction order: a few bf16 ulps of the logit range
+        assert err <= 0.03 * scale, f"{name}: prefill logits differ by {err:.4f} (range {scale:.3f})"
         assert all(len(t) >= 24 for t in res["sampled"])
+    # greedy tokens across TP degrees may flip on bf16 near-ties of a random-init model; the same
+    # TP degree with and without CUDA graphs runs the same kernels and must agree exactly
     assert fused["greedy"] == fused_eager["greedy"]  # graphs replay the same kernels

@@ -33,13 +33,19 @@ def main():
         return
     llm = LLM(cfg, **kw)
     prompts = [list(range(1, 70)), list(range(200, 230)), [5, 6, 7]]
+    # one prefill over 300 rows: several GEMM row tiles, every rank owns rows
+    long = [[(7 * i + 3 * j) % 3900 + 1 for j in range(100)] for i in range(3)]
+    llm.generate(long, SamplingParams(temperature=0.0, max_tokens=1, diffusion_block_size=4, mask_token_id=4000,
+                                      ignore_eos=True), use_tqdm=False)
+    logits = llm.model_runner.last_prefill_logits.float().cpu()
     greedy = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=12, diffusion_block_size=4,
                                                   mask_token_id=4000, ignore_eos=True), use_tqdm=False)
     sampled = llm.generate(prompts, SamplingParams(temperature=1.0, max_tokens=24, diffusion_block_size=4,
                                                    mask_token_id=4000, ignore_eos=True, seed=3), use_tqdm=False)
     from uno_b200.ops import cuda
 
-    print(json.dumps({"greedy": [o["token_ids"] for o in greedy], "sampled": [o["token_ids"] for o in sampled],
+    print(json.dumps({"logits": logits.tolist(), "greedy": [o["token_ids"] for o in greedy],
+                      "sampled": [o["token_ids"] for o in sampled],
                       "stats": llm.last_generate_stats, "err": cuda.error_flag()}), flush=True)
     llm.exit()
 

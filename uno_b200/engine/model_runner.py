@@ -204,6 +204,7 @@ class ModelRunner:
         input_ids = torch.tensor(ids, dtype=torch.int64, device=dev)
         hidden = self.model(input_ids, meta)
         logits = self._logits_full(self.model.compute_logits(hidden, meta))
+        self.last_prefill_logits = logits  # last-position logits of the latest prefill (diagnostics)
         tokens, _ = self.sampler.sample(logits, sp)
         out = tokens.tolist()
         for seq, t in zip(seqs, out):

@@ -30,15 +30,19 @@ class RMSNorm(nn.Module):
         self.eps = float(eps)
         self.n_groups = int(n_groups)
         self.weight = nn.Parameter(torch.ones(hidden_size), requires_grad=False)
+        # the model's last norm: its rows leave the fused tensor-parallel path
+        self.final = False
 
     def forward(self, x, residual=None):
         if residual is None:
+            if self.final:
+                return ops.rms_norm_first(x, self.weight, self.eps, self.n_groups, final=True)[0]
             return ops.rms_norm(x, self.weight, self.eps, self.n_groups)
-        return ops.add_rms_norm(x, residual, self.weight, self.eps, self.n_groups)
+        return ops.add_rms_norm(x, residual, self.weight, self.eps, self.n_groups, final=self.final)
 
     def first(self, x):
         """Normalise the start of the residual stream: returns (normed, residual)."""
-        return ops.rms_norm_first(x, self.weight, self.eps, self.n_groups)
+        return ops.rms_norm_first(x, self.weight, self.eps, self.n_groups, final=self.final)
 
 
 class VocabParallelEmbedding(nn.Module):
@@ -143,6 +147,7 @@ class DecoderModel(nn.Module):
         self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size)
         self.layers = nn.ModuleList([DecoderLayer(cfg) for _ in range(cfg.num_hidden_layers)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, int(cfg.layernorm_num_groups or 1))
+        self.norm.final = True
 
     def forward(self, input_ids, meta, cos_sin):
         x = self.embed_tokens(input_ids)

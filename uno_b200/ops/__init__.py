@@ -24,16 +24,17 @@ def rms_norm(x, weight, eps, n_groups=1):
     return ref.rms_norm(x, weight, eps, n_groups)
 
 
-def rms_norm_first(x, weight, eps, n_groups=1):
+def rms_norm_first(x, weight, eps, n_groups=1, final=False):
     """Norm that starts the residual stream: returns (normed, residual)."""
     if not isinstance(x, torch.Tensor) or x.is_cuda:
-        return _cuda().rms_norm_first(x, weight, eps, n_groups)
+        return _cuda().rms_norm_first(x, weight, eps, n_groups, final)
     return ref.rms_norm(x, weight, eps, n_groups), x
 
 
-def add_rms_norm(x, residual, weight, eps, n_groups=1):
+def add_rms_norm(x, residual, weight, eps, n_groups=1, final=False):
+    """``final``: last norm of a forward (completes the fused tensor-parallel gather)."""
     if not isinstance(x, torch.Tensor) or x.is_cuda:
-        return _cuda().add_rms_norm(x, residual, weight, eps, n_groups)
+        return _cuda().add_rms_norm(x, residual, weight, eps, n_groups, final)
     return ref.add_rms_norm(x, residual, weight, eps, n_groups)
 
 

@@ -25,7 +25,7 @@ void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at:
                        at::Tensor& par, at::Tensor& dep, at::Tensor& mass, at::Tensor& count);
 void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t H,
                                int64_t recv_off, int64_t gather_off, at::Tensor& residual, bool add_residual,
-                               const at::Tensor& weight, int64_t groups, double eps);
+                               const at::Tensor& weight, int64_t groups, double eps, bool wait_all);
 void embedding_scatter_launch(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& ids,
                               const at::Tensor& table, int64_t start, int64_t recv_off, int64_t gather_off);
 std::vector<int64_t> symm_alloc(int64_t nbytes);
@@ -79,7 +79,7 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
                  c10::optional<at::Tensor> cos_sin, c10::optional<at::Tensor> q_norm_w,
                  c10::optional<at::Tensor> k_norm_w, double eps, int64_t hq, int64_t hkv, int64_t page,
                  int64_t max_ctas, int64_t splits, std::vector<int64_t> rs_peers, int64_t rs_rank,
-                 int64_t rs_recv_off) {
+                 int64_t rs_recv_off, int64_t ag_base, int64_t ag_R) {
   check_dev(a, "gemm A");
   check_dev(b, "gemm B");
   UNO_CHECK_BF16(a);
@@ -136,6 +136,11 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
     TORCH_CHECK((p.N * 2) % 16 == 0, "row width must be 16-byte aligned");
   } else if (epi != 5) {
     TORCH_CHECK(p.C != nullptr, "output tensor missing");
+  }
+  if (ag_base) {
+    TORCH_CHECK(ag_R > 0, "all-gathered operand needs rows per rank");
+    p.ag_base = reinterpret_cast<const uint8_t*>(ag_base);
+    p.ag_R = (int)ag_R;
   }
   DeviceScratch& scratch = device_scratch();
   p.err = scratch.err;

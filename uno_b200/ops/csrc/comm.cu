@@ -45,6 +45,9 @@ struct CommCtl {
   unsigned long long done[MAX_TP];
 };
 
+static_assert(offsetof(CommCtl, epoch) == COMM_EPOCH_OFF && offsetof(CommCtl, done) == COMM_DONE_OFF,
+              "control block layout shared with the GEMM");
+
 struct RsParams {
   uint8_t* peers[MAX_TP];       // base of every rank's workspace (own included)
   int tp, rank;
@@ -55,6 +58,7 @@ struct RsParams {
   const __nv_bfloat16* weight;  // RMSNorm weight [H]
   int groups;
   float eps;
+  int wait_all;                 // 1: return only after every rank's rows have arrived
   int* err;
 };
 
@@ -216,8 +220,14 @@ __global__ void __launch_bounds__(512) reduce_norm_gather_kernel(RsParams p) {
         CommCtl* peer = reinterpret_cast<CommCtl*>(p.peers[j]);
         st_release_sys(&peer->done[p.rank], 2 * epoch + 2);
       }
-      wait_flags(ctl->done, p.tp, 2 * epoch + 2, p.err);
-      asm volatile("fence.proxy.async.global;" ::: "memory");
+      // Normally no wait here: the GEMM that reads the gathered rows waits for
+      // exactly their owners' done flags (wait_row_owners), tile by tile.  The
+      // last norm of a forward waits for all of them, since its rows leave the
+      // fused path (row selection, host reads, the next forward's scatter).
+      if (p.wait_all) {
+        wait_flags(ctl->done, p.tp, 2 * epoch + 2, p.err);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
       ctl->epoch = epoch + 1;
       __threadfence();
     }
@@ -260,7 +270,7 @@ static RsParams make_params(const std::vector<int64_t>& peers, int64_t rank, int
 
 void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t H,
                                int64_t recv_off, int64_t gather_off, at::Tensor& residual, bool add_residual,
-                               const at::Tensor& weight, int64_t groups, double eps) {
+                               const at::Tensor& weight, int64_t groups, double eps, bool wait_all) {
   check_dev(residual, "residual shard");
   check_dev(weight, "norm weight");
   RsParams p = make_params(peers, rank, T, H, recv_off, gather_off);
@@ -273,6 +283,7 @@ void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, 
   p.weight = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
   p.groups = (int)groups;
   p.eps = (float)eps;
+  p.wait_all = wait_all ? 1 : 0;
   const int rows = std::max(1, p.R);
   const int grid = std::min(rows, 4 * num_sms());
   const int threads = std::max(64, ((int)(H / 8) + 31) / 32 * 32);

@@ -84,6 +84,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// System-scope acquire load (flags written by peer GPUs over NVLink).
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until every rank owning a row of [r0, r1) has published flag value
+// >= target in done[]; then make the peers' generic-proxy stores visible to
+// this thread's TMA (async-proxy) loads.  Bounded: sets error code 3.
+__device__ __forceinline__ bool wait_row_owners(const unsigned long long* done, int r0, int r1, int rows_per_rank,
+                                                unsigned long long target, int* err) {
+  uint64_t start = 0;
+  for (int j = r0 / rows_per_rank; j <= (r1 - 1) / rows_per_rank; ++j) {
+    while (ld_acquire_sys_u64(done + j) < target) {
+      if (start == 0) start = globaltimer_ns();
+      if (globaltimer_ns() - start > 5000000000ull) {
+        set_error(err, 3);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 // ---------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {

@@ -365,10 +365,18 @@ __global__ void __launch_bounds__(192, 1)
       bool issued[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      const unsigned long long ag_target =
+          p.ag_base ? 2ull * *reinterpret_cast<const volatile unsigned long long*>(p.ag_base + COMM_EPOCH_OFF) : 0;
       for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
         const int tile = u % num_tiles, ks = u / num_tiles;
         const int m_blk = tile % p.num_m, n_blk = tile / p.num_m;
         const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
+        if (p.ag_base && !wait_row_owners(reinterpret_cast<const unsigned long long*>(p.ag_base + COMM_DONE_OFF),
+                                          m_blk * Cfg::BM, min(p.M, (m_blk + 1) * Cfg::BM), p.ag_R, ag_target,
+                                          p.err)) {
+          *abort_flag = 1;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
             *abort_flag = 1;
@@ -594,12 +602,20 @@ __global__ void __launch_bounds__(192, 1)
       bool issued[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      const unsigned long long ag_target =
+          p.ag_base ? 2ull * *reinterpret_cast<const volatile unsigned long long*>(p.ag_base + COMM_EPOCH_OFF) : 0;
       for (int u = cid; u < num_units && !*abort_flag; u += ncl) {
         const int tile = u % num_tiles, ks = u / num_tiles;
         const int m2 = tile % num_m2, n_blk = tile / num_m2;
         const int kb0 = ks * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
         const int arow = m2 * 256 + (int)rank * 128;
         const int brow = n_blk * BN + (int)rank * 128;
+        if (p.ag_base && arow < p.M &&
+            !wait_row_owners(reinterpret_cast<const unsigned long long*>(p.ag_base + COMM_DONE_OFF), arow,
+                             min(p.M, arow + 128), p.ag_R, ag_target, p.err)) {
+          *abort_flag = 1;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
             *abort_flag = 1;

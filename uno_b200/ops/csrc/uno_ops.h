@@ -44,6 +44,11 @@ struct GemmParams {
   // rs_rank, at byte offset rs_recv_off of that rank's symmetric workspace
   uint8_t* rs_peers[8];
   int rs_enable, rs_rank, rs_R, rs_recv_off;
+  // all-gathered A operand (fused TP collectives): before loading the A rows
+  // of a tile, wait until their owner ranks (row / ag_R) have published
+  // "done" for the current epoch in this rank's workspace control block
+  const uint8_t* ag_base;
+  int ag_R;
 };
 void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,
                    int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas);
@@ -85,6 +90,11 @@ struct AttnLaunch {
   int* err;
 };
 void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream);
+
+// Control block at the start of every rank's symmetric workspace (comm.cu):
+// u64 epoch, u32 CTA counter, u32 pad, u64 arrive[8], u64 done[8].
+constexpr int COMM_EPOCH_OFF = 0;
+constexpr int COMM_DONE_OFF = 80;
 
 // Device error word (allocated once per device by the bindings).
 inline int* device_error_flag() { return device_scratch().err; }

@@ -67,8 +67,9 @@ def _gemm(a, b, epi, *, c=None, r=None, a2=None, b2=None, scale=0.0, row_mask=No
           k_cache=None, v_cache=None, slots=None, positions=None, cos_sin=None, q_norm_w=None,
           k_norm_w=None, eps=0.0, hq=0, hkv=0, page=0, bn=0, max_ctas=0, splits=0, rs=None):
     peers, rank, off = ([], 0, 0) if rs is None else rs
+    ag_base, ag_rows = _COMM.gather_wait_args(a) if _COMM is not None else (0, 0)
     ext().gemm(a, b, epi, bn, c, r, a2, b2, scale, row_mask, q_out, k_cache, v_cache, slots, positions,
-               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas, splits, peers, rank, off)
+               cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, page, max_ctas, splits, peers, rank, off, ag_base, ag_rows)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, bn: int = 0, splits: int = 0) -> torch.Tensor:
@@ -136,17 +137,21 @@ def rms_norm(x, weight, eps, n_groups=1):
     return y.view(x.shape)
 
 
-def rms_norm_first(x, weight, eps, n_groups=1):
+def rms_norm_first(x, weight, eps, n_groups=1, final=False):
     """First norm of the residual stream: returns (normed, residual)."""
     if isinstance(x, PendingRS):
-        return _COMM.reduce_norm(x.T, None, weight, eps, n_groups)
+        return _COMM.reduce_norm(x.T, None, weight, eps, n_groups, final)
     return rms_norm(x, weight, eps, n_groups), x
 
 
-def add_rms_norm(x, residual, weight, eps, n_groups=1):
-    """Returns (normed, new_residual); the residual buffer is updated in place."""
+def add_rms_norm(x, residual, weight, eps, n_groups=1, final=False):
+    """Returns (normed, new_residual); the residual buffer is updated in place.
+
+    ``final`` marks the last norm of a forward (its output leaves the fused
+    tensor-parallel path, so the gather completes before the kernel returns).
+    """
     if isinstance(x, PendingRS):
-        return _COMM.reduce_norm(x.T, residual, weight, eps, n_groups)
+        return _COMM.reduce_norm(x.T, residual, weight, eps, n_groups, final)
     x2 = _rows(x)
     y = torch.empty(x2.shape, device=x.device, dtype=x.dtype)
     res = residual if residual.is_contiguous() else residual.contiguous()

@@ -74,10 +74,25 @@ class FusedTPComm:
             raise ValueError(f"{T} tokens exceed the fused TP workspace ({self.max_tokens})")
         return (self.peers, self.rank, self.recv_off)
 
-    def reduce_norm(self, T: int, residual: torch.Tensor | None, weight, eps: float, groups: int):
+    def gather_wait_args(self, a: torch.Tensor) -> tuple[int, int]:
+        """``(workspace base, rows per rank)`` when ``a`` lives in the gathered buffer, else ``(0, 0)``.
+
+        A GEMM reading gathered rows waits, per tile, for the ranks that own
+        them to finish broadcasting (the reduce kernel itself does not wait)."""
+        ptr = a.data_ptr()
+        lo = self.ptr + self.gather_off
+        if lo <= ptr < lo + self.gather.numel() * 2:
+            return self.ptr, self.rows_per_rank(a.shape[0])
+        return 0, 0
+
+    def reduce_norm(self, T: int, residual: torch.Tensor | None, weight, eps: float, groups: int,
+                    final: bool = False):
         """Sum partials of owned rows (+ residual), RMSNorm, broadcast rows.
 
-        Returns ``(gathered normed rows [T, H], residual shard [R, H])``.
+        Returns ``(gathered normed rows [T, H], residual shard [R, H])``.  The
+        kernel returns before the peers' rows have landed; GEMMs reading the
+        gathered rows wait for their owners tile by tile.  ``final`` (the last
+        norm of a forward, whose rows leave the fused path) waits for all rows.
         """
         from uno_b200.ops.cuda import ext
 
@@ -85,7 +100,7 @@ class FusedTPComm:
         if residual is None:
             residual = torch.empty(self.rows_per_rank(T), self.hidden, device=self.device, dtype=torch.bfloat16)
         ext().reduce_norm_gather(self.peers, self.rank, int(T), self.hidden, self.recv_off, self.gather_off,
-                                 residual, add, weight, int(groups), float(eps))
+                                 residual, add, weight, int(groups), float(eps), bool(final))
         return self.gather[:T], residual
 
     def embedding_scatter(self, ids: torch.Tensor, table: torch.Tensor, vocab_start: int) -> None:
