@@ -343,3 +343,32 @@ def test_sampling_on_strided_rows_matches_contiguous(C):
     a1, c1 = C.fused_verify(other, view, spec, 1.0, 5, 2)
     a2, c2 = C.fused_verify(other.reshape(-1, 4096).contiguous(), flat, spec, 1.0, 5, 2)
     assert torch.equal(a1, a2) and torch.equal(c1, c2)
+
+
+def test_vocab_parallel_kernels_single_rank(C):
+    """With one rank (the exchange goes to itself) the vocab-parallel kernels equal the full-vocab ones,
+    on strided rows, across calls that cycle the exchange epochs and slot parities."""
+    ext = C.ext()
+    max_rows = 256
+    region = torch.zeros(ext.vp_region_bytes(max_rows), dtype=torch.uint8, device=DEV)
+    args = ([region.data_ptr()], 0, max_rows)
+    torch.manual_seed(4)
+    for call in range(5):
+        x = (torch.randn(8, 9, 4096, device=DEV) * 3).bfloat16()
+        clean, draft = x[:, :8, :], x[:, 1:, :]  # [8, 8, V] strided views
+        n = 64
+        out = torch.empty(n, dtype=torch.int64, device=DEV)
+        ext.vp_sample(draft, out, 1.25, False, 3, call, *args, 0)
+        assert torch.equal(out, C.sample_gumbel(draft, 1.25, 3, call))
+        ext.vp_sample(clean, out, 1.0, True, 0, 0, *args, 0)
+        assert torch.equal(out, C.argmax(clean))
+        spec = C.sample_gumbel(draft, 1.0, 8, call)
+        acc = torch.empty(n, dtype=torch.int32, device=DEV)
+        corr = torch.empty(n, dtype=torch.int64, device=DEV)
+        ext.vp_verify(clean, draft, spec, 1.0, 6, call, acc, corr, *args, 0)
+        acc_w, corr_w = C.fused_verify(clean, draft, spec, 1.0, 6, call)
+        assert torch.equal(acc, acc_w)
+        rej = acc_w == 0
+        assert torch.equal(corr[rej], corr_w[rej])
+    torch.cuda.synchronize()
+    assert int(region[:8].view(torch.int64).item()) == 15  # one epoch per call

@@ -119,11 +119,12 @@ class TwoPassDecoder:
             proposal[:, 0] = clean
             if L > 1:
                 spec_rows = logits[:, 1:, :]
-                if not (spec_rows.is_cuda and not sp.filtered(logits.shape[-1])):
+                if not (spec_rows.is_cuda and not sp.filtered(self.sampler.vocab_size(logits))):
                     spec_rows = spec_rows.reshape(-1, logits.shape[-1])
                 spec, q_sparse = self.sampler.sample(spec_rows, sp)
                 proposal[:, 1:] = spec.view(B, L - 1)
         else:
+            logits = self.sampler.full(logits)  # the tree builder ranks candidates over the whole vocabulary
             proposal = torch.zeros((B, L), dtype=torch.int64, device=logits.device)
             root, _ = self.sampler.sample(logits[:, 0, :], sp)
             proposal[:, 0] = root
@@ -146,11 +147,12 @@ class TwoPassDecoder:
             accepted = proposal[:, 1:] == target
             corr = target
         else:
-            V = logits.shape[-1]
+            V = self.sampler.vocab_size(logits)
+            Vs = logits.shape[-1]  # the local vocabulary shard under vocab-parallel sampling
             clean = logits[:, : L - 1, :]
             draft = draft_logits[:, : L - 1, :]
             if not clean.is_cuda or sp.filtered(V):
-                clean, draft = clean.reshape(-1, V), draft.reshape(-1, V)
+                clean, draft = clean.reshape(-1, Vs), draft.reshape(-1, Vs)
             spec = proposal[:, 1:].reshape(-1)
             if sp.filtered(V):
                 if q_sparse is None:
@@ -162,13 +164,10 @@ class TwoPassDecoder:
             corr = c.view(B, L - 1)
         return self.build_payload(proposal, accepted, corr, lookahead, sp)
 
-    @staticmethod
-    def _argmax(logits):
-        from uno_b200.engine.sampling import argmax
-
+    def _argmax(self, logits):
         shape = logits.shape
         rows = logits if logits.is_cuda else logits.reshape(-1, shape[-1])
-        return argmax(rows).view(shape[:-1])
+        return self.sampler.argmax(rows).view(shape[:-1])
 
     def build_payload(self, proposal, accepted, corr, lookahead, sp: SamplingParams):
         """``[B, L+2]`` int64: committed tokens (L+1 slots) then the length."""

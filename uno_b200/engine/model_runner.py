@@ -24,7 +24,7 @@ import torch
 
 from uno_b200.engine.decoder import TwoPassDecoder
 from uno_b200.engine.draft_tree import tree_kv_moves
-from uno_b200.engine.sampling import Sampler
+from uno_b200.engine.sampling import Sampler, VocabShard
 from uno_b200.engine.sequence import Sequence
 from uno_b200.engine.workspace import DecodeWorkspace, slots_for
 from uno_b200.layers.meta import ForwardMeta, Mode, ancestor_masks, causal_suffix_masks
@@ -95,10 +95,18 @@ class ModelRunner:
                 max_q = max(config.max_diffusion_block_size, config.tree_verify_size or 0)
                 max_tokens = max(config.max_num_batched_tokens, config.max_num_seqs * max_q)
                 self.tp_comm = FusedTPComm(rank, self.world_size, control.group if control is not None else None,
-                                           max_tokens, cfg.hidden_size, self.device)
+                                           max_tokens, cfg.hidden_size, self.device,
+                                           max_logit_rows=config.max_num_seqs * max(max_q, 1))
                 cuda_ops.set_tp_comm(self.tp_comm)
 
-        self.sampler = Sampler(config.seed)
+        shard = None
+        head = self.model.lm_head
+        if (self.tp_comm is not None and os.environ.get("UNO_VOCAB_PARALLEL", "1") != "0"
+                and head.per_partition % 8 == 0 and head.vocab_start % 8 == 0):
+            # logits stay vocab-sharded: sampling and verify exchange per-row partials over NVLink
+            shard = VocabShard(head.vocab_start, cfg.vocab_size, tp.all_gather_last_dim)
+        self.vocab_parallel = shard is not None
+        self.sampler = Sampler(config.seed, shard)
         self.allocate_kv_cache()
         max_q = max(config.max_diffusion_block_size, config.tree_verify_size or 0)
         max_pages = -(-(config.max_model_len + max_q) // self.page) + 1
@@ -173,7 +181,10 @@ class ModelRunner:
 
     # ------------------------------------------------------------ forwards
     def _logits_full(self, logits: torch.Tensor) -> torch.Tensor:
-        """Gather vocab shards so every rank holds the full logits row."""
+        """Gather vocab shards so every rank holds the full logits row (kept sharded when
+        sampling is vocab-parallel)."""
+        if self.vocab_parallel:
+            return logits
         return tp.all_gather_last_dim(logits)
 
     @torch.inference_mode()

@@ -18,22 +18,61 @@ On CUDA the hot variants (full-vocab Gumbel sampling, argmax, fused verify)
 run the framework's Philox-keyed kernels; on CPU they run here with a torch
 generator.  Randomness is keyed by ``(seed, counter)`` so every TP rank that
 runs the same call draws the same numbers without a broadcast.
+
+Vocab-parallel mode (tensor parallelism with the fused NVLink collectives):
+the lm_head leaves each rank a ``[rows, V/tp]`` logits shard and
+:class:`VocabShard` tells the sampler where it sits.  Greedy, unfiltered
+sampling and the unfiltered verify then run the vocab-parallel kernels, which
+exchange a few numbers per row between ranks instead of the logits; the
+Philox noise is keyed by global token id, so the tokens equal those of the
+same logits on one GPU.  Top-k / top-p and the draft tree gather the full
+logits first (``Sampler.full``).
 """
 
 from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
 
 import torch
 
 from uno_b200.sampling_params import SamplingParams
 
 
+@dataclass
+class VocabShard:
+    """This rank's slice ``[start, start + logits.shape[-1])`` of a ``vocab``-sized vocabulary."""
+
+    start: int
+    vocab: int
+    gather: Callable[[torch.Tensor], torch.Tensor]  # shard -> full logits (all-gather over the last dim)
+
+
 class Sampler:
     """Stateful sampler: one RNG stream (seed, counter) shared by all ranks."""
 
-    def __init__(self, seed: int = 0):
+    def __init__(self, seed: int = 0, shard: VocabShard | None = None):
         self.seed = int(seed) & 0xFFFFFFFF
         self.counter = 0
         self._gen: torch.Generator | None = None
+        self.shard = shard
+
+    def _sharded(self, logits: torch.Tensor) -> bool:
+        return self.shard is not None and logits.shape[-1] != self.shard.vocab
+
+    def full(self, logits: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits (gathers a vocab-parallel shard)."""
+        return self.shard.gather(logits) if self._sharded(logits) else logits
+
+    def vocab_size(self, logits: torch.Tensor) -> int:
+        return self.shard.vocab if self._sharded(logits) else logits.shape[-1]
+
+    def argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        if self._sharded(logits):
+            from uno_b200.ops import cuda
+
+            return cuda.vp_sample(logits, 1.0, self.seed, 0, self.shard.start, greedy=True)
+        return argmax(logits)
 
     def reseed(self, seed: int) -> None:
         self.seed = int(seed) & 0xFFFFFFFF
@@ -53,9 +92,13 @@ class Sampler:
     # ---------------------------------------------------------------- sampling
     def sample(self, logits: torch.Tensor, sp: SamplingParams):
         """Return ``(tokens [N] int64, sparse_q or None)``."""
-        V = logits.shape[-1]
+        V = self.vocab_size(logits)
         if sp.greedy:
-            return argmax(logits), None
+            return self.argmax(logits), None
+        if self._sharded(logits):
+            if not sp.filtered(V):
+                return self.sample_full(logits, sp.temperature), None
+            logits = self.full(logits)
         if sp.uses_top_k(V):
             ids, probs = sparse_top_k(logits, sp.temperature, int(sp.top_k), sp.top_p)
             off = self.sample_probs(probs)
@@ -73,6 +116,8 @@ class Sampler:
         if logits.is_cuda:
             from uno_b200.ops import cuda
 
+            if self._sharded(logits):
+                return cuda.vp_sample(logits, 1.0 / temperature, self.seed, key, self.shard.start)
             return cuda.sample_gumbel(logits, 1.0 / temperature, self.seed, key)
         probs = torch.softmax(logits.float() / temperature, dim=-1)
         return self.sample_probs(probs)
@@ -100,11 +145,15 @@ class Sampler:
         if clean_logits.is_cuda:
             from uno_b200.ops import cuda
 
+            if self._sharded(clean_logits):
+                return cuda.vp_verify(clean_logits, draft_logits, spec, 1.0 / temperature, self.seed, key,
+                                      self.shard.start)
             return cuda.fused_verify(clean_logits, draft_logits, spec, 1.0 / temperature, self.seed, key)
         return verify_reference(clean_logits, draft_logits, spec, temperature, self._cpu_gen())
 
     def verify_filtered(self, clean_logits: torch.Tensor, spec: torch.Tensor, sp: SamplingParams,
                         draft_distribution):
+        clean_logits = self.full(clean_logits)
         V = clean_logits.shape[-1]
         if sp.top_k is None:
             clean_ids, clean_probs = sparse_top_p(clean_logits, sp.temperature, float(sp.top_p))

@@ -28,6 +28,13 @@ void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, 
                                const at::Tensor& weight, int64_t groups, double eps, bool wait_all);
 void embedding_scatter_launch(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& ids,
                               const at::Tensor& table, int64_t start, int64_t recv_off, int64_t gather_off);
+void vp_sample_launch(const at::Tensor& x, at::Tensor& out, double inv_temp, bool greedy, int64_t seed,
+                      int64_t offset, const std::vector<int64_t>& regions, int64_t rank, int64_t max_rows,
+                      int64_t vstart);
+void vp_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at::Tensor& spec, double inv_temp,
+                      int64_t seed, int64_t offset, at::Tensor& accepted, at::Tensor& corr,
+                      const std::vector<int64_t>& regions, int64_t rank, int64_t max_rows, int64_t vstart);
+int64_t vp_region_bytes(int64_t max_rows);
 std::vector<int64_t> symm_alloc(int64_t nbytes);
 int64_t symm_open(const std::vector<int64_t>& handle_bytes);
 void symm_close(int64_t ptr, bool owned);
@@ -226,6 +233,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("walk_tree", &uno::walk_tree_launch);
   m.def("reduce_norm_gather", &uno::reduce_norm_gather_launch);
   m.def("embedding_scatter", &uno::embedding_scatter_launch);
+  m.def("vp_sample", &uno::vp_sample_launch);
+  m.def("vp_verify", &uno::vp_verify_launch);
+  m.def("vp_region_bytes", &uno::vp_region_bytes);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);
   m.def("symm_close", &uno::symm_close);

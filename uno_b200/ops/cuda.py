@@ -326,6 +326,26 @@ def fused_verify(clean, draft, spec, inv_temp, seed, offset):
     return acc, corr
 
 
+def vp_sample(logits, inv_temp, seed, offset, vocab_start, greedy=False):
+    """Sample (or arg-max) from a vocab-parallel logits shard; every rank gets the same global ids."""
+    regions, rank, max_rows = _COMM.vp_args()
+    out = torch.empty(_n_rows(logits), device=logits.device, dtype=torch.int64)
+    ext().vp_sample(logits, out, float(inv_temp), bool(greedy), int(seed), int(offset), regions, rank, max_rows,
+                    int(vocab_start))
+    return out
+
+
+def vp_verify(clean, draft, spec, inv_temp, seed, offset, vocab_start):
+    """Psi-Spec accept test + residual resample on vocab-parallel shards of the target/draft logits."""
+    regions, rank, max_rows = _COMM.vp_args()
+    n = _n_rows(clean)
+    acc = torch.empty(n, device=clean.device, dtype=torch.int32)
+    corr = torch.empty(n, device=clean.device, dtype=torch.int64)
+    ext().vp_verify(clean, draft, spec.reshape(-1).contiguous(), float(inv_temp), int(seed), int(offset), acc, corr,
+                    regions, rank, max_rows, int(vocab_start))
+    return acc, corr
+
+
 def build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature):
     from uno_b200.engine.draft_tree import DraftTreeBatch
 

@@ -8,7 +8,9 @@ over NVLink (no NCCL on the hot path).  Layout (see ``ops/csrc/comm.cu``):
 * ``[0, 4096)`` control words (epoch counter, CTA counter, arrive/done flags);
 * ``recv``: ``tp x R x H`` bf16 receive slots for row-parallel partial rows;
 * ``gather``: ``T_max x H`` bf16 gathered activations (normalised rows that
-  their owners broadcast to every rank).
+  their owners broadcast to every rank);
+* ``vp``: the vocab-parallel sampling exchange region (per-row partials and
+  flags of ``ops/csrc/vocab_parallel.cu``) for up to ``max_logit_rows`` rows.
 
 :class:`FusedTPComm` is consumed by ``uno_b200.ops.cuda``: row-parallel GEMMs
 and the vocab-parallel embedding send their partial rows into the owners'
@@ -40,7 +42,8 @@ def _align(n: int, a: int = 4096) -> int:
 
 
 class FusedTPComm:
-    def __init__(self, rank: int, world: int, control_group, max_tokens: int, hidden: int, device):
+    def __init__(self, rank: int, world: int, control_group, max_tokens: int, hidden: int, device,
+                 max_logit_rows: int | None = None):
         from uno_b200.ops.cuda import ext
 
         if world > 8:
@@ -54,7 +57,9 @@ class FusedTPComm:
         recv_bytes = self.world * R * self.hidden * 2
         self.gather_off = _align(self.recv_off + recv_bytes)
         gather_bytes = self.world * R * self.hidden * 2
-        self.nbytes = _align(self.gather_off + gather_bytes)
+        self.vp_off = _align(self.gather_off + gather_bytes)
+        self.max_logit_rows = int(max_logit_rows or self.max_tokens)
+        self.nbytes = _align(self.vp_off + int(ext().vp_region_bytes(self.max_logit_rows)))
         out = ext().symm_alloc(self.nbytes)
         self.ptr = int(out[0])
         handle = [int(b) for b in out[1:]]
@@ -65,6 +70,10 @@ class FusedTPComm:
         self.gather = raw.view(torch.bfloat16).view(self.world * R, self.hidden)
         self._closed = False
         dist.barrier(group=control_group)
+
+    def vp_args(self) -> tuple[list[int], int, int]:
+        """``(exchange region of every rank, rank, max rows)`` for the vocab-parallel sampling kernels."""
+        return [p + self.vp_off for p in self.peers], self.rank, self.max_logit_rows
 
     def rows_per_rank(self, T: int) -> int:
         return -(-int(T) // self.world)
