@@ -4,10 +4,15 @@
 launches of the case, then one launch inside the NVTX range ``capture`` (for
 ``ncu --nvtx --nvtx-include capture/``), then times a CUDA graph of
 ``--repeat`` back-to-back launches with CUDA events (per-launch device time,
-host launch cost excluded) and prints one JSON line per kernel.  Inputs are random; the
-decode-attention KV cache (~240 MB) is larger than the L2.
+host launch cost excluded) and prints one JSON line per kernel.  Inputs are
+random.  Consecutive launches never find their operands in the L2: GEMM
+weights rotate through enough copies to exceed twice the 126 MB L2, the
+lm_head weight (1.24 GB) and the decode-attention KV cache (~240 MB) exceed it
+alone, and the sampling case alternates two 156 MB logit blocks.
 
-Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden), ``decode-attention``.
+Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden),
+``lm-head``, ``decode-attention``, ``sampling`` (full-vocab verify and one
+vocab-parallel shard).
 """
 
 from __future__ import annotations
@@ -18,31 +23,84 @@ import json
 import torch
 
 
+_L2_BYTES = 126 << 20
+
+
+def _copies(nbytes: int) -> int:
+    """Weight copies to rotate through so that consecutive launches never hit the L2."""
+    return max(1, -(-2 * _L2_BYTES // max(1, nbytes)))
+
+
+def _weights(n: int, k: int, scale: float = 0.02) -> list:
+    return [torch.randn(n, k, device="cuda").bfloat16() * scale for _ in range(_copies(n * k * 2))]
+
+
 def _layer_gemms():
     from uno_b200.ops import cuda as C
 
     M, H, I = 512, 4096, 12288
     x = torch.randn(M, H, device="cuda").bfloat16()
-    w_gu = C.interleave_gate_up(torch.randn(2 * I, H, device="cuda").bfloat16() * 0.02)
+    w_gu = [C.interleave_gate_up(w) for w in _weights(2 * I, H)]
     act = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
-    w_o = torch.randn(H, H, device="cuda").bfloat16() * 0.02
+    w_o = _weights(H, H)
     y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
-    w_qkv = torch.randn(6144, H, device="cuda").bfloat16() * 0.02
+    w_qkv = _weights(6144, H)
     qkv = torch.empty(M, 6144, device="cuda", dtype=torch.bfloat16)
     a_i = torch.randn(M, I, device="cuda").bfloat16()
-    w_d = torch.randn(H, I, device="cuda").bfloat16() * 0.02
-    a_l = torch.randn(192, H, device="cuda").bfloat16() * 0.02
+    w_d = _weights(H, I)
+    a_l = _weights(192, H)
     h_l = torch.empty(M, 192, device="cuda", dtype=torch.bfloat16)
     mask = torch.ones(M, device="cuda")
     return {
-        "gate_up_silu 512x24576x4096": (lambda: C._gemm(x, w_gu, C.EPI_SILU, c=act), 2 * M * 2 * I * H,
-                                        2 * I * H * 2),
-        "qkv (plain store) 512x6144x4096": (lambda: C._gemm(x, w_qkv, C.EPI_STORE, c=qkv), 2 * M * 6144 * H,
-                                            6144 * H * 2),
-        "o_proj 512x4096x4096": (lambda: C._gemm(x, w_o, C.EPI_STORE, c=y), 2 * M * H * H, H * H * 2),
-        "down 512x4096x12288": (lambda: C._gemm(a_i, w_d, C.EPI_STORE, c=y), 2 * M * H * I, H * I * 2),
-        "lora_hidden 512x192x4096": (lambda: C._gemm(x, a_l, C.EPI_ROWSCALE, c=h_l, scale=2.0, row_mask=mask),
-                                     2 * M * 192 * H, (M + 192) * H * 2),
+        "gate_up_silu 512x24576x4096": (lambda i: C._gemm(x, w_gu[i % len(w_gu)], C.EPI_SILU, c=act),
+                                        2 * M * 2 * I * H, 2 * I * H * 2),
+        "qkv (plain store) 512x6144x4096": (lambda i: C._gemm(x, w_qkv[i % len(w_qkv)], C.EPI_STORE, c=qkv),
+                                            2 * M * 6144 * H, 6144 * H * 2),
+        "o_proj 512x4096x4096": (lambda i: C._gemm(x, w_o[i % len(w_o)], C.EPI_STORE, c=y), 2 * M * H * H,
+                                 H * H * 2),
+        "down 512x4096x12288": (lambda i: C._gemm(a_i, w_d[i % len(w_d)], C.EPI_STORE, c=y), 2 * M * H * I,
+                                H * I * 2),
+        "lora_hidden 512x192x4096": (lambda i: C._gemm(x, a_l[i % len(a_l)], C.EPI_ROWSCALE, c=h_l, scale=2.0,
+                                                       row_mask=mask), 2 * M * 192 * H, (M + 192) * H * 2),
+    }
+
+
+def _lm_head():
+    from uno_b200.ops import cuda as C
+
+    M, H, V = 512, 4096, 151936
+    x = torch.randn(M, H, device="cuda").bfloat16()
+    w = [torch.randn(V, H, device="cuda").bfloat16() * 0.02]  # 1.24 GB: larger than the L2 by itself
+    return {"lm_head 512x151936x4096": (lambda i: C.lm_head(x, w[0]), 2 * M * V * H, V * H * 2)}
+
+
+def _sampling():
+    """Full-vocabulary verify at TP=1 and the vocab-parallel verify of one TP=8 shard (exchange with itself)."""
+    from uno_b200.ops import cuda as C
+
+    B, L, V = 64, 8, 151936
+    clean = [torch.randn(B, L, V, device="cuda").bfloat16() * 3 for _ in range(2)]  # 2 x 156 MB
+    draft = [c + 0.5 for c in clean]
+    spec = torch.randint(0, V, (B * (L - 1),), device="cuda")
+    Vs = V // 8
+    shards = [c[:, :, :Vs].contiguous() for c in clean]
+    dshards = [d[:, :, :Vs].contiguous() for d in draft]
+    max_rows = B * L
+    region = torch.zeros(C.ext().vp_region_bytes(max_rows), dtype=torch.uint8, device="cuda")
+    regions = [region.data_ptr()]
+    acc = torch.empty(B * (L - 1), dtype=torch.int32, device="cuda")
+    corr = torch.empty(B * (L - 1), dtype=torch.int64, device="cuda")
+    rows = B * (L - 1)
+
+    def vp(i):
+        j = i % 2
+        C.ext().vp_verify(shards[j][:, : L - 1], dshards[j][:, 1:], spec, 1.0, 1, i, acc, corr, regions, 0, max_rows,
+                          0)
+
+    return {
+        f"fused_verify {rows} rows x V={V}": (lambda i: C.fused_verify(clean[i % 2][:, : L - 1], draft[i % 2][:, 1:],
+                                                                       spec, 1.0, 1, i), 0, rows * V * 2 * 2),
+        f"vp_verify {rows} rows x V/8={Vs} (1 rank)": (vp, 0, rows * Vs * 2 * 2),
     }
 
 
@@ -68,10 +126,11 @@ def _decode_attention():
                        suffix_mask=causal_suffix_masks(Q, "cuda").repeat(B, 1), seqlen_q=Q, max_kv=3328)
     kv_bytes = sum(n + Q for n in lens) * hkv * 128 * 2 * 2
     return {f"decode_attention B={B} Q={Q} mean_kv={sum(lens) // B}":
-            (lambda: C.attention(q, kc, vc, meta, 128 ** -0.5), 0, kv_bytes)}
+            (lambda i: C.attention(q, kc, vc, meta, 128 ** -0.5), 0, kv_bytes)}
 
 
-CASES = {"layer-gemms": _layer_gemms, "decode-attention": _decode_attention}
+CASES = {"layer-gemms": _layer_gemms, "lm-head": _lm_head, "decode-attention": _decode_attention,
+         "sampling": _sampling}
 
 
 def main(argv=None):
@@ -83,13 +142,13 @@ def main(argv=None):
 
     torch.manual_seed(0)
     cases = CASES[args.case]()
-    for _ in range(2):
+    for i in range(2):
         for fn, _, _ in cases.values():
-            fn()
+            fn(i)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("capture")
     for fn, _, _ in cases.values():
-        fn()
+        fn(2)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     out = []
@@ -97,8 +156,8 @@ def main(argv=None):
         # replay a CUDA graph of back-to-back launches: host launch cost stays off the clock
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            for _ in range(args.repeat):
-                fn()
+            for i in range(args.repeat):
+                fn(i)
         graph.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
