@@ -372,3 +372,29 @@ def test_vocab_parallel_kernels_single_rank(C):
         assert torch.equal(corr[rej], corr_w[rej])
     torch.cuda.synchronize()
     assert int(region[:8].view(torch.int64).item()) == 15  # one epoch per call
+
+
+def test_fused_adamw_single_rank_matches_torch(C):
+    from uno_b200.train.optim import ShardedLoraAdamW
+
+    shapes = [(64, 4096), (4096, 64), (5,)]
+    init = [torch.randn(*sh, device=DEV) for sh in shapes]
+    mine = [torch.nn.Parameter(t.clone()) for t in init]
+    ref = [torch.nn.Parameter(t.clone()) for t in init]
+    opt = ShardedLoraAdamW(mine, lr=3e-3, weight_decay=0.05, max_grad_norm=0.5)
+    topt = torch.optim.AdamW(ref, lr=3e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.05)
+    g = torch.Generator(device=DEV).manual_seed(1)
+    for _ in range(3):
+        gs = [torch.randn(*sh, device=DEV, generator=g) for sh in shapes]
+        opt.zero_grad()
+        for p, x in zip(mine, gs):
+            p.grad += x
+        norm = opt.step()
+        for p, x in zip(ref, gs):
+            p.grad = x.clone()
+        want = torch.nn.utils.clip_grad_norm_(ref, 0.5)
+        topt.step()
+        assert abs(norm - float(want)) < 1e-3 * float(want)
+    for a, b in zip(mine, ref):
+        torch.testing.assert_close(a.detach(), b.detach(), rtol=1e-5, atol=1e-6)
+    opt.close()

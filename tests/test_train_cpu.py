@@ -234,3 +234,66 @@ def test_training_cli_stops_and_resumes_at_a_stage_boundary(tmp_path, capsys):
     # a different objective does not match the run manifest
     with pytest.raises(ValueError, match="does not match"):
         main(common + ["--resume", os.path.join(out, "checkpoint-2"), "--kl-weight", "1.0"])
+
+
+# ---------------------------------------------------------- sharded AdamW
+def _adamw_ref(init, grads_per_rank, steps, lr, wd, clip):
+    """torch.optim.AdamW on rank-averaged, globally clipped gradients."""
+    params = [torch.nn.Parameter(t.clone()) for t in init]
+    opt = torch.optim.AdamW(params, lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=wd)
+    for s in range(steps):
+        for i, p in enumerate(params):
+            p.grad = sum(g[s][i] for g in grads_per_rank) / len(grads_per_rank)
+        torch.nn.utils.clip_grad_norm_(params, clip)
+        opt.step()
+    return [p.detach() for p in params]
+
+
+def _grads(rank, steps, shapes):
+    g = torch.Generator().manual_seed(100 + rank)
+    return [[torch.randn(*sh, generator=g) * (3.0 if s == 0 else 0.01) for sh in shapes] for s in range(steps)]
+
+
+def _adamw_worker(rank, world, port, box):
+    import torch.distributed as dist
+
+    from uno_b200.train.optim import ShardedLoraAdamW
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    shapes = [(3, 5), (7,), (2, 2, 3)]
+    init = [torch.linspace(-1, 1, int(torch.tensor(sh).prod())).view(*sh) for sh in shapes]
+    params = [torch.nn.Parameter(t.clone()) for t in init]
+    opt = ShardedLoraAdamW(params, lr=0.05, weight_decay=0.1, max_grad_norm=1.0, group=dist.group.WORLD)
+    grads = _grads(rank, 3, shapes)
+    norms = []
+    for s in range(3):
+        opt.zero_grad()
+        for p, g in zip(params, grads[s]):
+            p.grad += g  # accumulate like autograd does into the flat buffer view
+        norms.append(opt.step())
+    box.put((rank, [p.detach().clone() for p in params], norms))
+    dist.destroy_process_group()
+
+
+def test_sharded_adamw_matches_torch_adamw_two_ranks():
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("fork")
+    box = ctx.Queue()
+    procs = [ctx.Process(target=_adamw_worker, args=(r, 2, port, box)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict((r, (ps, ns)) for r, ps, ns in (box.get(timeout=60) for _ in procs))
+    for p in procs:
+        p.join(30)
+    shapes = [(3, 5), (7,), (2, 2, 3)]
+    init = [torch.linspace(-1, 1, int(torch.tensor(sh).prod())).view(*sh) for sh in shapes]
+    want = _adamw_ref(init, [_grads(r, 3, shapes) for r in range(2)], 3, 0.05, 0.1, 1.0)
+    for r in range(2):
+        for got, ref in zip(out[r][0], want):
+            torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-6)
+    assert out[0][1] == out[1][1] and out[0][1][0] > 1.0  # the first step is clipped

@@ -35,6 +35,11 @@ void vp_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at
                       int64_t seed, int64_t offset, at::Tensor& accepted, at::Tensor& corr,
                       const std::vector<int64_t>& regions, int64_t rank, int64_t max_rows, int64_t vstart);
 int64_t vp_region_bytes(int64_t max_rows);
+void fused_adamw_launch(const std::vector<int64_t>& ws, int64_t rank, int64_t params_off, int64_t grads_off,
+                        int64_t ctl_off, int64_t n, at::Tensor& m, at::Tensor& v, at::Tensor& scratch,
+                        at::Tensor& norm_out, double lr, double beta1, double beta2, double eps, double weight_decay,
+                        double max_norm, int64_t step);
+int64_t opt_ctl_bytes();
 std::vector<int64_t> symm_alloc(int64_t nbytes);
 int64_t symm_open(const std::vector<int64_t>& handle_bytes);
 void symm_close(int64_t ptr, bool owned);
@@ -236,6 +241,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vp_sample", &uno::vp_sample_launch);
   m.def("vp_verify", &uno::vp_verify_launch);
   m.def("vp_region_bytes", &uno::vp_region_bytes);
+  m.def("fused_adamw", &uno::fused_adamw_launch);
+  m.def("opt_ctl_bytes", &uno::opt_ctl_bytes);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);
   m.def("symm_close", &uno::symm_close);

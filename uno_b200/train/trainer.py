@@ -12,7 +12,9 @@ decoder:
    (:func:`uno_b200.train.losses.fused_head_loss`);
 4. LoRA gradients are averaged over data-parallel ranks, clipped to
    ``max_grad_norm`` and applied with AdamW under a linear-warmup / cosine
-   schedule.
+   schedule -- ZeRO-2 style (each rank keeps the moments of one shard), on
+   CUDA as one fused reduce-scatter + clip + AdamW + all-gather kernel
+   (:class:`uno_b200.train.optim.ShardedLoraAdamW`).
 
 Checkpoints are written only at curriculum stage boundaries
 (``checkpoint-{step}/`` with the PEFT adapter, optimizer and RNG state and
@@ -37,6 +39,7 @@ from uno_b200.train.forward import uno_hidden_states
 from uno_b200.train.layout import build_uno_batch, shift_labels_for_next_token
 from uno_b200.train.lora import TrainableLoRA
 from uno_b200.train.losses import fused_head_loss
+from uno_b200.train.optim import ShardedLoraAdamW
 
 
 def lr_at(step: int, base_lr: float, warmup: int, total: int) -> float:
@@ -70,8 +73,9 @@ class UnoTrainer:
         for p in model.parameters():
             p.requires_grad_(False)
         self.device = next(lora.parameters()).device
-        self.optimizer = torch.optim.AdamW(lora.parameters(), lr=self.base_lr, betas=(0.9, 0.999), eps=1e-8,
-                                           weight_decay=weight_decay)
+        self.optimizer = ShardedLoraAdamW(list(lora.parameters()), lr=self.base_lr, betas=(0.9, 0.999), eps=1e-8,
+                                          weight_decay=weight_decay, max_grad_norm=self.max_grad_norm,
+                                          group=process_group)
         self.step = 0
         rank = dist.get_rank(process_group) if (process_group is not None and dist.is_initialized()) else 0
         self.generator = torch.Generator(device=self.device).manual_seed(int(seed) * 1000003 + rank)
@@ -113,7 +117,7 @@ class UnoTrainer:
             raise RuntimeError("training already reached the curriculum's last step")
         t0 = time.perf_counter()
         block = self.curriculum.stage_for_step(self.step).block_size
-        self.optimizer.zero_grad(set_to_none=True)
+        self.optimizer.zero_grad()
         total, tokens, noised = 0.0, 0, 0
         for mb in micro_batches:
             loss, info = self._micro_loss(mb, block)
@@ -121,29 +125,16 @@ class UnoTrainer:
             total += float(loss.detach()) / len(micro_batches)
             tokens += info["tokens"]
             noised += info["noised"]
-        params = [p for p in self.lora.parameters() if p.grad is not None]
-        if self.group is not None and dist.is_initialized() and dist.get_world_size(self.group) > 1:
-            world = dist.get_world_size(self.group)
-            flat = torch.cat([p.grad.reshape(-1) for p in params])
-            dist.all_reduce(flat, group=self.group)
-            flat /= world
-            off = 0
-            for p in params:
-                n = p.grad.numel()
-                p.grad.copy_(flat[off:off + n].view_as(p.grad))
-                off += n
-        grad_norm = float(torch.nn.utils.clip_grad_norm_(params, self.max_grad_norm)) if params else 0.0
         lr = lr_at(self.step, self.base_lr, self.warmup, self.curriculum.max_steps)
-        for g in self.optimizer.param_groups:
-            g["lr"] = lr
-        self.optimizer.step()
+        self.optimizer.set_lr(lr)
+        grad_norm = self.optimizer.step()  # DP gradient average, clip, AdamW, parameter all-gather
         self.step += 1
         metrics = {"step": self.step, "loss": total, "block_size": block, "lr": lr, "grad_norm": grad_norm,
                    "tokens": tokens, "noised_tokens": noised, "seconds": time.perf_counter() - t0,
                    "transformer_forwards": len(micro_batches)}
         self.last_metrics = metrics
         reason = self.curriculum.checkpoint_reasons.get(self.step)
-        if reason and self.output_dir is not None and self._is_main():
+        if reason and self.output_dir is not None:
             self.save_checkpoint(reason)
         return metrics
 
@@ -151,15 +142,20 @@ class UnoTrainer:
         return not (self.group is not None and dist.is_initialized() and dist.get_rank(self.group) != 0)
 
     # ---------------------------------------------------------- checkpoints
+    def _rank(self) -> int:
+        return dist.get_rank(self.group) if (self.group is not None and dist.is_initialized()) else 0
+
     def save_checkpoint(self, reason: str) -> Path:
+        """Every rank writes its optimizer shard and RNG state; rank 0 the adapter and the boundary record."""
         ckpt = self.output_dir / f"checkpoint-{self.step}"
         ckpt.mkdir(parents=True, exist_ok=True)
-        self.lora.save(str(ckpt), self.base_model_name)
         torch.save({"optimizer": self.optimizer.state_dict(), "generator": self.generator.get_state(),
-                    "step": self.step}, ckpt / "trainer_state.pt")
-        write_json_atomic(ckpt / "uno_curriculum_state.json",
-                          {"version": 1, "global_step": self.step, "reason": reason,
-                           "curriculum_sha256": self.curriculum.sha256()})
+                    "step": self.step}, ckpt / f"trainer_state_rank{self._rank()}.pt")
+        if self._is_main():
+            self.lora.save(str(ckpt), self.base_model_name)
+            write_json_atomic(ckpt / "uno_curriculum_state.json",
+                              {"version": 1, "global_step": self.step, "reason": reason,
+                               "curriculum_sha256": self.curriculum.sha256()})
         return ckpt
 
     def resume(self, checkpoint: str | Path) -> None:
@@ -175,7 +171,8 @@ class UnoTrainer:
         if step not in self.curriculum.checkpoint_reasons:
             raise ValueError(f"Checkpoint step {step} is not a curriculum boundary.")
         self.lora.load(str(ckpt))
-        blob = torch.load(ckpt / "trainer_state.pt", map_location=self.device, weights_only=False)
+        blob = torch.load(ckpt / f"trainer_state_rank{self._rank()}.pt", map_location=self.device,
+                          weights_only=False)
         self.optimizer.load_state_dict(blob["optimizer"])
         self.generator.set_state(blob["generator"].cpu() if hasattr(blob["generator"], "cpu") else blob["generator"])
         self.step = int(blob["step"])
