@@ -398,3 +398,27 @@ def test_fused_adamw_single_rank_matches_torch(C):
     for a, b in zip(mine, ref):
         torch.testing.assert_close(a.detach(), b.detach(), rtol=1e-5, atol=1e-6)
     opt.close()
+
+
+@pytest.mark.parametrize("K,M,N,splits", [(8192, 4096, 64, 0), (300, 72, 136, 0), (8192, 64, 4096, 0),
+                                          (4096, 1024, 64, 1), (1000, 384, 192, 3)])
+def test_gemm_weight_gradient(C, K, M, N, splits):
+    """c32 += a^T b with both operands reduced over their rows (MN-major tcgen05 operands)."""
+    torch.manual_seed(K + M + N)
+    a = torch.randn(K, M, device=DEV).bfloat16()
+    b = torch.randn(K, N, device=DEV).bfloat16()
+    c = torch.randn(M, N, device=DEV)
+    want = c + a.float().t() @ b.float()
+    C.ext().gemm_wgrad(a, b, c, splits)
+    assert rel_err(c, want) < 2e-3
+
+
+def test_gemm_weight_gradient_strided_slices(C):
+    """Operands that are column slices of wider row-major matrices (per-projection LoRA gradients)."""
+    torch.manual_seed(3)
+    dy = torch.randn(2048, 6144, device=DEV).bfloat16()
+    h = torch.randn(2048, 192, device=DEV).bfloat16()
+    c = torch.zeros(1024, 64, device=DEV)
+    C.ext().gemm_wgrad(dy[:, 4096:5120], h[:, 64:128], c, 0)
+    want = dy[:, 4096:5120].float().t() @ h[:, 64:128].float()
+    assert rel_err(c, want) < 2e-3

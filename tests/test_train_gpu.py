@@ -1,0 +1,97 @@
+"""Training on the GPU: native tcgen05 projections vs the torch-op path (same model, same LoRA)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(seed=0):
+    from uno_b200.models.decoder import build_model
+    from uno_b200.train import LoraSettings, TrainableLoRA, build_uno_batch
+    from uno_b200.train.optim import ShardedLoraAdamW
+    from uno_b200.utils.hf_compat import ModelConfig
+    from uno_b200.utils.loader import dummy_init
+
+    cfg = ModelConfig(model_type="qwen3", vocab_size=4096, hidden_size=256, intermediate_size=768,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                      max_position_embeddings=2048, mask_token_id=4095, rope_theta=1e6)
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device("cuda"):
+        model = build_model(cfg)
+    torch.set_default_dtype(torch.float32)
+    dummy_init(model, seed=seed)
+    lora = TrainableLoRA(cfg, LoraSettings(target="all", rank=8, alpha=16), device="cuda", seed=seed)
+    with torch.no_grad():
+        g = torch.Generator(device="cuda").manual_seed(seed + 1)
+        for p in lora.B.values():  # non-zero B so both factors receive gradients
+            p.copy_(torch.randn(p.shape, device="cuda", generator=g) * 0.05)
+    opt = ShardedLoraAdamW(list(lora.parameters()), lr=1e-3)
+    ids = torch.randint(1, 4000, (1, 256), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    labels = ids.clone()
+    labels[:, :32] = -100
+    pos = torch.arange(256, device="cuda")[None]
+    ub = build_uno_batch(ids, labels, pos, block_size=4, mask_token_id=4095,
+                         generator=torch.Generator(device="cuda").manual_seed(7))
+    return model, lora, opt, ub
+
+
+def _grads(native: bool):
+    from uno_b200.train.forward import uno_hidden_states
+    from uno_b200.train.native import build_projections
+
+    model, lora, opt, ub = _setup()
+    proj = build_projections(model, lora) if native else None
+    if proj is not None:
+        for layer in proj:
+            for p in layer.values():
+                p.refresh(0)
+    opt.zero_grad()
+    h = uno_hidden_states(model, lora, ub.ids, ub.positions, ub.attention_mask(), ub.noisy, native=proj)
+    w = torch.randn(h.shape, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
+    (h.float() * w).sum().backward()
+    torch.cuda.synchronize()
+    out = opt.flat_grad.clone(), h.detach().float()
+    opt.close()
+    return out
+
+
+def test_native_projections_match_torch_path():
+    from uno_b200.ops import cuda
+
+    g_ref, h_ref = _grads(native=False)
+    g_nat, h_nat = _grads(native=True)
+    assert cuda.error_flag() == 0
+    assert ((h_nat - h_ref).norm() / h_ref.norm()).item() < 2e-2
+    rel = ((g_nat - g_ref).norm() / g_ref.norm()).item()
+    assert g_ref.abs().sum() > 0 and rel < 5e-2, rel
+
+
+@pytest.mark.parametrize("weights,teacher_ce", [((1.0, 0.0, 0.0), True), ((0.3, 0.5, 0.7), True),
+                                                ((0.0, 0.0, 1.0), False)])
+def test_fused_loss_kernel_matches_fp32(weights, teacher_ce):
+    """tcgen05 logits + the fused TV/KL/CE kernel vs the fp32 torch chunks (loss and d loss / d h)."""
+    from uno_b200.ops import cuda
+    from uno_b200.train.losses import fused_head_loss
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    N, H, V = 300, 256, 4096
+    w = (torch.randn(V, H, device="cuda", generator=g) * 0.08).bfloat16()
+    s = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    t = (s.float() + 0.3 * torch.randn(N, H, device="cuda", generator=g)).bfloat16()
+    dist = torch.rand(N, device="cuda", generator=g) > 0.2
+    ce = torch.rand(N, device="cuda", generator=g) > 0.5
+    tgt = torch.randint(0, V, (N,), device="cuda", generator=g)
+    scale = 1.0 + torch.rand(N, device="cuda", generator=g)
+    kw = dict(dist_mask=dist, ce_mask=ce, ce_target=tgt, ce_scale=scale, tv_weight=weights[0],
+              kl_weight=weights[1], ce_weight=weights[2], teacher_ce=teacher_ce, normalizer=int(dist.sum()), chunk=128)
+    s1 = s.clone().requires_grad_(True)
+    loss = fused_head_loss(s1, t, w, **kw)
+    loss.backward()
+    s2 = s.float().clone().requires_grad_(True)
+    ref = fused_head_loss(s2, t.float(), w.float(), **kw)
+    ref.backward()
+    assert cuda.error_flag() == 0
+    assert abs(loss.item() - ref.item()) <= 2e-2 * abs(ref.item()) + 1e-4
+    gerr = ((s1.grad.float() - s2.grad).norm() / s2.grad.norm()).item()
+    assert gerr < 4e-2, gerr

@@ -40,6 +40,9 @@ void fused_adamw_launch(const std::vector<int64_t>& ws, int64_t rank, int64_t pa
                         at::Tensor& norm_out, double lr, double beta1, double beta2, double eps, double weight_decay,
                         double max_norm, int64_t step);
 int64_t opt_ctl_bytes();
+void uno_loss_launch(const at::Tensor& s, const at::Tensor& t, const at::Tensor& target, bool teacher_ce,
+                     const at::Tensor& ce_w, const at::Tensor& dist_w, double tv_w, double kl_w, double ce_weight,
+                     at::Tensor& row_loss, at::Tensor& grad);
 std::vector<int64_t> symm_alloc(int64_t nbytes);
 int64_t symm_open(const std::vector<int64_t>& handle_bytes);
 void symm_close(int64_t ptr, bool owned);
@@ -169,6 +172,38 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
                 ext ? b2->stride(0) : 0, p, cur_stream(), (int)max_ctas);
 }
 
+// c32[M, N] += a^T b with a [K, M], b [K, N] bf16 (row-major, reduced over rows) and c32 fp32.
+static void gemm_wgrad(const at::Tensor& a, const at::Tensor& b, at::Tensor& c32, int64_t splits) {
+  check_dev(a, "wgrad A");
+  check_dev(b, "wgrad B");
+  check_dev(c32, "wgrad C");
+  UNO_CHECK_BF16(a);
+  UNO_CHECK_BF16(b);
+  TORCH_CHECK(c32.scalar_type() == at::kFloat && c32.dim() == 2 && c32.stride(1) == 1, "wgrad C must be fp32 rows");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(0) == b.size(0), "wgrad: operands must share their rows");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "wgrad operands must be contiguous along their columns");
+  TORCH_CHECK(c32.size(0) == a.size(1) && c32.size(1) == b.size(1), "wgrad: C must be [a.cols, b.cols]");
+  TORCH_CHECK(c32.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(c32.data_ptr()) % 16 == 0,
+              "wgrad C rows must be 16-byte aligned");
+  GemmParams p{};
+  p.M = a.size(1);
+  p.N = b.size(1);
+  p.K = a.size(0);
+  if (p.M == 0 || p.N == 0 || p.K == 0) return;
+  p.C32 = c32.data_ptr<float>();
+  p.ldc32 = (int)c32.stride(0);
+  DeviceScratch& scratch = device_scratch();
+  p.err = scratch.err;
+  const int bn = p.N <= 64 ? 64 : 128;
+  p.splits = pick_splits(p.M, p.N, p.K, bn, (int)splits);
+  const int tiles = ((p.M + 127) / 128) * ((p.N + bn - 1) / bn);
+  if (p.splits > 1 && (tiles > scratch.max_counters || (size_t)tiles * p.splits * 128 * bn > scratch.ws_floats))
+    p.splits = 1;
+  p.ws = scratch.ws;
+  p.counters = scratch.counters;
+  gemm_wgrad_dispatch(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), p, bn, cur_stream());
+}
+
 static void rms_norm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, at::Tensor& y,
                      double eps, int64_t groups) {
   rmsnorm_launch(x, residual, w, y, eps, (int)groups);
@@ -238,11 +273,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("walk_tree", &uno::walk_tree_launch);
   m.def("reduce_norm_gather", &uno::reduce_norm_gather_launch);
   m.def("embedding_scatter", &uno::embedding_scatter_launch);
+  m.def("gemm_wgrad", &uno::gemm_wgrad);
   m.def("vp_sample", &uno::vp_sample_launch);
   m.def("vp_verify", &uno::vp_verify_launch);
   m.def("vp_region_bytes", &uno::vp_region_bytes);
   m.def("fused_adamw", &uno::fused_adamw_launch);
   m.def("opt_ctl_bytes", &uno::opt_ctl_bytes);
+  m.def("uno_loss", &uno::uno_loss_launch);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);
   m.def("symm_close", &uno::symm_close);

@@ -188,6 +188,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* smem) {
   return d;
 }
 
+// MN-major operand tile staged as BK-row boxes of 64 contiguous MN elements
+// (128 B rows, 128-byte swizzle): 8-row K groups are 1024 B apart (stride byte
+// offset) and consecutive 64-element MN groups are one 64 x 128 B box apart
+// (leading byte offset, 8 KB).  One 16-deep MMA step advances 16 rows = 2 KB.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(const void* smem) {
+  uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;      // start address
+  d |= (8192ull >> 4) << 16;         // leading byte offset: next 64-element MN group
+  d |= (1024ull >> 4) << 32;         // stride byte offset: next 8 K rows
+  d |= 1ull << 46;                   // descriptor version (sm_100)
+  d |= 2ull << 61;                   // layout: 128-byte swizzle
+  return d;
+}
+
 // Instruction descriptor: kind::f16, A/B bf16, D fp32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4)                    // D format fp32

@@ -46,11 +46,20 @@
 
 namespace uno {
 
-enum Epi : int { EPI_STORE = 0, EPI_SILU = 1, EPI_ROWSCALE = 2, EPI_ADD = 3, EPI_QKROPE = 5 };
+// EPI_WGRAD: weight-gradient form.  Both operands are MN-major (A is [K, M]
+// and B is [K, N], row-major, reduced over their rows: C = A^T B) and the
+// epilogue accumulates into an fp32 matrix (C32 += A^T B).  Used for LoRA
+// gradients, where the reduction runs over the tokens.
+enum Epi : int { EPI_STORE = 0, EPI_SILU = 1, EPI_ROWSCALE = 2, EPI_ADD = 3, EPI_QKROPE = 5, EPI_WGRAD = 6 };
 
 template <int EPI>
 constexpr bool is_qkrope() {
   return EPI == EPI_QKROPE;
+}
+
+template <int EPI>
+constexpr bool mn_major() {
+  return EPI == EPI_WGRAD;
 }
 
 template <int BN, int EPI>
@@ -240,6 +249,29 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, const AccSrc& 
       if (n0 + h * 128 >= p.N) break;
       qkrope_head(p, src, buf, lane, row, row_ok, h * 128, n0 + h * 128);
     }
+  } else if constexpr (EPI == EPI_WGRAD) {
+    if (!row_ok) return;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      const int col = n0 + c;
+      if (col >= p.N) break;
+      float v[32];
+      src.load32(c, v);
+      float* dst = p.C32 + (size_t)row * p.ldc32 + col;
+      if (col + 32 <= p.N) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 o = reinterpret_cast<float4*>(dst)[q];
+          o.x += v[4 * q];
+          o.y += v[4 * q + 1];
+          o.z += v[4 * q + 2];
+          o.w += v[4 * q + 3];
+          reinterpret_cast<float4*>(dst)[q] = o;
+        }
+      } else {
+        for (int i = 0; i < p.N - col; ++i) dst[i] += v[i];
+      }
+    }
   } else if constexpr (EPI == EPI_SILU) {
     using S = Stage<32>;
     // Tile columns hold [gate 64 | up 64] pairs; output column block n_blk*BN/2.
@@ -383,7 +415,17 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          if (kb < kb_main) {
+          if constexpr (mn_major<EPI>()) {
+            // [K rows][64 MN] boxes: BM / 64 for A, BN / 64 for B, 8 KB apart
+#pragma unroll
+            for (int h = 0; h < Cfg::BM / 64; ++h)
+              tma_load_2d(sA + stage * Cfg::A_BYTES + h * 8192, &tmA, &full[stage], m_blk * Cfg::BM + h * 64,
+                          kb * Cfg::BK);
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h)
+              tma_load_2d(sB + stage * Cfg::B_BYTES + h * 8192, &tmB, &full[stage], n_blk * BN + h * 64,
+                          kb * Cfg::BK);
+          } else if (kb < kb_main) {
             tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, m_blk * Cfg::BM);
             tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * Cfg::BK, n_blk * BN);
           } else {
@@ -411,7 +453,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, BN);
+      constexpr uint32_t idesc = idesc_bf16(128, BN) | (mn_major<EPI>() ? (1u << 15) | (1u << 16) : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -432,12 +474,22 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = smem_desc_sw128(sA + stage * Cfg::A_BYTES);
-          const uint64_t bdesc = smem_desc_sw128(sB + stage * Cfg::B_BYTES);
+          if constexpr (mn_major<EPI>()) {
+            const uint64_t adesc = smem_desc_mn_sw128(sA + stage * Cfg::A_BYTES);
+            const uint64_t bdesc = smem_desc_mn_sw128(sB + stage * Cfg::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 16; ++k) {
-            // advance 16 bf16 = 32 bytes along K inside the swizzle atom
-            tc_mma_bf16(d, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc, (kb > kb0 || k > 0));
+            for (int k = 0; k < Cfg::BK / 16; ++k) {
+              // advance 16 K rows = 2048 bytes (two 8-row groups)
+              tc_mma_bf16(d, adesc + (uint64_t)(k * 128), bdesc + (uint64_t)(k * 128), idesc, (kb > kb0 || k > 0));
+            }
+          } else {
+            const uint64_t adesc = smem_desc_sw128(sA + stage * Cfg::A_BYTES);
+            const uint64_t bdesc = smem_desc_sw128(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+            for (int k = 0; k < Cfg::BK / 16; ++k) {
+              // advance 16 bf16 = 32 bytes along K inside the swizzle atom
+              tc_mma_bf16(d, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc, (kb > kb0 || k > 0));
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -961,6 +1013,22 @@ static void dispatch_bn(int bn, const void* a, int64_t lda, const void* b, int64
       launch<32, EPI>(ta, tb, ta2, tb2, p, stream, max_ctas);
     }
   }
+}
+
+// C32[M, N] += A^T B for row-major A [K, M] and B [K, N] (weight gradients).
+void gemm_wgrad_dispatch(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p, int bn,
+                         cudaStream_t stream) {
+  TORCH_CHECK(p.K2 == 0, "the weight-gradient GEMM has no K extension");
+  CUtensorMap ta = make_tmap_bf16(a, p.K, p.M, lda, 64);
+  CUtensorMap tb = make_tmap_bf16(b, p.K, p.N, ldb, 64);
+  p.num_m = (p.M + 127) / 128;
+  p.num_n = (p.N + bn - 1) / bn;
+  if (bn == 64)
+    launch<64, EPI_WGRAD>(ta, tb, ta, tb, p, stream, 0);
+  else if (bn == 128)
+    launch<128, EPI_WGRAD>(ta, tb, ta, tb, p, stream, 0);
+  else
+    TORCH_CHECK(false, "weight-gradient GEMM tiles are 64 or 128 columns wide");
 }
 
 void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,

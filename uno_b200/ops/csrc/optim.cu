@@ -171,7 +171,8 @@ void fused_adamw_launch(const std::vector<int64_t>& ws, int64_t rank, int64_t pa
   TORCH_CHECK(n % world == 0, "parameter count must be a multiple of the world size");
   TORCH_CHECK(step >= 1, "AdamW step counts from 1");
   const int64_t shard = n / world;
-  for (at::Tensor* t : {&m, &v, &scratch}) {
+  at::Tensor* shards[3] = {&m, &v, &scratch};
+  for (at::Tensor* t : shards) {
     check_dev(*t, "optimizer state");
     TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() >= shard, "fp32 shard buffer");
   }

@@ -49,12 +49,17 @@ struct GemmParams {
   // "done" for the current epoch in this rank's workspace control block
   const uint8_t* ag_base;
   int ag_R;
+  // weight-gradient GEMM (EPI_WGRAD): C32[M, N] += A^T B in fp32
+  float* C32;
+  int ldc32;
 };
 void gemm_dispatch(int epi, int bn, const void* a, int64_t lda, const void* b, int64_t ldb, const void* a2,
                    int64_t lda2, const void* b2, int64_t ldb2, GemmParams& p, cudaStream_t stream, int max_ctas);
 int pick_bn(int M, int N, int forced);
 int pick_splits(int M, int N, int K, int bn, int forced);
 void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, int* bn, int* splits);
+void gemm_wgrad_dispatch(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p, int bn,
+                         cudaStream_t stream);
 int num_sms();
 
 // Per-device scratch shared by the GEMM split-K path (fp32 partials and

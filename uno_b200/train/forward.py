@@ -80,18 +80,57 @@ def _layer(x, layer, li, lora, mask, positions, cos_sin, attn_mask, cfg):
     return x + d
 
 
+def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask):
+    """The same layer with every projection on the tcgen05 GEMMs (``uno_b200.train.native``)."""
+    from uno_b200.train.native import projection
+
+    B, T, H = x.shape
+    attn = layer.self_attn
+    hq, hkv, hd = attn.num_heads, attn.num_kv_heads, attn.head_dim
+    ln1 = layer.input_layernorm
+    h = R.rms_norm(x, ln1.weight, ln1.eps, ln1.n_groups)
+    qkv = projection(h, proj["qkv"], mask)
+    q_end, k_end = hq * hd, (hq + hkv) * hd
+    q = qkv[..., :q_end].reshape(B, T, hq, hd)
+    k = qkv[..., q_end:k_end].reshape(B, T, hkv, hd)
+    v = qkv[..., k_end:].reshape(B, T, hkv, hd)
+    if attn.qk_norm:
+        q = R.head_rms_norm(q, attn.q_norm.weight, attn.eps)
+        k = R.head_rms_norm(k, attn.k_norm.weight, attn.eps)
+    pos = positions.reshape(-1)
+    q = R.apply_rope(q.reshape(B * T, hq, hd), pos, cos_sin).reshape(B, T, hq, hd)
+    k = R.apply_rope(k.reshape(B * T, hkv, hd), pos, cos_sin).reshape(B, T, hkv, hd)
+    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                       attn_mask=attn_mask[:, None], scale=attn.scale, enable_gqa=hq != hkv)
+    o = o.transpose(1, 2).reshape(B, T, hq * hd)
+    x = x + projection(o, proj["o"], mask)
+    ln2 = layer.post_attention_layernorm
+    h = R.rms_norm(x, ln2.weight, ln2.eps, ln2.n_groups)
+    gu = projection(h, proj["gate_up"], mask)
+    inter = gu.shape[-1] // 2
+    a = F.silu(gu[..., :inter]) * gu[..., inter:]
+    return x + projection(a, proj["down"], mask)
+
+
 def uno_hidden_states(model, lora: TrainableLoRA | None, ids: torch.Tensor, positions: torch.Tensor,
                       attn_mask: torch.Tensor, lora_rows: torch.Tensor | None,
-                      checkpoint_layers: bool = False) -> torch.Tensor:
-    """Final-norm hidden states ``[B, T, H]`` for the Uno layout."""
+                      checkpoint_layers: bool = False, native: list | None = None) -> torch.Tensor:
+    """Final-norm hidden states ``[B, T, H]`` for the Uno layout.
+
+    ``native`` (from :func:`uno_b200.train.native.build_projections`) runs the
+    projections on the tcgen05 GEMMs; without it every op is a torch op.
+    """
     dec = model.model
     x = F.embedding(ids, dec.embed_tokens.weight)
     cos_sin = model.cos_sin_cache
     for li, layer in enumerate(dec.layers):
-        if checkpoint_layers and torch.is_grad_enabled():
-            x = checkpoint(_layer, x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config,
-                           use_reentrant=False)
+        if native is not None:
+            fn, args = _layer_native, (x, layer, native[li], lora_rows, positions, cos_sin, attn_mask)
         else:
-            x = _layer(x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config)
+            fn, args = _layer, (x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config)
+        if checkpoint_layers and torch.is_grad_enabled():
+            x = checkpoint(fn, *args, use_reentrant=False)
+        else:
+            x = fn(*args)
     norm = dec.norm
     return R.rms_norm(x, norm.weight, norm.eps, norm.n_groups)

@@ -18,7 +18,9 @@ the student logits is formed in closed form inside the same pass --
   d CE / d s  = w * (p_s - onehot(y))
 
 -- and immediately projected back to ``d h = d s . W``; only the
-``[rows, H]`` gradient is kept for backward.
+``[rows, H]`` gradient is kept for backward.  On CUDA each chunk is two
+tcgen05 GEMMs for the logits, one kernel for the three terms and their
+gradient (written over the student logits), and one GEMM for ``d h``.
 """
 
 from __future__ import annotations
@@ -56,14 +58,58 @@ def _chunk_terms(s_logits, t_logits, targets, ce_w, dist_w, weights):
     return loss, grad
 
 
+def _transposed(weight: torch.Tensor) -> torch.Tensor:
+    """A cached ``[H, V]`` copy of the frozen lm_head weight (the K-major operand of ``d h = d s . W``)."""
+    cached = getattr(weight, "_uno_transposed", None)
+    if cached is None or cached.shape != weight.t().shape:
+        cached = weight.detach().t().contiguous()
+        weight._uno_transposed = cached
+    return cached
+
+
+def _head_loss_cuda(student_h, teacher_h, w, ce_target, ce_w, dist_w, weights, teacher_ce, chunk):
+    """Chunks through the tcgen05 GEMMs and the fused loss kernel (``ops/csrc/train_loss.cu``)."""
+    from uno_b200.ops import cuda as C
+
+    rows, H = student_h.shape
+    V = w.shape[0]
+    wt = _transposed(w)
+    tv_w, kl_w, ce_weight = weights
+    grad_h = torch.empty(rows, H, dtype=torch.bfloat16, device=student_h.device)
+    row_loss = torch.empty(rows, dtype=torch.float32, device=student_h.device)
+    s = torch.empty(min(chunk, rows), V, dtype=torch.bfloat16, device=student_h.device)
+    t = torch.empty_like(s)
+    sh = student_h.to(torch.bfloat16).contiguous()
+    th = teacher_h.to(torch.bfloat16).contiguous()
+    tgt = ce_target.long().contiguous()
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        n = r1 - r0
+        C._gemm(sh[r0:r1], w, C.EPI_STORE, c=s[:n])
+        C._gemm(th[r0:r1], w, C.EPI_STORE, c=t[:n])
+        # the gradient overwrites the student logits in place
+        C.ext().uno_loss(s[:n], t[:n], tgt[r0:r1], bool(teacher_ce), ce_w[r0:r1].contiguous(),
+                         dist_w[r0:r1].contiguous(), float(tv_w), float(kl_w), float(ce_weight), row_loss[r0:r1],
+                         s[:n])
+        C._gemm(s[:n], wt, C.EPI_STORE, c=grad_h[r0:r1])
+    return row_loss.sum(), grad_h
+
+
 class _FusedHeadLoss(torch.autograd.Function):
     @staticmethod
     def forward(ctx, student_h, teacher_h, weight, ce_target, ce_w, dist_w, weights, teacher_ce, normalizer,
                 chunk):
+        ctx.normalizer = normalizer
+        ctx.h_dtype = student_h.dtype
+        w = weight
+        if student_h.is_cuda and w.dtype == torch.bfloat16 and w.shape[1] % 64 == 0 and w.shape[0] % 64 == 0:
+            total, grad_h = _head_loss_cuda(student_h, teacher_h, w, ce_target, ce_w, dist_w, weights, teacher_ce,
+                                            chunk)
+            ctx.save_for_backward(grad_h)
+            return total / normalizer
         rows = student_h.shape[0]
         grad_h = torch.zeros(rows, student_h.shape[1], dtype=torch.float32, device=student_h.device)
         total = torch.zeros((), dtype=torch.float32, device=student_h.device)
-        w = weight
         for r0 in range(0, rows, chunk):
             r1 = min(rows, r0 + chunk)
             s = (student_h[r0:r1] @ w.t()).float()
@@ -73,8 +119,6 @@ class _FusedHeadLoss(torch.autograd.Function):
             total += loss
             grad_h[r0:r1] = (g.to(w.dtype) @ w).float()
         ctx.save_for_backward(grad_h)
-        ctx.normalizer = normalizer
-        ctx.h_dtype = student_h.dtype
         return total / normalizer
 
     @staticmethod

@@ -1,0 +1,163 @@
+"""Training projections on the framework's tcgen05 GEMMs (CUDA).
+
+A frozen base projection with gated LoRA segments (the reference trains PEFT
+LoRA on q,k,v,o,gate,up,down with a token-wise router, ``training/lora.py:
+136-179``; its GEMMs are cuBLAS through HF/PEFT):
+
+    y = x W^T + sum_seg  (s * mask * (x A_seg^T)) B_seg^T     (segments tile y's columns)
+
+Forward: ONE ROWSCALE GEMM for the concatenated LoRA hidden ``h = s * mask *
+(x A_cat^T)`` and ONE base GEMM whose K dimension is extended by ``h`` against
+the block-diagonal ``B_cat`` (the same K-extension the inference kernels use).
+
+Backward (base weights frozen: no weight gradient for W):
+
+    dh  = s * mask * (dy B_cat)              ROWSCALE GEMM against B_cat^T
+    dx  = dy W + dh A_cat                    base GEMM against W^T, K-extended by (dh, A_cat^T)
+    dB_seg += dy[:, seg]^T h[:, seg]         weight-gradient GEMMs (fp32 accumulate
+    dA_cat += dh^T x                         straight into the parameters' .grad)
+
+``W^T`` is a transposed copy of the frozen weight made once (weights never
+change during LoRA training), so every GEMM runs K-major operands except the
+weight gradients, which use the MN-major tcgen05 form.  LoRA gradients are
+accumulated by the backward directly into the fp32 ``.grad`` buffers of the
+LoRA parameters (the optimizer's flat gradient), not returned to autograd.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class LoraSegment:
+    """Columns ``[col0, col0 + width)`` of the output use ``A`` [r, K] and ``B`` [width, r] (fp32 params)."""
+
+    col0: int
+    width: int
+    A: torch.nn.Parameter
+    B: torch.nn.Parameter
+
+
+@dataclass
+class ProjectionWeights:
+    W: torch.Tensor                 # [N, K] bf16, frozen
+    Wt: torch.Tensor                # [K, N] bf16 copy
+    segments: list = field(default_factory=list)
+    scale: float = 1.0
+    # bf16 compute copies of the LoRA factors, rebuilt after every optimizer step
+    a_cat: torch.Tensor | None = None   # [S*r, K]
+    at_cat: torch.Tensor | None = None  # [K, S*r]
+    b_cat: torch.Tensor | None = None   # [N, S*r] block diagonal
+    bt_cat: torch.Tensor | None = None  # [S*r, N]
+    version: int = -1
+
+    @torch.no_grad()
+    def refresh(self, version: int) -> None:
+        if not self.segments or self.version == version:
+            return
+        r = self.segments[0].A.shape[0]
+        S = len(self.segments)
+        N, K = self.W.shape
+        a = torch.cat([seg.A for seg in self.segments], 0).to(torch.bfloat16)
+        b = torch.zeros(N, S * r, device=self.W.device, dtype=torch.bfloat16)
+        for i, seg in enumerate(self.segments):
+            b[seg.col0:seg.col0 + seg.width, i * r:(i + 1) * r] = seg.B.to(torch.bfloat16)
+        self.a_cat, self.at_cat = a.contiguous(), a.t().contiguous()
+        self.b_cat, self.bt_cat = b, b.t().contiguous()
+        self.version = version
+
+
+def _a_grad_block(segments) -> torch.Tensor:
+    """The contiguous fp32 [S*r, K] gradient region of the segments' A factors (one flat buffer)."""
+    g0 = segments[0].A.grad
+    r, K = g0.shape
+    for i, seg in enumerate(segments):
+        g = seg.A.grad
+        if g is None or g.data_ptr() != g0.data_ptr() + i * r * K * 4:
+            raise RuntimeError("LoRA A gradients of one projection must be adjacent in the flat gradient buffer")
+    return torch.as_strided(g0, (len(segments) * r, K), (K, 1))
+
+
+class _ProjectionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, proj: ProjectionWeights, mask):
+        from uno_b200.ops import cuda as C
+
+        M = x.shape[0]
+        N = proj.W.shape[0]
+        y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+        h = None
+        if proj.segments:
+            h = torch.empty(M, proj.a_cat.shape[0], device=x.device, dtype=torch.bfloat16)
+            C._gemm(x, proj.a_cat, C.EPI_ROWSCALE, c=h, scale=proj.scale, row_mask=mask)
+            C._gemm(x, proj.W, C.EPI_STORE, c=y, a2=h, b2=proj.b_cat)
+        else:
+            C._gemm(x, proj.W, C.EPI_STORE, c=y)
+        ctx.proj = proj
+        ctx.save_for_backward(x, h, mask)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from uno_b200.ops import cuda as C
+
+        x, h, mask = ctx.saved_tensors
+        proj: ProjectionWeights = ctx.proj
+        dy = dy.to(torch.bfloat16).contiguous()
+        M, K = x.shape
+        dx = torch.empty(M, K, device=x.device, dtype=torch.bfloat16)
+        if proj.segments:
+            r = proj.segments[0].A.shape[0]
+            dh = torch.empty_like(h)
+            C._gemm(dy, proj.bt_cat, C.EPI_ROWSCALE, c=dh, scale=proj.scale, row_mask=mask)
+            C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx, a2=dh, b2=proj.at_cat)
+            ext = C.ext()
+            for i, seg in enumerate(proj.segments):
+                ext.gemm_wgrad(dy[:, seg.col0:seg.col0 + seg.width], h[:, i * r:(i + 1) * r], seg.B.grad, 0)
+            ext.gemm_wgrad(dh, x, _a_grad_block(proj.segments), 0)
+        else:
+            C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx)
+        return dx, None, None
+
+
+def projection(x: torch.Tensor, proj: ProjectionWeights, mask: torch.Tensor | None) -> torch.Tensor:
+    """``x [..., K] -> [..., N]`` through the base + gated-LoRA projection."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+    m = (mask.reshape(-1).float().contiguous() if mask is not None
+         else torch.ones(x2.shape[0], device=x.device, dtype=torch.float32))
+    y = _ProjectionFn.apply(x2, proj, m)
+    return y.view(*shape[:-1], y.shape[-1])
+
+
+def build_projections(model, lora) -> list[dict[str, ProjectionWeights]]:
+    """Per layer: ``qkv``, ``o``, ``gate_up`` and ``down`` projections with their LoRA segments."""
+    layers = []
+    scale = float(lora.scaling) if lora is not None else 1.0
+
+    def seg(li, name, col0, width):
+        if lora is None or not lora.has(li, name):
+            return None
+        key = lora._key(li, name)
+        return LoraSegment(col0, width, lora.A[key], lora.B[key])
+
+    for li, layer in enumerate(model.model.layers):
+        attn, mlp = layer.self_attn, layer.mlp
+        hq, hkv, hd = attn.num_heads, attn.num_kv_heads, attn.head_dim
+        inter = mlp.gate_up_proj.weight.shape[0] // 2
+        out = {}
+        for name, w, segs in (
+            ("qkv", attn.qkv_proj.weight, [seg(li, "q_proj", 0, hq * hd), seg(li, "k_proj", hq * hd, hkv * hd),
+                                           seg(li, "v_proj", (hq + hkv) * hd, hkv * hd)]),
+            ("o", attn.o_proj.weight, [seg(li, "o_proj", 0, attn.o_proj.weight.shape[0])]),
+            ("gate_up", mlp.gate_up_proj.weight, [seg(li, "gate_proj", 0, inter), seg(li, "up_proj", inter, inter)]),
+            ("down", mlp.down_proj.weight, [seg(li, "down_proj", 0, mlp.down_proj.weight.shape[0])]),
+        ):
+            segs = [s for s in segs if s is not None]
+            wb = w.detach().to(torch.bfloat16).contiguous()
+            out[name] = ProjectionWeights(W=wb, Wt=wb.t().contiguous(), segments=segs, scale=scale)
+        layers.append(out)
+    return layers

@@ -55,7 +55,7 @@ class UnoTrainer:
                  curriculum: BlockCurriculumPlan, mask_token_id: int, lr: float = 1e-4, warmup_steps: int = 0,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, output_dir: str | None = None,
                  checkpoint_layers: bool = False, seed: int = 0, process_group=None,
-                 base_model_name: str | None = None, loss_chunk: int = 1024):
+                 base_model_name: str | None = None, loss_chunk: int = 1024, native_gemms: bool = True):
         objective.validate()
         self.model = model
         self.lora = lora
@@ -76,6 +76,12 @@ class UnoTrainer:
         self.optimizer = ShardedLoraAdamW(list(lora.parameters()), lr=self.base_lr, betas=(0.9, 0.999), eps=1e-8,
                                           weight_decay=weight_decay, max_grad_norm=self.max_grad_norm,
                                           group=process_group)
+        # CUDA: projections (forward and backward) on the tcgen05 GEMMs
+        self.native = None
+        if self.device.type == "cuda" and native_gemms:
+            from uno_b200.train.native import build_projections
+
+            self.native = build_projections(model, lora)
         self.step = 0
         rank = dist.get_rank(process_group) if (process_group is not None and dist.is_initialized()) else 0
         self.generator = torch.Generator(device=self.device).manual_seed(int(seed) * 1000003 + rank)
@@ -90,8 +96,12 @@ class UnoTrainer:
                      else positions.to(self.device))
         ub = build_uno_batch(ids, labels, positions, block_size=block_size, mask_token_id=self.mask_token_id,
                              generator=self.generator)
+        if self.native is not None:
+            for proj in self.native:
+                for p in proj.values():
+                    p.refresh(self.optimizer.step_count)
         hidden = uno_hidden_states(self.model, self.lora, ub.ids, ub.positions, ub.attention_mask(), ub.noisy,
-                                   self.checkpoint_layers)
+                                   self.checkpoint_layers, native=self.native)
         noisy_h, clean_h = ub.gather_regions(hidden)
         H = noisy_h.shape[-1]
         supervised = labels != IGNORE_INDEX
