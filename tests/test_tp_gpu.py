@@ -77,3 +77,13 @@ def test_fused_zero2_adamw_matches_torch_adamw():
            "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "optim_worker.py")]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "OPT_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_sharded_projection_gemms_match_replicated():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TORCH_DISTRIBUTED_TIMEOUT_MINUTES="2",
+               PYTHONPATH=HERE + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "fsdp_worker.py")]
+    out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and "FSDP_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]

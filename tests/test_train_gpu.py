@@ -41,7 +41,7 @@ def _grads(native: bool):
     from uno_b200.train.native import build_projections
 
     model, lora, opt, ub = _setup()
-    proj = build_projections(model, lora) if native else None
+    proj = build_projections(model, lora)[0] if native else None
     if proj is not None:
         for layer in proj:
             for p in layer.values():

@@ -45,6 +45,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--checkpoint-layers", action="store_true")
     p.add_argument("--resume")
     p.add_argument("--max-steps", type=int, help="stop after this many optimizer steps (default: curriculum end)")
+    p.add_argument("--fsdp", action="store_true",
+                   help="CUDA: shard the frozen projection weights over the ranks (GEMMs read peers' rows)")
     p.add_argument("--seed", type=int, default=0)
     return p
 
@@ -113,7 +115,7 @@ def main(argv: list[str] | None = None) -> list[dict]:
     trainer = UnoTrainer(model, lora, objective=objective, curriculum=plan, mask_token_id=mask_id, lr=args.lr,
                          warmup_steps=args.warmup_steps, weight_decay=args.weight_decay,
                          max_grad_norm=args.max_grad_norm, output_dir=out, checkpoint_layers=args.checkpoint_layers,
-                         seed=args.seed, process_group=group, base_model_name=args.model)
+                         seed=args.seed, process_group=group, base_model_name=args.model, fsdp=args.fsdp)
     if args.resume:
         validate_resume_manifest(out, compat)
         trainer.resume(args.resume)

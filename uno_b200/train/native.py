@@ -42,11 +42,24 @@ class LoraSegment:
 
 
 @dataclass
+class WeightShard:
+    """Rows ``[r0, r1)`` of a frozen weight, held by one rank (possibly a peer over NVLink)."""
+
+    r0: int
+    r1: int
+    W: torch.Tensor   # [r1 - r0, K] bf16
+    Wt: torch.Tensor  # [K, r1 - r0] bf16
+
+
+@dataclass
 class ProjectionWeights:
-    W: torch.Tensor                 # [N, K] bf16, frozen
-    Wt: torch.Tensor                # [K, N] bf16 copy
+    W: torch.Tensor | None          # [N, K] bf16, frozen (None when sharded)
+    Wt: torch.Tensor | None         # [K, N] bf16 copy
     segments: list = field(default_factory=list)
     scale: float = 1.0
+    shards: list | None = None      # FSDP: every rank's WeightShard, in row order
+    out_features: int = 0
+    in_features: int = 0
     # bf16 compute copies of the LoRA factors, rebuilt after every optimizer step
     a_cat: torch.Tensor | None = None   # [S*r, K]
     at_cat: torch.Tensor | None = None  # [K, S*r]
@@ -60,9 +73,10 @@ class ProjectionWeights:
             return
         r = self.segments[0].A.shape[0]
         S = len(self.segments)
-        N, K = self.W.shape
+        N = self.out_features
+        dev = self.segments[0].A.device
         a = torch.cat([seg.A for seg in self.segments], 0).to(torch.bfloat16)
-        b = torch.zeros(N, S * r, device=self.W.device, dtype=torch.bfloat16)
+        b = torch.zeros(N, S * r, device=dev, dtype=torch.bfloat16)
         for i, seg in enumerate(self.segments):
             b[seg.col0:seg.col0 + seg.width, i * r:(i + 1) * r] = seg.B.to(torch.bfloat16)
         self.a_cat, self.at_cat = a.contiguous(), a.t().contiguous()
@@ -87,15 +101,20 @@ class _ProjectionFn(torch.autograd.Function):
         from uno_b200.ops import cuda as C
 
         M = x.shape[0]
-        N = proj.W.shape[0]
+        N = proj.out_features
         y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
         h = None
         if proj.segments:
             h = torch.empty(M, proj.a_cat.shape[0], device=x.device, dtype=torch.bfloat16)
             C._gemm(x, proj.a_cat, C.EPI_ROWSCALE, c=h, scale=proj.scale, row_mask=mask)
-            C._gemm(x, proj.W, C.EPI_STORE, c=y, a2=h, b2=proj.b_cat)
+        if proj.shards is None:
+            C._gemm(x, proj.W, C.EPI_STORE, c=y, a2=h, b2=proj.b_cat if h is not None else None)
         else:
-            C._gemm(x, proj.W, C.EPI_STORE, c=y)
+            # FSDP all-gather fused into the GEMM: each output column block streams
+            # its weight rows straight from the owner's memory (TMA over NVLink)
+            for sh in proj.shards:
+                C._gemm(x, sh.W, C.EPI_STORE, c=y[:, sh.r0:sh.r1], a2=h,
+                        b2=proj.b_cat[sh.r0:sh.r1] if h is not None else None)
         ctx.proj = proj
         ctx.save_for_backward(x, h, mask)
         return y
@@ -109,17 +128,25 @@ class _ProjectionFn(torch.autograd.Function):
         dy = dy.to(torch.bfloat16).contiguous()
         M, K = x.shape
         dx = torch.empty(M, K, device=x.device, dtype=torch.bfloat16)
+        dh = None
         if proj.segments:
-            r = proj.segments[0].A.shape[0]
             dh = torch.empty_like(h)
             C._gemm(dy, proj.bt_cat, C.EPI_ROWSCALE, c=dh, scale=proj.scale, row_mask=mask)
-            C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx, a2=dh, b2=proj.at_cat)
+        if proj.shards is None:
+            C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx, a2=dh, b2=proj.at_cat if dh is not None else None)
+        else:
+            # dx = sum over owners of dy[:, rows_j] W_j; the first block also adds dh A_cat
+            for j, sh in enumerate(proj.shards):
+                first = j == 0
+                C._gemm(dy[:, sh.r0:sh.r1], sh.Wt, C.EPI_STORE if first else C.EPI_ADD, c=dx,
+                        r=None if first else dx, a2=dh if first else None,
+                        b2=proj.at_cat if (first and dh is not None) else None)
+        if proj.segments:
+            r = proj.segments[0].A.shape[0]
             ext = C.ext()
             for i, seg in enumerate(proj.segments):
                 ext.gemm_wgrad(dy[:, seg.col0:seg.col0 + seg.width], h[:, i * r:(i + 1) * r], seg.B.grad, 0)
             ext.gemm_wgrad(dh, x, _a_grad_block(proj.segments), 0)
-        else:
-            C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx)
         return dx, None, None
 
 
@@ -133,10 +160,8 @@ def projection(x: torch.Tensor, proj: ProjectionWeights, mask: torch.Tensor | No
     return y.view(*shape[:-1], y.shape[-1])
 
 
-def build_projections(model, lora) -> list[dict[str, ProjectionWeights]]:
-    """Per layer: ``qkv``, ``o``, ``gate_up`` and ``down`` projections with their LoRA segments."""
-    layers = []
-    scale = float(lora.scaling) if lora is not None else 1.0
+def _projection_specs(model, lora):
+    """``(layer, name, weight, segments)`` for every projection of the decoder."""
 
     def seg(li, name, col0, width):
         if lora is None or not lora.has(li, name):
@@ -148,7 +173,6 @@ def build_projections(model, lora) -> list[dict[str, ProjectionWeights]]:
         attn, mlp = layer.self_attn, layer.mlp
         hq, hkv, hd = attn.num_heads, attn.num_kv_heads, attn.head_dim
         inter = mlp.gate_up_proj.weight.shape[0] // 2
-        out = {}
         for name, w, segs in (
             ("qkv", attn.qkv_proj.weight, [seg(li, "q_proj", 0, hq * hd), seg(li, "k_proj", hq * hd, hkv * hd),
                                            seg(li, "v_proj", (hq + hkv) * hd, hkv * hd)]),
@@ -156,8 +180,34 @@ def build_projections(model, lora) -> list[dict[str, ProjectionWeights]]:
             ("gate_up", mlp.gate_up_proj.weight, [seg(li, "gate_proj", 0, inter), seg(li, "up_proj", inter, inter)]),
             ("down", mlp.down_proj.weight, [seg(li, "down_proj", 0, mlp.down_proj.weight.shape[0])]),
         ):
-            segs = [s for s in segs if s is not None]
+            yield li, name, w, [s for s in segs if s is not None]
+
+
+def build_projections(model, lora, group=None, fsdp: bool = False):
+    """Per layer: ``qkv``, ``o``, ``gate_up`` and ``down`` projections with their LoRA segments.
+
+    With ``fsdp`` every frozen weight is split by output rows across the ranks
+    of ``group`` (:class:`uno_b200.train.fsdp.ShardedWeights`): each rank keeps
+    1/world of the rows (and of their transposes), and the GEMMs stream the
+    other ranks' rows from their memory -- the FSDP all-gather fused into the
+    GEMM's operand loads.  Returns ``(layers, sharded)``.
+    """
+    scale = float(lora.scaling) if lora is not None else 1.0
+    specs = list(_projection_specs(model, lora))
+    sharded = None
+    if fsdp:
+        from uno_b200.train.fsdp import ShardedWeights
+
+        sharded = ShardedWeights([(f"{li}.{name}", w) for li, name, w, _ in specs], group)
+    layers: list[dict[str, ProjectionWeights]] = [dict() for _ in model.model.layers]
+    for li, name, w, segs in specs:
+        N, K = w.shape
+        if sharded is None:
             wb = w.detach().to(torch.bfloat16).contiguous()
-            out[name] = ProjectionWeights(W=wb, Wt=wb.t().contiguous(), segments=segs, scale=scale)
-        layers.append(out)
-    return layers
+            pw = ProjectionWeights(W=wb, Wt=wb.t().contiguous(), segments=segs, scale=scale, out_features=N,
+                                   in_features=K)
+        else:
+            pw = ProjectionWeights(W=None, Wt=None, segments=segs, scale=scale,
+                                   shards=sharded.shards(f"{li}.{name}"), out_features=N, in_features=K)
+        layers[li][name] = pw
+    return layers, sharded

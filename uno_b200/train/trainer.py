@@ -55,7 +55,8 @@ class UnoTrainer:
                  curriculum: BlockCurriculumPlan, mask_token_id: int, lr: float = 1e-4, warmup_steps: int = 0,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, output_dir: str | None = None,
                  checkpoint_layers: bool = False, seed: int = 0, process_group=None,
-                 base_model_name: str | None = None, loss_chunk: int = 1024, native_gemms: bool = True):
+                 base_model_name: str | None = None, loss_chunk: int = 1024, native_gemms: bool = True,
+                 fsdp: bool = False):
         objective.validate()
         self.model = model
         self.lora = lora
@@ -77,11 +78,14 @@ class UnoTrainer:
                                           weight_decay=weight_decay, max_grad_norm=self.max_grad_norm,
                                           group=process_group)
         # CUDA: projections (forward and backward) on the tcgen05 GEMMs
+        # (with fsdp the frozen projection weights are row-sharded over the ranks and
+        # the GEMMs read the peers' rows over NVLink)
         self.native = None
+        self.sharded = None
         if self.device.type == "cuda" and native_gemms:
             from uno_b200.train.native import build_projections
 
-            self.native = build_projections(model, lora)
+            self.native, self.sharded = build_projections(model, lora, group=process_group, fsdp=fsdp)
         self.step = 0
         rank = dist.get_rank(process_group) if (process_group is not None and dist.is_initialized()) else 0
         self.generator = torch.Generator(device=self.device).manual_seed(int(seed) * 1000003 + rank)
