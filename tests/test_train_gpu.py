@@ -95,3 +95,41 @@ def test_fused_loss_kernel_matches_fp32(weights, teacher_ce):
     assert abs(loss.item() - ref.item()) <= 2e-2 * abs(ref.item()) + 1e-4
     gerr = ((s1.grad.float() - s2.grad).norm() / s2.grad.norm()).item()
     assert gerr < 4e-2, gerr
+
+
+@pytest.mark.parametrize("S,block,packed,hq,hkv", [(200, 4, False, 4, 2), (256, 8, True, 8, 2), (96, 16, False, 2, 2)])
+def test_block_diffusion_attention_matches_sdpa(S, block, packed, hq, hkv):
+    """Forward output and q/k/v gradients of the training attention kernels vs fp32 SDPA with the dense mask."""
+    from uno_b200.ops import cuda
+    from uno_b200.train import build_uno_batch
+    from uno_b200.train.attention import AttentionMeta, block_diffusion_attention
+
+    g = torch.Generator(device="cuda").manual_seed(S + block)
+    B = 2
+    ids = torch.randint(1, 1000, (B, S), device="cuda", generator=g)
+    pos = torch.arange(S, device="cuda").expand(B, S).clone()
+    if packed:  # two packed sequences in every row
+        pos[:, S // 2 + 8:] -= S // 2 + 8
+    ub = build_uno_batch(ids, ids.clone(), pos, block_size=block, mask_token_id=1001, generator=g)
+    vis = ub.attention_mask()
+    meta = AttentionMeta(ub.segment, ub.positions, ub.noisy, block, vis=vis)
+    T = 2 * S
+    q = torch.randn(B, T, hq, 128, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    k = torch.randn(B, T, hkv, 128, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    v = torch.randn(B, T, hkv, 128, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    dout = torch.randn(B, T, hq, 128, device="cuda", generator=g).bfloat16()
+    scale = 128 ** -0.5
+    out = block_diffusion_attention(q, k, v, meta, scale)
+    out.backward(dout)
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        qf.transpose(1, 2), kf.transpose(1, 2), vf.transpose(1, 2), attn_mask=vis[:, None], scale=scale,
+        enable_gqa=hq != hkv).transpose(1, 2)
+    ref.backward(dout.float())
+    assert cuda.error_flag() == 0
+
+    def rel(a, b):
+        return ((a.float() - b).norm() / b.norm()).item()
+
+    assert rel(out, ref) < 1e-2
+    assert rel(q.grad, qf.grad) < 3e-2 and rel(k.grad, kf.grad) < 3e-2 and rel(v.grad, vf.grad) < 3e-2

@@ -40,6 +40,13 @@ void fused_adamw_launch(const std::vector<int64_t>& ws, int64_t rank, int64_t pa
                         at::Tensor& norm_out, double lr, double beta1, double beta2, double eps, double weight_decay,
                         double max_norm, int64_t step);
 int64_t opt_ctl_bytes();
+void train_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg,
+                    const at::Tensor& pos, const at::Tensor& noisy, const at::Tensor& tiles, int64_t block,
+                    double scale, at::Tensor& out, at::Tensor& lse);
+void train_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg,
+                    const at::Tensor& pos, const at::Tensor& noisy, const at::Tensor& tiles, int64_t block,
+                    double scale, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+                    at::Tensor& delta, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv);
 void uno_loss_launch(const at::Tensor& s, const at::Tensor& t, const at::Tensor& target, bool teacher_ce,
                      const at::Tensor& ce_w, const at::Tensor& dist_w, double tv_w, double kl_w, double ce_weight,
                      at::Tensor& row_loss, at::Tensor& grad);
@@ -280,6 +287,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_adamw", &uno::fused_adamw_launch);
   m.def("opt_ctl_bytes", &uno::opt_ctl_bytes);
   m.def("uno_loss", &uno::uno_loss_launch);
+  m.def("train_attn_fwd", &uno::train_attn_fwd);
+  m.def("train_attn_bwd", &uno::train_attn_bwd);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);
   m.def("symm_close", &uno::symm_close);

@@ -80,7 +80,7 @@ def _layer(x, layer, li, lora, mask, positions, cos_sin, attn_mask, cfg):
     return x + d
 
 
-def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask):
+def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask, attn_meta=None):
     """The same layer with every projection on the tcgen05 GEMMs (``uno_b200.train.native``)."""
     from uno_b200.train.native import projection
 
@@ -100,9 +100,14 @@ def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask):
     pos = positions.reshape(-1)
     q = R.apply_rope(q.reshape(B * T, hq, hd), pos, cos_sin).reshape(B, T, hq, hd)
     k = R.apply_rope(k.reshape(B * T, hkv, hd), pos, cos_sin).reshape(B, T, hkv, hd)
-    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                       attn_mask=attn_mask[:, None], scale=attn.scale, enable_gqa=hq != hkv)
-    o = o.transpose(1, 2).reshape(B, T, hq * hd)
+    if attn_meta is not None and hd == 128:
+        from uno_b200.train.attention import block_diffusion_attention
+
+        o = block_diffusion_attention(q, k, v, attn_meta, attn.scale).reshape(B, T, hq * hd)
+    else:
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           attn_mask=attn_mask[:, None], scale=attn.scale, enable_gqa=hq != hkv)
+        o = o.transpose(1, 2).reshape(B, T, hq * hd)
     x = x + projection(o, proj["o"], mask)
     ln2 = layer.post_attention_layernorm
     h = R.rms_norm(x, ln2.weight, ln2.eps, ln2.n_groups)
@@ -114,18 +119,22 @@ def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask):
 
 def uno_hidden_states(model, lora: TrainableLoRA | None, ids: torch.Tensor, positions: torch.Tensor,
                       attn_mask: torch.Tensor, lora_rows: torch.Tensor | None,
-                      checkpoint_layers: bool = False, native: list | None = None) -> torch.Tensor:
+                      checkpoint_layers: bool = False, native: list | None = None,
+                      attn_meta=None) -> torch.Tensor:
     """Final-norm hidden states ``[B, T, H]`` for the Uno layout.
 
     ``native`` (from :func:`uno_b200.train.native.build_projections`) runs the
-    projections on the tcgen05 GEMMs; without it every op is a torch op.
+    projections on the tcgen05 GEMMs and, with ``attn_meta``
+    (:class:`uno_b200.train.attention.AttentionMeta`, head_dim 128), the
+    attention on the block-diffusion kernels; without them every op is a
+    torch op.
     """
     dec = model.model
     x = F.embedding(ids, dec.embed_tokens.weight)
     cos_sin = model.cos_sin_cache
     for li, layer in enumerate(dec.layers):
         if native is not None:
-            fn, args = _layer_native, (x, layer, native[li], lora_rows, positions, cos_sin, attn_mask)
+            fn, args = _layer_native, (x, layer, native[li], lora_rows, positions, cos_sin, attn_mask, attn_meta)
         else:
             fn, args = _layer, (x, layer, li, lora, lora_rows, positions, cos_sin, attn_mask, model.config)
         if checkpoint_layers and torch.is_grad_enabled():

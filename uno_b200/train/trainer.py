@@ -104,8 +104,14 @@ class UnoTrainer:
             for proj in self.native:
                 for p in proj.values():
                     p.refresh(self.optimizer.step_count)
-        hidden = uno_hidden_states(self.model, self.lora, ub.ids, ub.positions, ub.attention_mask(), ub.noisy,
-                                   self.checkpoint_layers, native=self.native)
+        vis = ub.attention_mask()
+        meta = None
+        if self.native is not None:
+            from uno_b200.train.attention import AttentionMeta
+
+            meta = AttentionMeta(ub.segment, ub.positions, ub.noisy, ub.block_size, vis=vis)
+        hidden = uno_hidden_states(self.model, self.lora, ub.ids, ub.positions, vis, ub.noisy,
+                                   self.checkpoint_layers, native=self.native, attn_meta=meta)
         noisy_h, clean_h = ub.gather_regions(hidden)
         H = noisy_h.shape[-1]
         supervised = labels != IGNORE_INDEX
