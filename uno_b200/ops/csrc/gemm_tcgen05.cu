@@ -414,21 +414,25 @@ __global__ void __launch_bounds__(192, 1)
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           if constexpr (mn_major<EPI>()) {
-            // [K rows][64 MN] boxes: BM / 64 for A, BN / 64 for B, 8 KB apart
-#pragma unroll
-            for (int h = 0; h < Cfg::BM / 64; ++h)
+            // [K rows][64 MN] boxes: BM / 64 for A, BN / 64 for B, 8 KB apart.  A
+            // box that would start past the matrix edge is not issued (its
+            // smem only feeds output rows / columns that are never stored).
+            const int na = min(Cfg::BM / 64, (p.M - m_blk * Cfg::BM + 63) / 64);
+            const int nb = min(BN / 64, (p.N - n_blk * BN + 63) / 64);
+            mbar_arrive_expect_tx(&full[stage], (uint32_t)(na + nb) * 8192u);
+            for (int h = 0; h < na; ++h)
               tma_load_2d(sA + stage * Cfg::A_BYTES + h * 8192, &tmA, &full[stage], m_blk * Cfg::BM + h * 64,
                           kb * Cfg::BK);
-#pragma unroll
-            for (int h = 0; h < BN / 64; ++h)
+            for (int h = 0; h < nb; ++h)
               tma_load_2d(sB + stage * Cfg::B_BYTES + h * 8192, &tmB, &full[stage], n_blk * BN + h * 64,
                           kb * Cfg::BK);
           } else if (kb < kb_main) {
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
             tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, m_blk * Cfg::BM);
             tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * Cfg::BK, n_blk * BN);
           } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
             const int k2 = (kb - kb_main) * Cfg::BK;
             tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA2, &full[stage], k2, m_blk * Cfg::BM);
             tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB2, &full[stage], k2, n_blk * BN);
