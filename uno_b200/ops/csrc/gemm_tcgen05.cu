@@ -250,13 +250,15 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, const AccSrc& 
       qkrope_head(p, src, buf, lane, row, row_ok, h * 128, n0 + h * 128);
     }
   } else if constexpr (EPI == EPI_WGRAD) {
-    if (!row_ok) return;
+    // every lane takes part in the (warp-collective) TMEM loads; only the
+    // stores of rows inside the matrix happen
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       const int col = n0 + c;
       if (col >= p.N) break;
       float v[32];
       src.load32(c, v);
+      if (!row_ok) continue;
       float* dst = p.C32 + (size_t)row * p.ldc32 + col;
       if (col + 32 <= p.N) {
 #pragma unroll
