@@ -68,9 +68,33 @@ def test_native_projections_match_torch_path():
 
 
 @pytest.mark.parametrize("weights,teacher_ce", [((1.0, 0.0, 0.0), True), ((0.3, 0.5, 0.7), True),
-                                                ((0.0, 0.0, 1.0), False)])
-def test_fused_loss_kernel_matches_fp32(weights, teacher_ce):
-    """tcgen05 logits + the fused TV/KL/CE kernel vs the fp32 torch chunks (loss and d loss / d h)."""
+                                                ((0.0, 0.0, 1.0), False), ((0.2, 1.0, 0.0), False)])
+def test_loss_kernel_matches_fp32_terms(weights, teacher_ce):
+    """The fused TV/KL/CE kernel vs the fp32 torch terms on the same bf16 logits (row losses and d/d logits)."""
+    from uno_b200.ops import cuda
+    from uno_b200.train.losses import _chunk_terms
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    N, V = 100, 5003  # V not a multiple of 8: the scalar tail runs too
+    s = (torch.randn(N, V, device="cuda", generator=g) * 2).bfloat16()
+    t = (s.float() + torch.randn(N, V, device="cuda", generator=g)).bfloat16()
+    s = torch.nn.functional.pad(s, (0, 5)).contiguous()[:, :V]  # row stride 5008 (16-byte aligned rows)
+    t = torch.nn.functional.pad(t, (0, 5)).contiguous()[:, :V]
+    tgt = torch.randint(0, V, (N,), device="cuda", generator=g)
+    ce_w = torch.rand(N, device="cuda", generator=g) + 0.5
+    dist_w = (torch.rand(N, device="cuda", generator=g) > 0.3).float()
+    row_loss = torch.empty(N, device="cuda")
+    grad = torch.empty(N, V + 5, device="cuda", dtype=torch.bfloat16)[:, :V]
+    cuda.ext().uno_loss(s, t, tgt, teacher_ce, ce_w, dist_w, *weights, row_loss, grad)
+    y = t.float().argmax(-1) if teacher_ce else tgt
+    ref_loss, ref_grad = _chunk_terms(s.float(), t.float(), y, ce_w, dist_w, weights)
+    assert cuda.error_flag() == 0
+    assert abs(row_loss.sum().item() - ref_loss.item()) <= 1e-3 * abs(ref_loss.item()) + 1e-3
+    assert ((grad.float() - ref_grad).norm() / ref_grad.norm()).item() < 1e-2
+
+
+def test_fused_head_loss_cuda_path_matches_fp32():
+    """lm_head GEMM chunks + loss kernel + d h GEMM vs the fp32 path (data-target CE: no arg-max near-ties)."""
     from uno_b200.ops import cuda
     from uno_b200.train.losses import fused_head_loss
 
@@ -83,8 +107,8 @@ def test_fused_loss_kernel_matches_fp32(weights, teacher_ce):
     ce = torch.rand(N, device="cuda", generator=g) > 0.5
     tgt = torch.randint(0, V, (N,), device="cuda", generator=g)
     scale = 1.0 + torch.rand(N, device="cuda", generator=g)
-    kw = dict(dist_mask=dist, ce_mask=ce, ce_target=tgt, ce_scale=scale, tv_weight=weights[0],
-              kl_weight=weights[1], ce_weight=weights[2], teacher_ce=teacher_ce, normalizer=int(dist.sum()), chunk=128)
+    kw = dict(dist_mask=dist, ce_mask=ce, ce_target=tgt, ce_scale=scale, tv_weight=0.0, kl_weight=0.5,
+              ce_weight=1.0, teacher_ce=False, normalizer=int(dist.sum()), chunk=128)
     s1 = s.clone().requires_grad_(True)
     loss = fused_head_loss(s1, t, w, **kw)
     loss.backward()
@@ -92,9 +116,9 @@ def test_fused_loss_kernel_matches_fp32(weights, teacher_ce):
     ref = fused_head_loss(s2, t.float(), w.float(), **kw)
     ref.backward()
     assert cuda.error_flag() == 0
-    assert abs(loss.item() - ref.item()) <= 2e-2 * abs(ref.item()) + 1e-4
+    assert abs(loss.item() - ref.item()) <= 1e-2 * abs(ref.item()) + 1e-4
     gerr = ((s1.grad.float() - s2.grad).norm() / s2.grad.norm()).item()
-    assert gerr < 4e-2, gerr
+    assert gerr < 3e-2, gerr
 
 
 @pytest.mark.parametrize("S,block,packed,hq,hkv", [(200, 4, False, 4, 2), (256, 8, True, 8, 2), (96, 16, False, 2, 2)])

@@ -96,8 +96,11 @@ def _a_grad_block(segments) -> torch.Tensor:
 
 
 class _ProjectionFn(torch.autograd.Function):
+    # The LoRA factors are passed as extra inputs only so that autograd records
+    # the op when ``x`` itself needs no gradient (the first projection sees the
+    # frozen embedding); their gradients are accumulated by the backward itself.
     @staticmethod
-    def forward(ctx, x, proj: ProjectionWeights, mask):
+    def forward(ctx, x, proj: ProjectionWeights, mask, *lora_params):
         from uno_b200.ops import cuda as C
 
         M = x.shape[0]
@@ -127,12 +130,15 @@ class _ProjectionFn(torch.autograd.Function):
         proj: ProjectionWeights = ctx.proj
         dy = dy.to(torch.bfloat16).contiguous()
         M, K = x.shape
-        dx = torch.empty(M, K, device=x.device, dtype=torch.bfloat16)
+        n_params = len(ctx.needs_input_grad) - 3
+        dx = torch.empty(M, K, device=x.device, dtype=torch.bfloat16) if ctx.needs_input_grad[0] else None
         dh = None
         if proj.segments:
             dh = torch.empty_like(h)
             C._gemm(dy, proj.bt_cat, C.EPI_ROWSCALE, c=dh, scale=proj.scale, row_mask=mask)
-        if proj.shards is None:
+        if dx is None:
+            pass
+        elif proj.shards is None:
             C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx, a2=dh, b2=proj.at_cat if dh is not None else None)
         else:
             # dx = sum over owners of dy[:, rows_j] W_j; the first block also adds dh A_cat
@@ -147,7 +153,7 @@ class _ProjectionFn(torch.autograd.Function):
             for i, seg in enumerate(proj.segments):
                 ext.gemm_wgrad(dy[:, seg.col0:seg.col0 + seg.width], h[:, i * r:(i + 1) * r], seg.B.grad, 0)
             ext.gemm_wgrad(dh, x, _a_grad_block(proj.segments), 0)
-        return dx, None, None
+        return (dx, None, None) + (None,) * n_params
 
 
 def projection(x: torch.Tensor, proj: ProjectionWeights, mask: torch.Tensor | None) -> torch.Tensor:
@@ -156,7 +162,8 @@ def projection(x: torch.Tensor, proj: ProjectionWeights, mask: torch.Tensor | No
     x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
     m = (mask.reshape(-1).float().contiguous() if mask is not None
          else torch.ones(x2.shape[0], device=x.device, dtype=torch.float32))
-    y = _ProjectionFn.apply(x2, proj, m)
+    params = [t for seg in proj.segments for t in (seg.A, seg.B)]
+    y = _ProjectionFn.apply(x2, proj, m, *params)
     return y.view(*shape[:-1], y.shape[-1])
 
 
