@@ -6,7 +6,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _setup(seed=0):
+def _setup(seed=0, head_dim=64):
     from uno_b200.models.decoder import build_model
     from uno_b200.train import LoraSettings, TrainableLoRA, build_uno_batch
     from uno_b200.train.optim import ShardedLoraAdamW
@@ -14,7 +14,7 @@ def _setup(seed=0):
     from uno_b200.utils.loader import dummy_init
 
     cfg = ModelConfig(model_type="qwen3", vocab_size=4096, hidden_size=256, intermediate_size=768,
-                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=head_dim,
                       max_position_embeddings=2048, mask_token_id=4095, rope_theta=1e6)
     torch.set_default_dtype(torch.bfloat16)
     with torch.device("cuda"):
@@ -36,18 +36,21 @@ def _setup(seed=0):
     return model, lora, opt, ub
 
 
-def _grads(native: bool):
+def _grads(native: bool, head_dim: int = 64):
+    from uno_b200.train.attention import AttentionMeta
     from uno_b200.train.forward import uno_hidden_states
     from uno_b200.train.native import build_projections
 
-    model, lora, opt, ub = _setup()
+    model, lora, opt, ub = _setup(head_dim=head_dim)
     proj = build_projections(model, lora)[0] if native else None
     if proj is not None:
         for layer in proj:
             for p in layer.values():
                 p.refresh(0)
     opt.zero_grad()
-    h = uno_hidden_states(model, lora, ub.ids, ub.positions, ub.attention_mask(), ub.noisy, native=proj)
+    vis = ub.attention_mask()
+    meta = AttentionMeta(ub.segment, ub.positions, ub.noisy, ub.block_size, vis=vis) if native else None
+    h = uno_hidden_states(model, lora, ub.ids, ub.positions, vis, ub.noisy, native=proj, attn_meta=meta)
     w = torch.randn(h.shape, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
     (h.float() * w).sum().backward()
     torch.cuda.synchronize()
@@ -56,11 +59,13 @@ def _grads(native: bool):
     return out
 
 
-def test_native_projections_match_torch_path():
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_native_projections_match_torch_path(head_dim):
+    """head_dim 128 also runs the block-diffusion attention kernels inside the training forward/backward."""
     from uno_b200.ops import cuda
 
-    g_ref, h_ref = _grads(native=False)
-    g_nat, h_nat = _grads(native=True)
+    g_ref, h_ref = _grads(native=False, head_dim=head_dim)
+    g_nat, h_nat = _grads(native=True, head_dim=head_dim)
     assert cuda.error_flag() == 0
     assert ((h_nat - h_ref).norm() / h_ref.norm()).item() < 2e-2
     rel = ((g_nat - g_ref).norm() / g_ref.norm()).item()
