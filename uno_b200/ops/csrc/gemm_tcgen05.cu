@@ -957,11 +957,17 @@ void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, i
   const int t128 = ((M + 127) / 128) * ((N + 127) / 128);
   const bool narrow_rows = M <= 128 && N > 256;
   const bool mid = M > 128 && N > 256 && t128 <= sms;
+  // ... except a long K loop (down_proj, K = 12288), where two K splits of
+  // CTA-pair 256x256 tiles beat one wave of 128x128 tiles (64 -> 53 us at
+  // 512 x 4096 x 12288)
+  const bool mid_long_k = mid && K >= 6144 && M >= 256 && pair_enabled();
   int tile;
   if (forced_bn) {
     tile = forced_bn;
   } else if (narrow_rows) {
     tile = (!wide_epi && K <= 4096) ? 64 : 128;
+  } else if (mid_long_k) {
+    tile = 256;
   } else if (mid) {
     tile = 128;
   } else {
@@ -975,6 +981,8 @@ void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, i
   } else if (!forced_bn && narrow_rows) {
     const int tiles = (N + tile - 1) / tile;
     s = std::max(1, std::min({4, (128 + tiles / 2) / tiles, kb / 16}));
+  } else if (!forced_bn && mid_long_k) {
+    s = 2;
   } else if (!forced_bn && mid) {
     s = t128 * 2 >= sms ? 1 : std::max(1, std::min({4, (128 + t128 / 2) / t128, kb / 16}));
   } else {
