@@ -176,8 +176,7 @@ def run_native(args):
         llm.step()  # prefill (unchunked) until every request is admitted
     for _ in range(args.warmup):
         llm.step()
-    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out", "bench_clocks.csv") if os.path.isdir(
-        os.path.join(ROOT, "gpurun_out")) else "/tmp/bench_clocks.csv")
+    clocks = ClockSampler(os.environ.get("UNO_BENCH_CLOCKS_CSV", "/tmp/bench_clocks.csv"))
     clocks.start()
     llm.call("timer_start")
     tokens = 0
