@@ -69,41 +69,9 @@ __global__ void __launch_bounds__(SAMPLE_THREADS)
   const __nv_bfloat16* c = clean + cm_.off(r);
   const __nv_bfloat16* d = draft + dm_.off(r);
   const int nvec = V / 8;
-  // pass 1: max of both rows, then sums
-  float cm = -INFINITY, dm = -INFINITY;
-  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-    float a[8], b[8];
-    load8(c + k * 8, a);
-    load8(d + k * 8, b);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      cm = fmaxf(cm, a[i]);
-      dm = fmaxf(dm, b[i]);
-    }
-  }
-  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
-    cm = fmaxf(cm, __bfloat162float(c[i]));
-    dm = fmaxf(dm, __bfloat162float(d[i]));
-  }
-  cm = block_max(cm) * inv_temp;
-  dm = block_max(dm) * inv_temp;
-  float cs = 0.f, ds = 0.f;
-  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-    float a[8], b[8];
-    load8(c + k * 8, a);
-    load8(d + k * 8, b);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      cs += __expf(a[i] * inv_temp - cm);
-      ds += __expf(b[i] * inv_temp - dm);
-    }
-  }
-  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
-    cs += __expf(__bfloat162float(c[i]) * inv_temp - cm);
-    ds += __expf(__bfloat162float(d[i]) * inv_temp - dm);
-  }
-  cs = block_sum(cs);
-  ds = block_sum(ds);
+  // pass 1: softmax statistics of both rows (one read of each)
+  float cm, cs, dm, ds;
+  row_stats2(c, d, V, inv_temp, cm, cs, dm, ds);
   const int64_t s = spec[r];
   const float ps = __expf(__bfloat162float(c[s]) * inv_temp - cm) / cs;
   const float qs = __expf(__bfloat162float(d[s]) * inv_temp - dm) / ds;

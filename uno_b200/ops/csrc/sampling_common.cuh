@@ -120,6 +120,86 @@ __device__ __forceinline__ float gumbel1(uint32_t seed, uint32_t offset, uint32_
   return -__logf(-__logf(u01(bits[v & 3])));
 }
 
+struct MaxSum {
+  float m, s;
+};
+
+__device__ __forceinline__ MaxSum ms_merge(MaxSum a, MaxSum b) {
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return {m, 0.f};
+  return {m, a.s * __expf(a.m - m) + b.s * __expf(b.m - m)};
+}
+
+static __device__ MaxSum block_maxsum(MaxSum v) {
+  __shared__ float sm[32], ss[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MaxSum w{__shfl_xor_sync(0xffffffff, v.m, o), __shfl_xor_sync(0xffffffff, v.s, o)};
+    v = ms_merge(v, w);
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sm[warp] = v.m;
+    ss[warp] = v.s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    MaxSum w{-INFINITY, 0.f};
+    if (lane < (int)(blockDim.x >> 5)) w = MaxSum{sm[lane], ss[lane]};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      MaxSum u{__shfl_xor_sync(0xffffffff, w.m, o), __shfl_xor_sync(0xffffffff, w.s, o)};
+      w = ms_merge(w, u);
+    }
+    if (lane == 0) {
+      sm[0] = w.m;
+      ss[0] = w.s;
+    }
+  }
+  __syncthreads();
+  return {sm[0], ss[0]};
+}
+
+// Softmax statistics of two rows in ONE pass: (max, sum exp(x * inv_temp - max))
+// of each, merged online per 8-wide vector and then across the block.
+static __device__ void row_stats2(const __nv_bfloat16* c, const __nv_bfloat16* d, int n, float inv_temp, float& cm,
+                                  float& cs, float& dm, float& ds) {
+  MaxSum a{-INFINITY, 0.f}, b{-INFINITY, 0.f};
+  const int nvec = n / 8;
+  for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+    float x[8], y[8];
+    load8(c + k * 8, x);
+    load8(d + k * 8, y);
+    float mx = x[0] * inv_temp, my = y[0] * inv_temp;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x[i] *= inv_temp;
+      y[i] *= inv_temp;
+      mx = fmaxf(mx, x[i]);
+      my = fmaxf(my, y[i]);
+    }
+    float sx = 0.f, sy = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sx += __expf(x[i] - mx);
+      sy += __expf(y[i] - my);
+    }
+    a = ms_merge(a, MaxSum{mx, sx});
+    b = ms_merge(b, MaxSum{my, sy});
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x) {
+    a = ms_merge(a, MaxSum{__bfloat162float(c[i]) * inv_temp, 1.f});
+    b = ms_merge(b, MaxSum{__bfloat162float(d[i]) * inv_temp, 1.f});
+  }
+  a = block_maxsum(a);
+  b = block_maxsum(b);
+  cm = a.m;
+  cs = a.s;
+  dm = b.m;
+  ds = b.s;
+}
+
 // ------------------------------------------------------------------- host
 // 2-D [rows, V] or 3-D [groups, rpg, V] logits with unit stride along V.
 static inline RowMap row_map(const at::Tensor& x, int& rows, int& V) {

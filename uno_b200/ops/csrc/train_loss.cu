@@ -26,47 +26,6 @@ namespace uno {
 
 constexpr int LOSS_THREADS = 512;
 
-struct MaxSum {
-  float m, s;
-};
-
-__device__ __forceinline__ MaxSum ms_merge(MaxSum a, MaxSum b) {
-  const float m = fmaxf(a.m, b.m);
-  if (m == -INFINITY) return {m, 0.f};
-  return {m, a.s * __expf(a.m - m) + b.s * __expf(b.m - m)};
-}
-
-__device__ MaxSum block_maxsum(MaxSum v) {
-  __shared__ float sm[32], ss[32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    MaxSum w{__shfl_xor_sync(0xffffffff, v.m, o), __shfl_xor_sync(0xffffffff, v.s, o)};
-    v = ms_merge(v, w);
-  }
-  __syncthreads();
-  if (lane == 0) {
-    sm[warp] = v.m;
-    ss[warp] = v.s;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    MaxSum w{-INFINITY, 0.f};
-    if (lane < (int)(blockDim.x >> 5)) w = MaxSum{sm[lane], ss[lane]};
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      MaxSum u{__shfl_xor_sync(0xffffffff, w.m, o), __shfl_xor_sync(0xffffffff, w.s, o)};
-      w = ms_merge(w, u);
-    }
-    if (lane == 0) {
-      sm[0] = w.m;
-      ss[0] = w.s;
-    }
-  }
-  __syncthreads();
-  return {sm[0], ss[0]};
-}
-
 __global__ void __launch_bounds__(LOSS_THREADS)
     uno_loss_kernel(const __nv_bfloat16* __restrict__ s, int64_t lds, const __nv_bfloat16* __restrict__ t, int64_t ldt,
                     int V, const int64_t* __restrict__ target, int teacher_ce, const float* __restrict__ ce_w,

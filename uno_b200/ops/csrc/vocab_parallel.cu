@@ -205,40 +205,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS)
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const __nv_bfloat16* c = clean + cmap.off(r);
     const __nv_bfloat16* d = draft + dmap.off(r);
-    float cm = -INFINITY, dm = -INFINITY;
-    for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-      float a[8], b[8];
-      load8(c + k * 8, a);
-      load8(d + k * 8, b);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        cm = fmaxf(cm, a[i]);
-        dm = fmaxf(dm, b[i]);
-      }
-    }
-    for (int i = nvec * 8 + threadIdx.x; i < Vs; i += blockDim.x) {
-      cm = fmaxf(cm, __bfloat162float(c[i]));
-      dm = fmaxf(dm, __bfloat162float(d[i]));
-    }
-    cm = block_max(cm) * inv_temp;
-    dm = block_max(dm) * inv_temp;
-    float cs = 0.f, ds = 0.f;
-    for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-      float a[8], b[8];
-      load8(c + k * 8, a);
-      load8(d + k * 8, b);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        cs += __expf(a[i] * inv_temp - cm);
-        ds += __expf(b[i] * inv_temp - dm);
-      }
-    }
-    for (int i = nvec * 8 + threadIdx.x; i < Vs; i += blockDim.x) {
-      cs += __expf(__bfloat162float(c[i]) * inv_temp - cm);
-      ds += __expf(__bfloat162float(d[i]) * inv_temp - dm);
-    }
-    cs = block_sum(cs);
-    ds = block_sum(ds);
+    float cm, cs, dm, ds;
+    row_stats2(c, d, Vs, inv_temp, cm, cs, dm, ds);
     if (threadIdx.x == 0) {
       const int64_t s = spec[r] - p.vstart;
       const bool mine = s >= 0 && s < Vs;
