@@ -12,7 +12,7 @@ alone, and the sampling case alternates two 156 MB logit blocks.
 
 Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden),
 ``lm-head``, ``decode-attention``, ``sampling`` (full-vocab verify and one
-vocab-parallel shard).
+vocab-parallel shard), ``train-attention`` (block-diffusion forward / backward).
 """
 
 from __future__ import annotations
@@ -129,8 +129,47 @@ def _decode_attention():
             (lambda i: C.attention(q, kc, vc, meta, 128 ** -0.5), 0, kv_bytes)}
 
 
+def _train_attention():
+    """Training attention (block-diffusion mask) of one 4,096-token sequence: 8,192 laid-out tokens,
+    32 query / 8 KV heads of 128, diffusion block 8.  Forward and backward are timed separately."""
+    from uno_b200.ops import cuda as C
+    from uno_b200.train import build_uno_batch
+    from uno_b200.train.attention import AttentionMeta
+
+    S, hq, hkv, D = 4096, 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ids = torch.randint(1, 1000, (1, S), device="cuda", generator=g)
+    ub = build_uno_batch(ids, ids.clone(), torch.arange(S, device="cuda")[None], block_size=8, mask_token_id=1001,
+                         generator=g)
+    vis = ub.attention_mask()
+    meta = AttentionMeta(ub.segment, ub.positions, ub.noisy, 8, vis=vis)
+    pairs = int(vis.sum())
+    T = 2 * S
+    q = torch.randn(1, T, hq, D, device="cuda").bfloat16()
+    k = torch.randn(1, T, hkv, D, device="cuda").bfloat16()
+    v = torch.randn(1, T, hkv, D, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    lse = torch.empty(1, hq, T, device="cuda")
+    dout = torch.randn_like(q)
+    delta = torch.empty_like(lse)
+    dq = torch.zeros(q.shape, device="cuda")
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    ext = C.ext()
+    args = (meta.seg, meta.pos, meta.noisy, meta.tiles, 8, D ** -0.5)
+
+    def fwd(i):
+        ext.train_attn_fwd(q, k, v, *args, out, lse)
+
+    def bwd(i):
+        ext.train_attn_bwd(q, k, v, *args, out, dout, lse, delta, dq, dk, dv)
+
+    fwd(0)
+    return {f"train_attn_fwd T={T} hq={hq} hkv={hkv} visible={pairs / T / T:.3f}": (fwd, 4 * D * pairs * hq, 0),
+            f"train_attn_bwd T={T} hq={hq} hkv={hkv}": (bwd, 10 * D * pairs * hq, 0)}
+
+
 CASES = {"layer-gemms": _layer_gemms, "lm-head": _lm_head, "decode-attention": _decode_attention,
-         "sampling": _sampling}
+         "sampling": _sampling, "train-attention": _train_attention}
 
 
 def main(argv=None):
