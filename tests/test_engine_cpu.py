@@ -119,3 +119,55 @@ def test_data_parallel_replicas_cpu():
     llm.exit()
     assert len(out) == 5 and all(len(o["token_ids"]) >= 10 for o in out)
     assert st["forwards"] > 0
+
+
+def test_block_fp8_checkpoint_loads_dequantized(tmp_path):
+    """A block-FP8 checkpoint (128x128 weight blocks + scale_inv) loads as its dequantized weights."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from uno_b200.models.decoder import build_model
+    from uno_b200.utils.hf_compat import model_config_from_dict
+    from uno_b200.parallel.state import set_tp_state
+    from uno_b200.utils.loader import dummy_init, load_model
+
+    set_tp_state(0, 1)  # single-rank shapes, whatever an earlier test left behind
+    raw = dict(model_type="qwen3", vocab_size=512, hidden_size=256, intermediate_size=768, num_hidden_layers=1,
+               num_attention_heads=4, num_key_value_heads=2, head_dim=64, eos_token_id=1, torch_dtype="float32")
+    cfg = model_config_from_dict(raw)
+    src = build_model(cfg)
+    dummy_init(src, seed=3, std=0.05)
+    sd = src.state_dict()
+    hf = {n: t.contiguous() for n, t in sd.items() if "qkv_proj" not in n and "gate_up_proj" not in n}
+    pre = "model.layers.0."
+    qkv, gu = sd[pre + "self_attn.qkv_proj.weight"], sd[pre + "mlp.gate_up_proj.weight"]
+    hf[pre + "self_attn.q_proj.weight"], hf[pre + "self_attn.k_proj.weight"], hf[pre + "self_attn.v_proj.weight"] = \
+        qkv[:256].clone(), qkv[256:384].clone(), qkv[384:].clone()
+    hf[pre + "mlp.gate_proj.weight"], hf[pre + "mlp.up_proj.weight"] = gu[:768].clone(), gu[768:].clone()
+
+    def up(s):
+        return s.repeat_interleave(128, 0).repeat_interleave(128, 1)
+
+    deq = {}
+    for name in [n for n in hf if n.endswith("_proj.weight")]:
+        w = hf[name].float()
+        scale = w.view(w.shape[0] // 128, 128, w.shape[1] // 128, 128).abs().amax(dim=(1, 3)).clamp_min(1e-8) / 448.0
+        q = (w / up(scale)).to(torch.float8_e4m3fn)
+        hf[name], hf[name + "_scale_inv"] = q, scale
+        deq[name] = q.float() * up(scale)
+    d = tmp_path / "fp8"
+    d.mkdir()
+    save_file(hf, str(d / "model.safetensors"))
+    (d / "config.json").write_text(json.dumps(dict(raw, quantization_config={
+        "quant_method": "fp8", "weight_block_size": [128, 128], "activation_scheme": "dynamic"})))
+    dst = build_model(cfg)
+    load_model(dst, str(d))
+    got = dst.state_dict()
+    want_qkv = torch.cat([deq[pre + f"self_attn.{x}_proj.weight"] for x in "qkv"])
+    want_gu = torch.cat([deq[pre + "mlp.gate_proj.weight"], deq[pre + "mlp.up_proj.weight"]])
+    assert torch.allclose(got[pre + "self_attn.qkv_proj.weight"], want_qkv)
+    assert torch.allclose(got[pre + "mlp.gate_up_proj.weight"], want_gu)
+    assert torch.allclose(got[pre + "mlp.down_proj.weight"], deq[pre + "mlp.down_proj.weight"])
+    # quantisation error stays at the fp8 level
+    assert ((want_qkv - qkv).abs().max() / qkv.abs().max()).item() < 0.07

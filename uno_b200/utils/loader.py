@@ -42,17 +42,67 @@ def iter_checkpoint(path: str):
                 yield key, value
 
 
+FP8_BLOCK = 128
+
+
+def quantization_config(path: str) -> dict | None:
+    """The checkpoint's ``quantization_config`` (``config.json``), validated; None when unquantized.
+
+    Supported: ``quant_method: fp8`` with ``weight_block_size: [128, 128]`` and dynamic activations
+    (the registry of ``nano_vllm_uno/layers/quantization.py:79-150``)."""
+    import json
+
+    cfg_path = os.path.join(path, "config.json")
+    if not os.path.isfile(cfg_path):
+        return None
+    with open(cfg_path, encoding="utf-8") as fh:
+        q = json.load(fh).get("quantization_config")
+    if not q:
+        return None
+    method = q.get("quant_method")
+    if method != "fp8":
+        raise ValueError(f"unsupported quantization method {method!r} (registered: fp8)")
+    if list(q.get("weight_block_size") or []) != [FP8_BLOCK, FP8_BLOCK]:
+        raise ValueError("block FP8 checkpoints need weight_block_size=[128, 128]")
+    if q.get("activation_scheme", "dynamic") != "dynamic":
+        raise ValueError("block FP8 checkpoints need activation_scheme='dynamic'")
+    return q
+
+
+def dequantize_block_fp8(weight: torch.Tensor, scale_inv: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """``W[n, k] = fp8[n, k] * scale_inv[n // 128, k // 128]`` (128 x 128 weight blocks)."""
+    N, K = weight.shape
+    if N % FP8_BLOCK or K % FP8_BLOCK or scale_inv.shape != (N // FP8_BLOCK, K // FP8_BLOCK):
+        raise ValueError(f"block FP8 weight {tuple(weight.shape)} does not match scales {tuple(scale_inv.shape)}")
+    s = scale_inv.float().repeat_interleave(FP8_BLOCK, 0).repeat_interleave(FP8_BLOCK, 1)
+    return (weight.float() * s).to(dtype)
+
+
 def load_model(model: nn.Module, path: str) -> int:
-    """Load every tensor of the checkpoint at ``path``; returns the count loaded."""
+    """Load every tensor of the checkpoint at ``path``; returns the count loaded.
+
+    Block-FP8 checkpoints (``quantization_config.quant_method == "fp8"``) are
+    dequantized to the model's dtype while loading: every ``*.weight`` stored
+    as float8_e4m3 is multiplied by its ``*.weight_scale_inv`` blocks, then
+    goes through the usual packing and tensor-parallel slicing, and the
+    projections run on the bf16 kernels."""
     if not os.path.isdir(path):
         raise ValueError(f"load_model: not a directory: {path}")
     if not _checkpoint_files(path):
         raise FileNotFoundError(f"no *.safetensors or *.bin files in {path}")
     mapping = getattr(model, "packed_modules_mapping", {})
+    scales = {}
+    if quantization_config(path) is not None:
+        scales = {name[: -len("_scale_inv")]: t for name, t in iter_checkpoint(path)
+                  if name.endswith(".weight_scale_inv")}
     loaded = 0
     for name, tensor in iter_checkpoint(path):
-        if name.endswith("rotary_emb.inv_freq"):
+        if name.endswith("rotary_emb.inv_freq") or name.endswith(".weight_scale_inv"):
             continue
+        if tensor.dtype == torch.float8_e4m3fn:
+            if name not in scales:
+                raise ValueError(f"{name} is float8 but the checkpoint has no {name}_scale_inv")
+            tensor = dequantize_block_fp8(tensor, scales[name], dtype=torch.float32)  # cast by the copy
         if name == "lm_head.weight" and model.config.tie_word_embeddings:
             continue
         for short, (packed, shard_id) in mapping.items():
