@@ -56,7 +56,17 @@ def parse():
     ap.add_argument("--e2e-tokens", type=int, default=0, help="override new tokens for the e2e run")
     ap.add_argument("--sampler", default="linear", choices=["linear", "tree"],
                     help="tree: BASELINE config 3 (64-node tree of depth 8, per-request tok/s; default batch 1)")
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "uno-0.9b-dp"],
+                    help="uno-0.9b-dp: BASELINE config 4 (0.9B dense model, one data-parallel replica per GPU, "
+                         "256 requests per replica, prompts U[64,512], 1024 new tokens, block 16, LoRA rank 32)")
     args = ap.parse_args()
+    if args.config == "uno-0.9b-dp":
+        if args.batch == 64:
+            args.batch = 256
+        if args.block == 8:
+            args.block = 16
+        if args.new_tokens == 2048:
+            args.new_tokens = 1024
     if args.sampler == "tree":
         # config 3: prompt 512 Zipf ids, 4096 new tokens, depth 8 (block 9), 64 nodes, top-4 candidates
         if args.batch == 64:
@@ -68,10 +78,11 @@ def parse():
     return args
 
 
-def make_prompts(batch: int, seed: int, fixed_len: int | None = None) -> list[list[int]]:
+def make_prompts(batch: int, seed: int, fixed_len: int | None = None, lo: int = 128,
+                 hi: int = 1024) -> list[list[int]]:
     rng = np.random.default_rng(seed)
     perm = rng.permutation(VOCAB - 2) + 1
-    lens = rng.integers(128, 1025, size=batch) if fixed_len is None else np.full(batch, fixed_len)
+    lens = rng.integers(lo, hi + 1, size=batch) if fixed_len is None else np.full(batch, fixed_len)
     prompts = []
     for n in lens:
         ranks = rng.zipf(1.1, size=int(n)) - 1
@@ -128,7 +139,8 @@ class ClockSampler:
 
 
 def engine_kwargs(args, tp: int) -> dict:
-    ladder = list(range(1, 9)) + list(range(10, 33, 2)) + list(range(40, 65, 4))
+    ladder = list(range(1, 9)) + list(range(10, 33, 2)) + list(range(40, 65, 4)) + list(range(80, 257, 16))
+    dp = getattr(args, "config", "qwen3-8b") == "uno-0.9b-dp"
     return dict(
         tensor_parallel_size=tp,
         max_num_seqs=args.batch,
@@ -138,16 +150,118 @@ def engine_kwargs(args, tp: int) -> dict:
         max_diffusion_block_size=args.block,
         cuda_graph_block_sizes=sorted({1, args.block}),
         cuda_graph_batch_sizes=[b for b in ladder if b <= args.batch],
-        dummy_lora_rank=64,
-        dummy_lora_alpha=128.0,
+        dummy_lora_rank=32 if dp else 64,
+        dummy_lora_alpha=64.0 if dp else 128.0,
         gpu_memory_utilization=0.90,
         seed=args.seed,
     ) | ({"tree_verify_size": 64, "tree_candidate_top_k": 4} if getattr(args, "sampler", "linear") == "tree" else {})
 
 
+def run_dp_replicas(args):
+    """one independent 0.9B replica per GPU (weak scaling over N replicas).
+
+    Every rank times ``--steps`` steps of its own replica with CUDA events; the
+    job's value is the sum of the committed tokens over the slowest rank's time
+    (max over ranks), gathered over a gloo group."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo")
+    sys.path.insert(0, ROOT)
+    from uno_b200 import LLM, SamplingParams
+
+    llm = LLM("preset:uno-0.9b", **engine_kwargs(args, 1))
+    sp = SamplingParams(temperature=1.0, max_tokens=args.new_tokens, diffusion_block_size=args.block,
+                        mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed + rank)
+    prompts = make_prompts(args.batch, args.seed + 1000 * rank, None, 64, 512)
+    for p in prompts:
+        llm.add_request(p, sp)
+    while llm.scheduler.waiting:
+        llm.step()
+    for _ in range(args.warmup):
+        llm.step()
+    clocks = ClockSampler(os.environ.get("UNO_BENCH_CLOCKS_CSV", "/tmp/bench_clocks.csv"))
+    if world > 1:
+        dist.barrier()
+    clocks.start()
+    llm.call("timer_start")
+    tokens = 0
+    stats0 = {k: sum(s.stats[k] for s in llm.scheduler.running) for k in ("forwards", "accepts")}
+    for _ in range(args.steps):
+        _, n = llm.step()
+        tokens += -n
+    ms = llm.call("timer_stop")
+    clock_info = clocks.stop()
+    stats1 = {k: sum(s.stats[k] for s in llm.scheduler.running) for k in ("forwards", "accepts")}
+    running = len(llm.scheduler.running)
+    launches = count_launches(llm)
+    t = torch.tensor([float(tokens), ms], dtype=torch.float64)
+    if world > 1:
+        tot = t.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tokens_all, ms_max = float(tot[0]), float(mx[1])
+    else:
+        tokens_all, ms_max = float(tokens), ms
+    e2e = None
+    if not args.no_e2e:
+        while not llm.is_finished():
+            llm.step()
+        sp2 = SamplingParams(temperature=1.0, max_tokens=args.e2e_tokens or args.new_tokens,
+                             diffusion_block_size=args.block, mask_token_id=MASK_ID, ignore_eos=True,
+                             seed=args.seed + 7 + rank)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        outs = llm.generate(prompts, sp2, use_tqdm=False, detokenize=False)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        e2 = torch.tensor([float(sum(len(o["token_ids"]) for o in outs)), dt], dtype=torch.float64)
+        if world > 1:
+            s2 = e2.clone()
+            dist.all_reduce(s2, op=dist.ReduceOp.SUM)
+            m2 = e2.clone()
+            dist.all_reduce(m2, op=dist.ReduceOp.MAX)
+            e2 = torch.tensor([float(s2[0]), float(m2[1])], dtype=torch.float64)
+        ws = llm.model_runner.workspace
+        e2e = {"value": float(e2[0]) / float(e2[1]), "unit": "tok/s", "seconds": float(e2[1]),
+               "output_tokens": int(e2[0]),
+               "h2d_bytes_per_step": int(ws.host64.numel() * 8 + ws.host32.numel() * 4) * 2 + args.batch * args.block * 4,
+               "d2h_bytes_per_step": args.batch * (args.block + 2) * 8, "api": "uno_b200.LLM.generate"}
+    if rank == 0:
+        line = {
+            "metric": "Uno 0.9B-class Psi-Spec system output tok/s, data-parallel replicas (config 4)",
+            "value": tokens_all / (ms_max / 1e3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, Zipf(1.1) prompt ids)",
+            "config": {"model": "uno-0.9b (16 layers, hidden 2048, 16 heads, SwiGLU 5632) + rank-32 gated LoRA",
+                       "global_batch": args.batch * world, "seq_len": "prompt U[64,512] + 1024 new",
+                       "block_size": args.block, "sampler": "linear Psi-Spec, T=1.0", "kv_page": 256,
+                       "parallelism": f"dp{world}", "running_requests_rank0": running,
+                       "l2": "working set > L2 (1.8 GB weights + KV per step)"},
+            "tpf": (stats1["accepts"] - stats0["accepts"]) / max(1, stats1["forwards"] - stats0["forwards"]),
+            "clocks": clock_info, "e2e": e2e,
+            "gpu_launches": launches * args.steps if launches is not None else None, "impl": "native",
+        }
+        print(json.dumps(line), flush=True)
+    llm.exit()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_native(args):
     import torch
 
+    if args.config == "uno-0.9b-dp":
+        return run_dp_replicas(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world != args.gpus:
@@ -268,6 +382,11 @@ def count_launches(llm):
 
 
 def run_reference(args):
+    if args.config != "qwen3-8b":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is wired for the "
+                              "Qwen3-8B headline configs only"}), flush=True)
+        return
     if args.sampler == "tree":
         # The reference tree sampler requires attention_backend fa3 or fa4 (its config.py:134-138):
         # FA3 (flash_attn_interface / sgl_kernel) is Hopper-only and FA4 comes with SGLang; neither
