@@ -162,3 +162,32 @@ def test_block_diffusion_attention_matches_sdpa(S, block, packed, hq, hkv):
 
     assert rel(out, ref) < 1e-2
     assert rel(q.grad, qf.grad) < 3e-2 and rel(k.grad, kf.grad) < 3e-2 and rel(v.grad, vf.grad) < 3e-2
+
+
+@pytest.mark.parametrize("groups", [1, 4])
+def test_training_rmsnorm_and_silu_kernels_match_torch(groups):
+    """Fused RMSNorm / SiLU*up forward and backward vs torch autograd of the fp32-statistics formulation."""
+    from uno_b200.ops import reference as R
+    from uno_b200.train.native import rms_norm, silu_mul
+
+    g = torch.Generator(device="cuda").manual_seed(groups)
+    x = (torch.randn(300, 1024, device="cuda", generator=g) * 2).bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(1024, device="cuda", generator=g)).bfloat16()
+    dy = torch.randn(300, 1024, device="cuda", generator=g).bfloat16()
+    y = rms_norm(x, w, 1e-6, groups)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_(True)
+    yr = R.rms_norm(xr, w.float(), 1e-6, groups)
+    yr.backward(dy.float())
+    assert ((y.float() - yr).norm() / yr.norm()).item() < 1e-2
+    assert ((x.grad.float() - xr.grad).norm() / xr.grad.norm()).item() < 1e-2
+
+    gu = torch.randn(300, 2 * 768, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    da = torch.randn(300, 768, device="cuda", generator=g).bfloat16()
+    a = silu_mul(gu)
+    a.backward(da)
+    gr = gu.detach().float().requires_grad_(True)
+    ar = torch.nn.functional.silu(gr[:, :768]) * gr[:, 768:]
+    ar.backward(da.float())
+    assert ((a.float() - ar).norm() / ar.norm()).item() < 1e-2
+    assert ((gu.grad.float() - gr.grad).norm() / gr.grad.norm()).item() < 1e-2

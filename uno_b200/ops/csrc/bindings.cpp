@@ -40,6 +40,12 @@ void fused_adamw_launch(const std::vector<int64_t>& ws, int64_t rank, int64_t pa
                         at::Tensor& norm_out, double lr, double beta1, double beta2, double eps, double weight_decay,
                         double max_norm, int64_t step);
 int64_t opt_ctl_bytes();
+void rmsnorm_fwd_train(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps,
+                       int64_t groups);
+void rmsnorm_bwd_train(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                       at::Tensor& dx, int64_t groups);
+void silu_mul_fwd(const at::Tensor& gu, at::Tensor& a);
+void silu_mul_bwd(const at::Tensor& da, const at::Tensor& gu, at::Tensor& dgu);
 void train_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg,
                     const at::Tensor& pos, const at::Tensor& noisy, const at::Tensor& tiles, int64_t block,
                     double scale, at::Tensor& out, at::Tensor& lse);
@@ -288,6 +294,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("opt_ctl_bytes", &uno::opt_ctl_bytes);
   m.def("uno_loss", &uno::uno_loss_launch);
   m.def("train_attn_fwd", &uno::train_attn_fwd);
+  m.def("rmsnorm_fwd_train", &uno::rmsnorm_fwd_train);
+  m.def("rmsnorm_bwd_train", &uno::rmsnorm_bwd_train);
+  m.def("silu_mul_fwd", &uno::silu_mul_fwd);
+  m.def("silu_mul_bwd", &uno::silu_mul_bwd);
   m.def("train_attn_bwd", &uno::train_attn_bwd);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);

@@ -82,13 +82,13 @@ def _layer(x, layer, li, lora, mask, positions, cos_sin, attn_mask, cfg):
 
 def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask, attn_meta=None):
     """The same layer with every projection on the tcgen05 GEMMs (``uno_b200.train.native``)."""
-    from uno_b200.train.native import projection
+    from uno_b200.train.native import projection, rms_norm, silu_mul
 
     B, T, H = x.shape
     attn = layer.self_attn
     hq, hkv, hd = attn.num_heads, attn.num_kv_heads, attn.head_dim
     ln1 = layer.input_layernorm
-    h = R.rms_norm(x, ln1.weight, ln1.eps, ln1.n_groups)
+    h = rms_norm(x, ln1.weight, ln1.eps, ln1.n_groups)
     qkv = projection(h, proj["qkv"], mask)
     q_end, k_end = hq * hd, (hq + hkv) * hd
     q = qkv[..., :q_end].reshape(B, T, hq, hd)
@@ -110,10 +110,8 @@ def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask, attn_meta
         o = o.transpose(1, 2).reshape(B, T, hq * hd)
     x = x + projection(o, proj["o"], mask)
     ln2 = layer.post_attention_layernorm
-    h = R.rms_norm(x, ln2.weight, ln2.eps, ln2.n_groups)
-    gu = projection(h, proj["gate_up"], mask)
-    inter = gu.shape[-1] // 2
-    a = F.silu(gu[..., :inter]) * gu[..., inter:]
+    h = rms_norm(x, ln2.weight, ln2.eps, ln2.n_groups)
+    a = silu_mul(projection(h, proj["gate_up"], mask))
     return x + projection(a, proj["down"], mask)
 
 
@@ -142,4 +140,8 @@ def uno_hidden_states(model, lora: TrainableLoRA | None, ids: torch.Tensor, posi
         else:
             x = fn(*args)
     norm = dec.norm
+    if native is not None:
+        from uno_b200.train.native import rms_norm
+
+        return rms_norm(x, norm.weight, norm.eps, norm.n_groups)
     return R.rms_norm(x, norm.weight, norm.eps, norm.n_groups)

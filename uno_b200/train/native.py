@@ -218,3 +218,61 @@ def build_projections(model, lora, group=None, fsdp: bool = False):
                                    shards=sharded.shards(f"{li}.{name}"), out_features=N, in_features=K)
         layers[li][name] = pw
     return layers, sharded
+
+
+# ------------------------------------------------------------ elementwise ops
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps: float, groups: int):
+        from uno_b200.ops.cuda import ext
+
+        x = x.to(torch.bfloat16).contiguous()
+        H = x.shape[-1]
+        y = torch.empty_like(x)
+        rstd = torch.empty(x.numel() // H * groups, device=x.device, dtype=torch.float32)
+        w = weight.detach().to(torch.bfloat16).contiguous()
+        ext().rmsnorm_fwd_train(x, w, y, rstd, float(eps), int(groups))
+        ctx.save_for_backward(x, w, rstd)
+        ctx.groups = int(groups)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from uno_b200.ops.cuda import ext
+
+        x, w, rstd = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        dx = torch.empty_like(x)
+        ext().rmsnorm_bwd_train(dy, x, w, rstd, dx, ctx.groups)
+        return dx, None, None, None
+
+
+class _SiluMulFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        from uno_b200.ops.cuda import ext
+
+        gu = gu.to(torch.bfloat16).contiguous()
+        a = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, device=gu.device, dtype=torch.bfloat16)
+        ext().silu_mul_fwd(gu, a)
+        ctx.save_for_backward(gu)
+        return a
+
+    @staticmethod
+    def backward(ctx, da):
+        from uno_b200.ops.cuda import ext
+
+        (gu,) = ctx.saved_tensors
+        dgu = torch.empty_like(gu)
+        ext().silu_mul_bwd(da.to(torch.bfloat16).contiguous(), gu, dgu)
+        return dgu
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, groups: int = 1) -> torch.Tensor:
+    """RMSNorm (fp32 statistics, frozen weight) with a fused backward kernel."""
+    return _RMSNormFn.apply(x, weight, eps, groups)
+
+
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` of ``[..., 2I] = [gate | up]`` with a fused backward kernel."""
+    return _SiluMulFn.apply(gu)
