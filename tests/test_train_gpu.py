@@ -191,3 +191,31 @@ def test_training_rmsnorm_and_silu_kernels_match_torch(groups):
     ar.backward(da.float())
     assert ((a.float() - ar).norm() / ar.norm()).item() < 1e-2
     assert ((gu.grad.float() - gr.grad).norm() / gr.grad.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("norm", [True, False])
+def test_training_qk_norm_rope_kernel_matches_torch(norm):
+    """Fused per-head RMSNorm + NeoX RoPE (forward and backward) on a column slice of a fused qkv output."""
+    from uno_b200.layers.rotary import cos_sin_cache
+    from uno_b200.ops import reference as R
+    from uno_b200.train.native import qk_norm_rope
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    T, H, N = 300, 4, 1024
+    qkv = torch.randn(T, N, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).bfloat16() if norm else None
+    pos = torch.randint(0, 2000, (T,), device="cuda", generator=g)
+    cs = cos_sin_cache(128, 4096, 1e6, None, device="cuda").float()
+    dy = torch.randn(T, H, 128, device="cuda", generator=g).bfloat16()
+    x = qkv[:, 128:128 + H * 128].unflatten(1, (H, 128))
+    out = qk_norm_rope(x, w, 1e-6, pos, cs)
+    out.backward(dy)
+    qf = qkv.detach().float().requires_grad_(True)
+    xf = qf[:, 128:128 + H * 128].unflatten(1, (H, 128))
+    if norm:
+        xf = R.head_rms_norm(xf, w.float(), 1e-6)
+    ref = R.apply_rope(xf, pos, cs)
+    ref.backward(dy.float())
+    assert ((out.float() - ref).norm() / ref.norm()).item() < 1e-2
+    assert ((qkv.grad.float() - qf.grad).norm() / qf.grad.norm()).item() < 1e-2
+    assert qkv.grad[:, :128].abs().max().item() == 0 and qkv.grad[:, 128 + H * 128:].abs().max().item() == 0

@@ -46,6 +46,10 @@ void rmsnorm_bwd_train(const at::Tensor& dy, const at::Tensor& x, const at::Tens
                        at::Tensor& dx, int64_t groups);
 void silu_mul_fwd(const at::Tensor& gu, at::Tensor& a);
 void silu_mul_bwd(const at::Tensor& da, const at::Tensor& gu, at::Tensor& dgu);
+void qk_norm_rope_fwd(const at::Tensor& x, c10::optional<at::Tensor> w, double eps, const at::Tensor& pos,
+                      const at::Tensor& cos_sin, at::Tensor& out, at::Tensor& rstd);
+void qk_norm_rope_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Tensor> w, const at::Tensor& pos,
+                      const at::Tensor& cos_sin, const at::Tensor& rstd, at::Tensor& dx);
 void train_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg,
                     const at::Tensor& pos, const at::Tensor& noisy, const at::Tensor& tiles, int64_t block,
                     double scale, at::Tensor& out, at::Tensor& lse);
@@ -298,6 +302,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd_train", &uno::rmsnorm_bwd_train);
   m.def("silu_mul_fwd", &uno::silu_mul_fwd);
   m.def("silu_mul_bwd", &uno::silu_mul_bwd);
+  m.def("qk_norm_rope_fwd", &uno::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &uno::qk_norm_rope_bwd);
   m.def("train_attn_bwd", &uno::train_attn_bwd);
   m.def("symm_alloc", &uno::symm_alloc);
   m.def("symm_open", &uno::symm_open);

@@ -9,6 +9,10 @@
 // * silu_mul_fwd / silu_mul_bwd  a = silu(gate) * up on [rows, 2I] = [gate | up];
 //   backward dgate = da * up * s * (1 + gate * (1 - s)), dup = da * silu(gate)
 //   with s = sigmoid(gate) (``layers/activation.py:6-14``).
+// * qk_norm_rope_fwd / _bwd  optional per-head RMSNorm (Qwen3 QK-norm,
+//   ``jit_kernel/qk_norm.py:10-87``) followed by the NeoX rotation
+//   (``layers/rotary_embedding.py:8-59``); backward applies the transposed
+//   rotation, then the per-head norm backward.
 #include "common.cuh"
 #include "sampling_common.cuh"
 #include "uno_ops.h"
@@ -123,6 +127,91 @@ __global__ void silu_mul_bwd_kernel(const __nv_bfloat16* __restrict__ da, const 
   }
 }
 
+// QK-norm (optional) + NeoX RoPE of one 128-wide head row per warp.  Lane l
+// holds elements 4l..4l+3; the rotation partner of element d < 64 is d + 64,
+// held by lane l ^ 16.  x rows have a token stride (q / k are column slices of
+// the fused qkv output); out is contiguous [tokens, heads, 128].
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int heads, int64_t n_rows,
+                            const __nv_bfloat16* __restrict__ w, float eps, const int64_t* __restrict__ pos,
+                            const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ out,
+                            float* __restrict__ rstd) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // token * heads + head
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const int64_t t = row / heads;
+  const int h = (int)(row % heads);
+  const __nv_bfloat16* xr = x + t * ld + h * 128 + lane * 4;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(xr[i]);
+  if (w != nullptr) {
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * (1.f / 128.f) + eps);
+    if (lane == 0) rstd[row] = r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * r * __bfloat162float(w[lane * 4 + i]));
+  }
+  const float* cs = cos_sin + pos[t] * 128;
+  const int j0 = (lane & 15) * 4;  // frequency index of element 0 of this lane
+  const bool first = lane < 16;
+  float o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float partner = __shfl_xor_sync(0xffffffff, v[i], 16);
+    const float c = cs[j0 + i], sn = cs[64 + j0 + i];
+    o[i] = first ? v[i] * c - partner * sn : v[i] * c + partner * sn;
+  }
+  __nv_bfloat16* orow = out + row * 128 + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) orow[i] = __float2bfloat16(o[i]);
+}
+
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, int64_t ld,
+                            int heads, int64_t n_rows, const __nv_bfloat16* __restrict__ w,
+                            const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
+                            const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const int64_t t = row / heads;
+  const int h = (int)(row % heads);
+  const __nv_bfloat16* dr = dy + row * 128 + lane * 4;
+  float d[4], g[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = __bfloat162float(dr[i]);
+  // transpose of the rotation: first half gets dy1 c + dy2 s, second half dy2 c - dy1 s
+  const float* cs = cos_sin + pos[t] * 128;
+  const int j0 = (lane & 15) * 4;
+  const bool first = lane < 16;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float partner = __shfl_xor_sync(0xffffffff, d[i], 16);
+    const float c = cs[j0 + i], sn = cs[64 + j0 + i];
+    g[i] = first ? d[i] * c + partner * sn : d[i] * c - partner * sn;
+  }
+  __nv_bfloat16* orow = dx + t * ld + h * 128 + lane * 4;
+  if (w == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) orow[i] = __float2bfloat16(g[i]);
+    return;
+  }
+  const __nv_bfloat16* xr = x + t * ld + h * 128 + lane * 4;
+  const float r = rstd[row];
+  float xh[4], dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    xh[i] = __bfloat162float(xr[i]) * r;
+    g[i] *= __bfloat162float(w[lane * 4 + i]);
+    dot += g[i] * xh[i];
+  }
+  dot = warp_sum(dot) * (1.f / 128.f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) orow[i] = __float2bfloat16(r * (g[i] - xh[i] * dot));
+}
+
 // ------------------------------------------------------------------- host
 static void ew_check(const at::Tensor& t, const char* what) {
   check_dev(t, what);
@@ -188,6 +277,53 @@ void silu_mul_bwd(const at::Tensor& da, const at::Tensor& gu, at::Tensor& dgu) {
   silu_mul_bwd_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()),
                                                       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
                                                       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), rows, (int)I);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static void qk_check(const at::Tensor& x, int64_t& ld, int& heads, int64_t& rows) {
+  check_dev(x, "q/k");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 3 && x.size(2) == 128 && x.stride(2) == 1 &&
+                  x.stride(1) == 128,
+              "q/k must be bf16 [tokens, heads, 128] with contiguous heads");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 8 == 0, "q/k row alignment");
+  ld = x.stride(0);
+  heads = (int)x.size(1);
+  rows = x.size(0) * x.size(1);
+}
+
+void qk_norm_rope_fwd(const at::Tensor& x, c10::optional<at::Tensor> w, double eps, const at::Tensor& pos,
+                      const at::Tensor& cos_sin, at::Tensor& out, at::Tensor& rstd) {
+  int64_t ld, rows;
+  int heads;
+  qk_check(x, ld, heads, rows);
+  TORCH_CHECK(out.is_contiguous() && out.numel() == rows * 128 && out.scalar_type() == at::kBFloat16, "out");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.numel() == x.size(0), "positions");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(-1) == 128, "cos_sin [max_pos, 128] fp32");
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= rows, "rstd");
+  if (rows == 0) return;
+  const __nv_bfloat16* wp = (w.has_value() && w->defined()) ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr())
+                                                            : nullptr;
+  qk_norm_rope_fwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), ld, heads, rows, wp, (float)eps, pos.data_ptr<int64_t>(),
+      cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rstd.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_norm_rope_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Tensor> w, const at::Tensor& pos,
+                      const at::Tensor& cos_sin, const at::Tensor& rstd, at::Tensor& dx) {
+  int64_t ld, rows;
+  int heads;
+  qk_check(x, ld, heads, rows);
+  TORCH_CHECK(dy.is_contiguous() && dy.numel() == rows * 128 && dy.scalar_type() == at::kBFloat16, "dy");
+  TORCH_CHECK(dx.sizes() == x.sizes() && dx.strides() == x.strides() && dx.scalar_type() == at::kBFloat16,
+              "dx must have the layout of x");
+  if (rows == 0) return;
+  const __nv_bfloat16* wp = (w.has_value() && w->defined()) ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr())
+                                                            : nullptr;
+  qk_norm_rope_bwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), ld,
+      heads, rows, wp, pos.data_ptr<int64_t>(), cos_sin.data_ptr<float>(), rstd.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

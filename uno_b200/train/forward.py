@@ -82,7 +82,7 @@ def _layer(x, layer, li, lora, mask, positions, cos_sin, attn_mask, cfg):
 
 def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask, attn_meta=None):
     """The same layer with every projection on the tcgen05 GEMMs (``uno_b200.train.native``)."""
-    from uno_b200.train.native import projection, rms_norm, silu_mul
+    from uno_b200.train.native import projection, qk_norm_rope, rms_norm, silu_mul
 
     B, T, H = x.shape
     attn = layer.self_attn
@@ -91,15 +91,24 @@ def _layer_native(x, layer, proj, mask, positions, cos_sin, attn_mask, attn_meta
     h = rms_norm(x, ln1.weight, ln1.eps, ln1.n_groups)
     qkv = projection(h, proj["qkv"], mask)
     q_end, k_end = hq * hd, (hq + hkv) * hd
-    q = qkv[..., :q_end].reshape(B, T, hq, hd)
-    k = qkv[..., q_end:k_end].reshape(B, T, hkv, hd)
-    v = qkv[..., k_end:].reshape(B, T, hkv, hd)
-    if attn.qk_norm:
-        q = R.head_rms_norm(q, attn.q_norm.weight, attn.eps)
-        k = R.head_rms_norm(k, attn.k_norm.weight, attn.eps)
     pos = positions.reshape(-1)
-    q = R.apply_rope(q.reshape(B * T, hq, hd), pos, cos_sin).reshape(B, T, hq, hd)
-    k = R.apply_rope(k.reshape(B * T, hkv, hd), pos, cos_sin).reshape(B, T, hkv, hd)
+    if hd == 128:  # fused QK-norm + RoPE straight from the qkv columns
+        flat = qkv.reshape(B * T, -1)
+        qn = attn.q_norm.weight if attn.qk_norm else None
+        kn = attn.k_norm.weight if attn.qk_norm else None
+        q = qk_norm_rope(flat[:, :q_end].unflatten(1, (hq, hd)), qn, attn.eps, pos, cos_sin).reshape(B, T, hq, hd)
+        k = qk_norm_rope(flat[:, q_end:k_end].unflatten(1, (hkv, hd)), kn, attn.eps, pos, cos_sin)
+        k = k.reshape(B, T, hkv, hd)
+        v = qkv[..., k_end:].reshape(B, T, hkv, hd)
+    else:
+        q = qkv[..., :q_end].reshape(B, T, hq, hd)
+        k = qkv[..., q_end:k_end].reshape(B, T, hkv, hd)
+        v = qkv[..., k_end:].reshape(B, T, hkv, hd)
+        if attn.qk_norm:
+            q = R.head_rms_norm(q, attn.q_norm.weight, attn.eps)
+            k = R.head_rms_norm(k, attn.k_norm.weight, attn.eps)
+        q = R.apply_rope(q.reshape(B * T, hq, hd), pos, cos_sin).reshape(B, T, hq, hd)
+        k = R.apply_rope(k.reshape(B * T, hkv, hd), pos, cos_sin).reshape(B, T, hkv, hd)
     if attn_meta is not None and hd == 128:
         from uno_b200.train.attention import block_diffusion_attention
 

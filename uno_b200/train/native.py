@@ -276,3 +276,36 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, groups: int = 1)
 def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` of ``[..., 2I] = [gate | up]`` with a fused backward kernel."""
     return _SiluMulFn.apply(gu)
+
+
+class _QKNormRopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps: float, positions, cos_sin):
+        from uno_b200.ops.cuda import ext
+
+        T, H, _ = x.shape
+        out = torch.empty(T, H, 128, device=x.device, dtype=torch.bfloat16)
+        rstd = torch.empty(T * H, device=x.device, dtype=torch.float32)
+        w = weight.detach().to(torch.bfloat16).contiguous() if weight is not None else None
+        ext().qk_norm_rope_fwd(x, w, float(eps), positions, cos_sin, out, rstd)
+        ctx.save_for_backward(x, rstd, positions, cos_sin)
+        ctx.w = w
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        from uno_b200.ops.cuda import ext
+
+        x, rstd, positions, cos_sin = ctx.saved_tensors
+        dx = torch.empty_strided(x.shape, x.stride(), device=x.device, dtype=torch.bfloat16)
+        ext().qk_norm_rope_bwd(dy.to(torch.bfloat16).contiguous(), x, ctx.w, positions, cos_sin, rstd, dx)
+        return dx, None, None, None, None
+
+
+def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor | None, eps: float, positions: torch.Tensor,
+                 cos_sin: torch.Tensor) -> torch.Tensor:
+    """Per-head RMSNorm (when ``weight`` is given) + NeoX RoPE of ``x [tokens, heads, 128]``.
+
+    ``x`` may be a column slice of the fused qkv output (token stride > heads * 128); the
+    result is contiguous and its backward writes a gradient of ``x``'s layout."""
+    return _QKNormRopeFn.apply(x, weight, eps, positions.reshape(-1).long().contiguous(), cos_sin.float().contiguous())
