@@ -16,7 +16,8 @@
 // Forward: one CTA per (64-query tile, query head, batch row), 4 warps of 16
 // queries; S = Q K^T and O += P V on mma.sync m16n8k16 (bf16 in, fp32
 // accumulate), online softmax in the log2 domain, K/V tiles double-buffered
-// with cp.async.  Outputs O and the per-row log2-sum-exp (for backward).
+// with cp.async, three CTAs per SM.  Outputs O and the per-row log2-sum-exp
+// (for backward).
 //
 // Backward: one CTA per (64-key tile, KV head, batch row) looping over the
 // query heads of its group and the query tiles that see it (FlashAttention-2
@@ -110,15 +111,17 @@ __device__ __forceinline__ TokMeta ta_meta(const TAParams& p, int b, int t) {
 }
 
 // ------------------------------------------------------------------ forward
-__global__ void __launch_bounds__(128) train_attn_fwd_kernel(TAParams p) {
+__global__ void __launch_bounds__(128, 3) train_attn_fwd_kernel(TAParams p) {
   extern __shared__ __align__(128) uint8_t ta_smem[];
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.hq / p.hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
-  uint8_t* sQ = ta_smem;
-  uint8_t* sK = sQ + TA_TILE_BYTES;        // 2 stages
+  // K and V stages 0/1; the Q tile is staged in V stage 1 and moved to registers
+  // before that stage is first loaded (4 tiles: three CTAs fit on an SM)
+  uint8_t* sK = ta_smem;                   // 2 stages
   uint8_t* sV = sK + 2 * TA_TILE_BYTES;    // 2 stages
+  uint8_t* sQ = sV + TA_TILE_BYTES;
   int* sKm = reinterpret_cast<int*>(sV + 2 * TA_TILE_BYTES);  // [2][3][64] key meta
   int* sList = sKm + 2 * 3 * TA_B;                             // visible key tiles (<= nt)
   __shared__ int s_count;
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(128) train_attn_fwd_kernel(TAParams p) {
     const int r = warp * 16 + (lane & 15), c = kk * 16 + (lane >> 4) * 8;
     ta_ldsm(qs + (uint32_t)(r * TA_PITCH + c) * 2, qa[kk]);
   }
+  __syncthreads();  // every warp holds its Q fragments before V stage 1 is overwritten
 
   for (int it = 0; it < n_tiles; ++it) {
     const int stage = it & 1;
@@ -542,11 +546,11 @@ void train_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
   TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == (int64_t)p.B * p.hq * p.T, "lse [B, hq, T] fp32");
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.lse = lse.data_ptr<float>();
-  const int smem = 5 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + p.nt * 4;
+  const int smem = 4 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + p.nt * 4;
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(train_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        5 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + 4096 * 4));
+                                        4 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + 4096 * 4));
     configured = true;
   }
   TORCH_CHECK(p.nt <= 4096, "sequence too long for the tile list");
