@@ -422,3 +422,25 @@ def test_gemm_weight_gradient_strided_slices(C):
     C.ext().gemm_wgrad(dy[:, 4096:5120], h[:, 64:128], c, 0)
     want = dy[:, 4096:5120].float().t() @ h[:, 64:128].float()
     assert rel_err(c, want) < 2e-3
+
+
+def test_peer_wait_times_out_with_an_error_status(C):
+    """A vocab-parallel exchange whose second rank never publishes: the kernel's bounded wait gives up,
+    records error bit 4 in the device error word and returns; the context stays usable."""
+    import time
+
+    ext = C.ext()
+    max_rows = 64
+    regions = [torch.zeros(ext.vp_region_bytes(max_rows), dtype=torch.uint8, device=DEV) for _ in range(2)]
+    x = torch.randn(8, 4096, device=DEV).bfloat16()
+    out = torch.empty(8, dtype=torch.int64, device=DEV)
+    C.error_flag(reset=True)
+    t0 = time.time()
+    # rank 0 of 2; nobody plays rank 1, so its partials never arrive
+    ext.vp_sample(x, out, 1.0, False, 1, 1, [r.data_ptr() for r in regions], 0, max_rows, 0)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    err = C.error_flag(reset=True)
+    assert err & (1 << 4), err
+    assert elapsed < 30
+    assert torch.equal(C.argmax(x), C.argmax(x))  # the device still runs kernels afterwards
