@@ -37,6 +37,7 @@ from uno_b200.engine.noise import build_draft_batch
 from uno_b200.engine.sampling import Sampler
 from uno_b200.engine.sequence import Sequence
 from uno_b200.sampling_params import SamplingParams
+from uno_b200.utils.trace import nvtx
 
 
 class TwoPassDecoder:
@@ -77,11 +78,14 @@ class TwoPassDecoder:
         if not seqs:
             return []
         L = int(sp.diffusion_block_size)
-        proposal, draft_logits, q_sparse = self.draft_stage(seqs, L, sp)
+        with nvtx("draft"):
+            proposal, draft_logits, q_sparse = self.draft_stage(seqs, L, sp)
         if self.tree_verify_size is None:
-            payload = self.verify_stage(seqs, proposal, draft_logits, q_sparse, sp)
+            with nvtx("verify"):
+                payload = self.verify_stage(seqs, proposal, draft_logits, q_sparse, sp)
         else:
-            payload = self.tree_verify_stage(seqs, proposal[:, 0], draft_logits, L, sp)
+            with nvtx("tree"):
+                payload = self.tree_verify_stage(seqs, proposal[:, 0], draft_logits, L, sp)
         rows = payload.cpu().numpy()  # the single host synchronisation of the cycle
         accepted = [[] for _ in seqs]
         if apply:

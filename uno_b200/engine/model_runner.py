@@ -33,6 +33,7 @@ from uno_b200.parallel import state as tp
 from uno_b200.sampling_params import SamplingParams
 from uno_b200.utils.loader import dummy_init, load_model
 from uno_b200.utils.lora import dummy_lora, load_lora_adapter
+from uno_b200.utils.trace import nvtx
 
 logger = logging.getLogger(__name__)
 
@@ -213,8 +214,9 @@ class ModelRunner:
             logits_indices=torch.tensor(cu_q[1:], dtype=torch.int64, device=dev) - 1,
         )
         input_ids = torch.tensor(ids, dtype=torch.int64, device=dev)
-        hidden = self.model(input_ids, meta)
-        logits = self._logits_full(self.model.compute_logits(hidden, meta))
+        with nvtx("prefill"):
+            hidden = self.model(input_ids, meta)
+            logits = self._logits_full(self.model.compute_logits(hidden, meta))
         self.last_prefill_logits = logits  # last-position logits of the latest prefill (diagnostics)
         tokens, _ = self.sampler.sample(logits, sp)
         out = tokens.tolist()

@@ -37,6 +37,7 @@ from typing import Callable
 import torch
 
 from uno_b200.sampling_params import SamplingParams
+from uno_b200.utils.trace import nvtx
 
 
 @dataclass
@@ -92,6 +93,10 @@ class Sampler:
     # ---------------------------------------------------------------- sampling
     def sample(self, logits: torch.Tensor, sp: SamplingParams):
         """Return ``(tokens [N] int64, sparse_q or None)``."""
+        with nvtx("sample"):
+            return self._sample(logits, sp)
+
+    def _sample(self, logits: torch.Tensor, sp: SamplingParams):
         V = self.vocab_size(logits)
         if sp.greedy:
             return self.argmax(logits), None
