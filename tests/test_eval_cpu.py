@@ -204,3 +204,59 @@ def test_pull_suite_distributes_resumes_and_guards_manifest(tmp_path):
     assert kind == "err" and "manifest mismatch" in msg
     t2.join(30)
     assert "1 jobs unfinished" in seen.get("timeout", "")
+
+
+# ------------------------------------------------------------------ ifeval
+@pytest.mark.parametrize("iid,kwargs,good,bad", [
+    ("keywords:existence", {"keywords": ["apple", "pie"]}, "An apple Pie.", "An apple."),
+    ("keywords:frequency", {"keyword": "cat", "frequency": 2, "relation": "at least"}, "cat CAT", "cat"),
+    ("keywords:forbidden_words", {"forbidden_words": ["bad"]}, "badge is fine", "that is bad"),
+    ("keywords:letter_frequency", {"letter": "z", "let_frequency": 3, "let_relation": "less than"}, "zz", "zzz"),
+    ("language:response_language", {"language": "ru"}, "Привет, как дела?", "Hello there"),
+    ("language:response_language", {"language": "de"}, "Das ist nicht der Weg und die Zeit",
+     "The way and the time of it"),
+    ("length_constraints:number_sentences", {"num_sentences": 3, "relation": "less than"}, "One. Two.",
+     "One. Two. Three."),
+    ("length_constraints:number_paragraphs", {"num_paragraphs": 2}, "first\n***\nsecond", "only one"),
+    ("length_constraints:number_words", {"num_words": 5, "relation": "at least"}, "one two three four five",
+     "one two"),
+    ("length_constraints:nth_paragraph_first_word",
+     {"num_paragraphs": 2, "nth_paragraph": 2, "first_word": "then"}, "First.\n\nThen, more.", "First.\n\nNo."),
+    ("detectable_content:number_placeholders", {"num_placeholders": 2}, "[name] at [address]", "[name]"),
+    ("detectable_content:postscript", {"postscript_marker": "P.S."}, "Body.\nP.S. hi", "Body only."),
+    ("detectable_format:number_bullet_lists", {"num_bullets": 2}, "* a\n* b", "* a\n* b\n* c"),
+    ("detectable_format:constrained_response", {}, "My answer is yes.", "Yes."),
+    ("detectable_format:number_highlighted_sections", {"num_highlights": 2}, "*one* and *two*", "*one*"),
+    ("detectable_format:multiple_sections", {"section_spliter": "Section", "num_sections": 2},
+     "Section 1\na\nSection 2\nb", "Section 1\na"),
+    ("detectable_format:json_format", {}, '```json\n{"a": 1}\n```', "{a: 1}"),
+    ("detectable_format:title", {}, "<<My Title>>\ntext", "no title"),
+    ("combination:two_responses", {}, "first answer\n******\nsecond answer", "one answer"),
+    ("combination:repeat_prompt", {"prompt_to_repeat": "Say hi"}, "Say hi. Hi!", "Hi!"),
+    ("startend:end_checker", {"end_phrase": "Is there anything else?"}, "Done. Is there anything else?", "Done."),
+    ("change_case:capital_word_frequency", {"capital_frequency": 2, "capital_relation": "at least"},
+     "THIS is VERY good", "This is good"),
+    ("change_case:english_capital", {}, "THIS IS ALL CAPS AND THE END", "This is not"),
+    ("change_case:english_lowercase", {}, "this is all lower and the end", "This is not"),
+    ("punctuation:no_comma", {}, "no commas here", "one, two"),
+    ("startend:quotation", {}, '"quoted"', "not quoted"),
+])
+def test_ifeval_checkers(iid, kwargs, good, bad):
+    from uno_b200.eval.ifeval import check
+
+    assert check(iid, good, kwargs) and not check(iid, bad, kwargs)
+
+
+def test_ifeval_grade_strict_loose_and_scoring(tmp_path):
+    from uno_b200.eval.ifeval import grade_ifeval
+    from uno_b200.eval.score import grade_row
+
+    truth = {"instruction_id_list": ["punctuation:no_comma", "startend:end_checker"],
+             "kwargs": [{}, {"end_phrase": "bye"}]}
+    # the trailing sign-off line breaks strict end_checker; loose drops the last line
+    gen = "<think>plan, then answer</think>hello there\nbye\n**thanks**"
+    g = grade_ifeval(gen, truth)
+    assert g["strict_inst_follow"] == [True, False] and not g["strict_prompt_follow"]
+    assert g["loose_inst_follow"] == [True, True] and g["loose_prompt_follow"] and g["correct"] is False
+    row = {"generation": "hello bye", "ground_truth": truth}
+    assert grade_row(row, None, task="ifeval", parser="passthrough")["correct"] is True

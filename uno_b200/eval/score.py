@@ -3,7 +3,7 @@
 Routing by task: multiple-choice parsers grade letters; ``humaneval`` /
 ``mbpp`` (and any ``code_completion`` parser) run the sandboxed code grader;
 benchmarks with a judge use the LLM judge when a transport is given (else the
-rows are reported as ungraded); ``ifeval`` is reported as unsupported;
+rows are reported as ungraded); ``ifeval`` uses the instruction checkers of ``eval/ifeval.py``;
 everything else is graded as math (boxed answer equivalence).  Scores are
 the mean correctness over all samples, the per-question mean, and the
 generation throughput (TPS, TPF) copied from the generation summary.
@@ -26,7 +26,10 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     gen = row.get("generation", "")
     truth = row.get("ground_truth")
     if task == "ifeval":
-        return {"correct": None, "status": "unsupported grader"}
+        from uno_b200.eval.ifeval import grade_ifeval
+
+        prompt = row.get("question") or (record or {}).get("prompt", "")
+        return grade_ifeval(gen, truth if truth is not None else (record or {}), prompt)
     if parser == "mc_answer":
         return grade_multiple_choice(parse_generation("mc_answer", gen), truth)
     if parser == "code_completion" or task in ("humaneval", "mbpp"):
