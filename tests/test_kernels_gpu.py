@@ -444,3 +444,22 @@ def test_peer_wait_times_out_with_an_error_status(C):
     assert err & (1 << 4), err
     assert elapsed < 30
     assert torch.equal(C.argmax(x), C.argmax(x))  # the device still runs kernels afterwards
+
+
+def test_sparse_top_k_kernel_path_matches_torch(C):
+    """Top-k (k <= 32) candidates and their renormalised probabilities from the top-K kernel vs torch.topk."""
+    from uno_b200.engine.sampling import sparse_top_k
+
+    torch.manual_seed(12)
+    x = (torch.randn(37, 151936, device=DEV) * 3).bfloat16()
+    for k, top_p in ((20, None), (32, 0.9), (5, 0.5)):
+        ids, probs = sparse_top_k(x, 0.7, k, top_p)
+        vals, want_ids = torch.topk(x.float(), k, dim=-1)
+        want = torch.softmax(vals / 0.7, dim=-1)
+        if top_p is not None:
+            cdf = want.cumsum(-1)
+            want = want.masked_fill((cdf - want) > top_p, 0.0)
+            want = want / want.sum(-1, keepdim=True)
+        same = (ids == want_ids).all(dim=1)  # rows without bf16 ties at the k-th place
+        assert same.float().mean().item() > 0.9
+        assert torch.allclose(probs[same], want[same], atol=1e-4)

@@ -184,8 +184,19 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
 
 
 def sparse_top_k(logits: torch.Tensor, temperature: float, k: int, top_p: float | None):
-    values, ids = torch.topk(logits, k=int(k), dim=-1)
-    probs = torch.softmax(values.float() / float(temperature), dim=-1)
+    if (logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and int(k) <= 32
+            and logits.is_contiguous()):
+        # one kernel pass per row: top-k ids with their log-softmax values (sorted, lowest id on ties)
+        from uno_b200.ops.cuda import ext
+
+        n = logits.shape[0]
+        ids = torch.empty(n, int(k), device=logits.device, dtype=torch.int64)
+        lp = torch.empty(n, int(k), device=logits.device, dtype=torch.float32)
+        ext().topk_lse(logits, int(k), 1.0 / float(temperature), ids, lp)
+        probs = torch.softmax(lp, dim=-1)  # renormalised over the k candidates
+    else:
+        values, ids = torch.topk(logits, k=int(k), dim=-1)
+        probs = torch.softmax(values.float() / float(temperature), dim=-1)
     if top_p is not None and float(top_p) < 1.0:
         cdf = probs.cumsum(dim=-1)
         probs = probs.masked_fill((cdf - probs) > float(top_p), 0.0)
