@@ -460,6 +460,6 @@ def test_sparse_top_k_kernel_path_matches_torch(C):
             cdf = want.cumsum(-1)
             want = want.masked_fill((cdf - want) > top_p, 0.0)
             want = want / want.sum(-1, keepdim=True)
-        same = (ids == want_ids).all(dim=1)  # rows without bf16 ties at the k-th place
-        assert same.float().mean().item() > 0.9
-        assert torch.allclose(probs[same], want[same], atol=1e-4)
+        # bf16 logits tie often: compare the selected values (descending) rather than the ids
+        assert torch.equal(x.gather(1, ids).float(), vals)
+        assert torch.allclose(probs, want, atol=1e-4)
