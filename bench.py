@@ -20,6 +20,10 @@ host->device from pinned memory and reads committed tokens back every step.
 
 ``--impl reference`` runs the unmodified reference package from
 ``baseline/_ref`` through its own ``LLM`` API on the same workload.
+
+``--sampler tree`` measures BASELINE config 3 (per-request tok/s of the tree
+sampler) and ``--config uno-0.9b-dp`` config 4 (one 0.9B replica per GPU,
+weak scaling).
 """
 
 from __future__ import annotations
