@@ -13,7 +13,6 @@ from __future__ import annotations
 import atexit
 import logging
 import os
-import random
 import socket
 from time import perf_counter, perf_counter_ns
 from typing import Callable

@@ -22,7 +22,7 @@ from glob import glob
 import torch
 from torch import nn
 
-from uno_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear
+from uno_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear
 
 _QKV = ("q_proj", "k_proj", "v_proj")
 _GATE_UP = {"gate_proj": 0, "up_proj": 1}
