@@ -171,3 +171,26 @@ def test_block_fp8_checkpoint_loads_dequantized(tmp_path):
     assert torch.allclose(got[pre + "mlp.down_proj.weight"], deq[pre + "mlp.down_proj.weight"])
     # quantisation error stays at the fp8 level
     assert ((want_qkv - qkv).abs().max() / qkv.abs().max()).item() < 0.07
+
+
+def test_bench_configs_and_tool_modules_parse(monkeypatch):
+    """bench.py maps each BASELINE config to its workload; the profiling tools import without a GPU."""
+    import importlib
+    import sys
+
+    root = __import__("os").path.dirname(__import__("os").path.dirname(__import__("os").path.abspath(__file__)))
+    sys.path.insert(0, root)
+    bench = importlib.import_module("bench")
+    monkeypatch.setattr(sys, "argv", ["bench.py"])
+    a = bench.parse()
+    assert (a.batch, a.block, a.new_tokens, a.config) == (64, 8, 2048, "qwen3-8b")
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--config", "uno-0.9b-dp"])
+    a = bench.parse()
+    assert (a.batch, a.block, a.new_tokens) == (256, 16, 1024)
+    assert bench.engine_kwargs(a, 1)["dummy_lora_rank"] == 32
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--sampler", "tree"])
+    a = bench.parse()
+    assert (a.batch, a.block, a.new_tokens) == (1, 9, 4096)
+    kc = importlib.import_module("uno_b200.ops.kernel_cases")
+    assert set(kc.CASES) >= {"layer-gemms", "lm-head", "decode-attention", "sampling", "train-attention"}
+    importlib.import_module("uno_b200.parallel.comm_cases")
