@@ -297,3 +297,38 @@ def test_sharded_adamw_matches_torch_adamw_two_ranks():
         for got, ref in zip(out[r][0], want):
             torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-6)
     assert out[0][1] == out[1][1] and out[0][1][0] > 1.0  # the first step is clipped
+
+
+def _dp_trainer_worker(rank, port, box):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2)
+    cfg, model, lora = _tiny_setup(seed=4)  # same initial weights on every rank
+    plan = BlockCurriculumPlan.fixed([4], 3, 64, 2)
+    tr = UnoTrainer(model, lora, objective=UnoObjectiveConfig(), curriculum=plan, mask_token_id=cfg.mask_token_id,
+                    lr=1e-2, seed=9, process_group=dist.group.WORLD)
+    metrics = [tr.train_step([_batch(1, 64, seed=rank * 10 + s)]) for s in range(2)]  # different data per rank
+    flat = torch.cat([p.detach().reshape(-1) for p in lora.parameters()])
+    box.put((rank, flat, [m["grad_norm"] for m in metrics]))
+    dist.destroy_process_group()
+
+
+def test_data_parallel_training_keeps_ranks_in_sync():
+    """Two gloo ranks on different data: the ZeRO-2 step leaves identical LoRA parameters on both."""
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("fork")
+    box = ctx.Queue()
+    procs = [ctx.Process(target=_dp_trainer_worker, args=(r, port, box)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict((r, (flat, norms)) for r, flat, norms in (box.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(30)
+    assert torch.equal(out[0][0], out[1][0])
+    assert out[0][1] == out[1][1]  # the global gradient norm is the same on both ranks
+    assert float(out[0][0].abs().sum()) > 0
