@@ -332,3 +332,55 @@ def test_data_parallel_training_keeps_ranks_in_sync():
     assert torch.equal(out[0][0], out[1][0])
     assert out[0][1] == out[1][1]  # the global gradient norm is the same on both ranks
     assert float(out[0][0].abs().sum()) > 0
+
+
+def _dp_resume_worker(rank, port, out_dir, box):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2)
+    plan = BlockCurriculumPlan.fixed([4, 8], 2, 64, 2)  # boundary checkpoint after step 2
+
+    def trainer(output_dir):
+        cfg, model, lora = _tiny_setup(seed=4)
+        return UnoTrainer(model, lora, objective=UnoObjectiveConfig(), curriculum=plan,
+                          mask_token_id=cfg.mask_token_id, lr=1e-2, seed=9, process_group=dist.group.WORLD,
+                          output_dir=output_dir), lora
+
+    def batches(steps):
+        return [[_batch(1, 64, seed=rank * 10 + s)] for s in steps]
+
+    tr, lora = trainer(None)  # uninterrupted: 4 steps
+    for b in batches(range(4)):
+        tr.train_step(b)
+    straight = torch.cat([p.detach().reshape(-1) for p in lora.parameters()])
+    tr1, _ = trainer(out_dir)  # 2 steps, checkpoint at the stage boundary
+    for b in batches(range(2)):
+        tr1.train_step(b)
+    dist.barrier()
+    tr2, lora2 = trainer(None)  # fresh process state, resume, 2 more steps
+    tr2.resume(f"{out_dir}/checkpoint-2")
+    for b in batches(range(2, 4)):
+        tr2.train_step(b)
+    resumed = torch.cat([p.detach().reshape(-1) for p in lora2.parameters()])
+    box.put((rank, torch.equal(straight, resumed), float((straight - resumed).abs().max())))
+    dist.destroy_process_group()
+
+
+def test_data_parallel_resume_from_boundary_matches_uninterrupted(tmp_path):
+    """Per-rank optimizer shards + RNG state in the boundary checkpoint: resuming reproduces the run."""
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("fork")
+    box = ctx.Queue()
+    procs = [ctx.Process(target=_dp_resume_worker, args=(r, port, str(tmp_path), box)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [box.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(30)
+    assert (tmp_path / "checkpoint-2" / "trainer_state_rank1.pt").is_file()
+    assert all(same for _, same, _ in out), out
