@@ -321,7 +321,7 @@ def test_data_parallel_training_keeps_ranks_in_sync():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    ctx = mp.get_context("fork")
+    ctx = mp.get_context("spawn")  # forked children of a process with torch threads can deadlock
     box = ctx.Queue()
     procs = [ctx.Process(target=_dp_trainer_worker, args=(r, port, box)) for r in range(2)]
     for p in procs:
@@ -374,7 +374,7 @@ def test_data_parallel_resume_from_boundary_matches_uninterrupted(tmp_path):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    ctx = mp.get_context("fork")
+    ctx = mp.get_context("spawn")  # forked children of a process with torch threads can deadlock
     box = ctx.Queue()
     procs = [ctx.Process(target=_dp_resume_worker, args=(r, port, str(tmp_path), box)) for r in range(2)]
     for p in procs:
