@@ -446,12 +446,11 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t 
 template <int NWR, int KS>
 static void launch_attn(dim3 grid, int smem, const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p,
                         cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce smem_opt_in;
+  smem_opt_in([smem] {
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(paged_attention_kernel<NWR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  });
   paged_attention_kernel<NWR, KS><<<grid, 32 * (NWR * KS + 1), smem, stream>>>(tk, tv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

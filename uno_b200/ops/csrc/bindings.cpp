@@ -178,7 +178,7 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, int64_t epi, int64_t 
   p.err = scratch.err;
   int tile = 0;
   pick_tile(p.M, p.N, p.K + p.K2, (int)epi, (int)bn, (int)splits, &tile, &p.splits);
-  const int tiles = ((p.M + 127) / 128) * ((p.N + tile - 1) / tile);
+  const int64_t tiles = splitk_tiles(p.M, p.N, tile);
   if (p.splits > 1 &&
       (tiles > scratch.max_counters || (size_t)tiles * p.splits * 128 * tile > scratch.ws_floats))
     p.splits = 1;

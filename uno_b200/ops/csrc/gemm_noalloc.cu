@@ -1,4 +1,5 @@
-// Split-K GEMM entry point that allocates no memory (plain C ABI).
+// Split-K GEMM entry point that allocates no memory (plain C ABI, declared in
+// uno_noalloc.h).
 //
 // This entry point has no counterpart in the reference implementation.
 //
@@ -15,28 +16,38 @@
 //
 // Who needs that: callers that are not allowed to allocate at call time, e.g.
 // code that runs inside a custom device allocator or its out-of-memory path
-// (an allocation there could recurse or fail), a serving process that sizes
-// every device buffer at start-up and treats later growth as a bug, or a C or
-// C++ host program that links this library without PyTorch.  All buffers
-// (A, B, out) belong to the caller.
+// (an allocation there could recurse or fail), or a serving process that
+// sizes every device buffer at start-up and treats later growth as a bug.
+// A C or C++ host can call it through uno_noalloc.h; the library links
+// libtorch, which must be loadable, but no PyTorch allocator is involved.
+// All buffers (A, B, out) belong to the caller.
 //
 // Limits: a split-K launch needs tiles * splits * 128 * tile_width fp32
-// partials and one counter per output tile.  The fixed scratch holds
-// kNoAllocWsFloats floats (4 MiB) and kNoAllocCounters counters; a request
-// above either is rejected with UNO_NOALLOC_TOO_LARGE before anything is
-// launched (uno_noalloc_last_error() says why).  splits == 1 needs no scratch.
+// partials and one counter per output tile (uno::splitk_tiles).  The fixed
+// scratch holds kNoAllocWsFloats floats (4 MiB) and kNoAllocCounters
+// counters.  With splits == 0 (automatic) a problem whose split does not fit
+// runs without a K split, as the regular entry point does; an explicit split
+// count that does not fit is rejected with UNO_NOALLOC_TOO_LARGE before
+// anything is launched (uno_noalloc_last_error() says why).  splits == 1
+// needs no scratch.
 //
-// Set-up: uno_gemm_noalloc_setup() looks up the device addresses of the
-// arrays for the current device (cudaGetSymbolAddress) and clears the
-// counters, which must start at zero; the kernel returns each counter to zero
-// after use.  The first call on a device runs the set-up itself; run it
-// explicitly, with the device current, before capturing a stream that will
-// contain a call, since the set-up itself synchronises with the device.
+// Set-up: uno_gemm_noalloc_setup() waits for the device to be idle, looks up
+// the device addresses of the arrays for the current device
+// (cudaGetSymbolAddress) and clears the counters and the error word, which
+// must start at zero; the kernel returns each counter to zero after use.  The
+// first call on a device runs the set-up itself; run it explicitly, with the
+// device current, before capturing a stream that will contain a call, since
+// the set-up synchronises with the device.
 //
-// Concurrency: all calls on a device share one scratch area.  Calls that can
-// overlap in time (different streams, or host threads without ordering
-// between their launches) race on it and give wrong results; issue them on a
-// single stream.
+// Errors on the device: the kernels' bounded waits write this module's own
+// error word, read with uno_noalloc_error_flag(); a non-zero value means the
+// output is incomplete and the counters must be cleared by running the
+// set-up again.
+//
+// Concurrency: all calls on a device share one scratch area, which keeps the
+// last call's contents.  Calls that can overlap in time (different streams,
+// or host threads without ordering between their launches) race on it and
+// give wrong results; issue them on a single stream.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -44,6 +55,7 @@
 #include <cstdio>
 #include <exception>
 
+#include "uno_noalloc.h"
 #include "uno_ops.h"
 
 namespace {
@@ -77,13 +89,6 @@ int fail(int code, const char* fmt, ...) {
 
 extern "C" {
 
-enum {
-  UNO_NOALLOC_OK = 0,
-  UNO_NOALLOC_BAD_ARGS = 1,
-  UNO_NOALLOC_TOO_LARGE = 2,
-  UNO_NOALLOC_CUDA_ERROR = 3,
-};
-
 __attribute__((visibility("default"))) const char* uno_noalloc_last_error() { return g_message; }
 
 __attribute__((visibility("default"))) int uno_gemm_noalloc_setup() {
@@ -91,6 +96,9 @@ __attribute__((visibility("default"))) int uno_gemm_noalloc_setup() {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(UNO_NOALLOC_CUDA_ERROR, "cudaGetDevice failed: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(UNO_NOALLOC_BAD_ARGS, "device index %d out of range", dev);
+  // never clear counters under a call that is still running on this device
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(UNO_NOALLOC_CUDA_ERROR, "waiting for the device failed: %s", cudaGetErrorString(e));
   DevicePtrs d{};
   e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.ws), g_noalloc_ws);
   if (e != cudaSuccess) return fail(UNO_NOALLOC_CUDA_ERROR, "cudaGetSymbolAddress(workspace) failed: %s", cudaGetErrorString(e));
@@ -111,7 +119,8 @@ __attribute__((visibility("default"))) int uno_gemm_noalloc_setup() {
 // Returns 0 on success, else an UNO_NOALLOC_* code with a message in
 // uno_noalloc_last_error().  Leading dimensions are in elements; every
 // pointer must be 16-byte aligned and every leading dimension a multiple of 8.
-// splits == 0 picks the split count the regular entry point would use.
+// splits == 0 picks the split count the regular entry point would use, and no
+// split when that does not fit the fixed scratch.
 __attribute__((visibility("default"))) int uno_gemm_splitk_noalloc(const void* a, long long lda, const void* b,
                                                                     long long ldb, void* out, long long ldo, int M,
                                                                     int N, int K, int splits, void* stream) {
@@ -142,16 +151,20 @@ __attribute__((visibility("default"))) int uno_gemm_splitk_noalloc(const void* a
     int bn = 0;
     uno::pick_tile(M, N, K, 0 /* STORE */, 0, splits, &bn, &p.splits);
     if (p.splits > 1) {
-      // 128-row tiles, or 256-row CTA pairs counted as two tiles
-      const long long m_tiles = std::max((M + 127) / 128, ((M + 255) / 256) * 2);
-      const long long tiles = m_tiles * ((N + bn - 1) / bn);
+      const long long tiles = uno::splitk_tiles(M, N, bn);
       const long long need = tiles * p.splits * 128LL * bn;
-      if (tiles > kNoAllocCounters || need > (long long)kNoAllocWsFloats)
+      const bool fits = tiles <= kNoAllocCounters && need <= (long long)kNoAllocWsFloats;
+      if (!fits && splits == 0) {
+        p.splits = 1;  // automatic split count: run unsplit, as the regular entry point does
+      } else if (!fits) {
         return fail(UNO_NOALLOC_TOO_LARGE,
                     "split-K scratch too small: %lld tiles x %d splits x 128 x %d needs %lld floats and %lld "
                     "counters; the fixed scratch holds %zu floats and %d counters (use fewer splits or a "
                     "smaller problem)",
                     tiles, p.splits, bn, need, tiles, kNoAllocWsFloats, kNoAllocCounters);
+      }
+    }
+    if (p.splits > 1) {
       p.ws = d.ws;
       p.counters = d.counters;
     }
@@ -164,6 +177,27 @@ __attribute__((visibility("default"))) int uno_gemm_splitk_noalloc(const void* a
   if (e != cudaSuccess) return fail(UNO_NOALLOC_CUDA_ERROR, "launch failed: %s", cudaGetErrorString(e));
   g_message[0] = '\0';
   return UNO_NOALLOC_OK;
+}
+
+__attribute__((visibility("default"))) int uno_noalloc_error_flag(int reset) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices || !g_devices[dev].ready) return 0;  // nothing ran here
+  int word = 0;  // host stack memory: a plain synchronous copy allocates nothing
+  e = cudaMemcpy(&word, g_devices[dev].err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    fail(UNO_NOALLOC_CUDA_ERROR, "reading the error word failed: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpy(g_devices[dev].err, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      fail(UNO_NOALLOC_CUDA_ERROR, "clearing the error word failed: %s", cudaGetErrorString(e));
+      return -1;
+    }
+  }
+  return word;
 }
 
 }  // extern "C"

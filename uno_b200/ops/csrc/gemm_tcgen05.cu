@@ -862,11 +862,14 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t 
 }
 
 int num_sms() {
-  static int n = 0;
+  static std::atomic<int> counts[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  int n = counts[dev].load(std::memory_order_relaxed);
   if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -875,12 +878,11 @@ template <int BN, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
                    GemmParams& p, cudaStream_t stream, int max_ctas) {
   using Cfg = GemmCfg<BN, EPI>;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce smem_opt_in;
+  smem_opt_in([] {
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    configured = true;
-  }
+  });
   const int units = p.num_m * p.num_n * p.splits;
   const int grid = std::min(units, max_ctas > 0 ? max_ctas : num_sms());
   gemm_bf16_kernel<BN, EPI><<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, ta2, tb2, p);
@@ -891,12 +893,11 @@ template <int EPI>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
                         GemmParams& p, cudaStream_t stream, int max_ctas) {
   using Cfg = GemmCfg<128, EPI>;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce smem_opt_in;
+  smem_opt_in([] {
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    configured = true;
-  }
+  });
   const int units = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.splits;
   const int pairs = std::max(1, std::min(units, (max_ctas > 0 ? max_ctas : num_sms()) / 2));
   cudaLaunchConfig_t cfg = {};

@@ -547,12 +547,11 @@ void train_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.lse = lse.data_ptr<float>();
   const int smem = 4 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + p.nt * 4;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce smem_opt_in;
+  smem_opt_in([] {
     C10_CUDA_CHECK(cudaFuncSetAttribute(train_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         4 * TA_TILE_BYTES + 2 * 3 * TA_B * 4 + 4096 * 4));
-    configured = true;
-  }
+  });
   TORCH_CHECK(p.nt <= 4096, "sequence too long for the tile list");
   train_attn_fwd_kernel<<<dim3(p.nt, p.hq, p.B), 128, smem, cur_stream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -582,12 +581,11 @@ void train_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
   train_attn_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, cur_stream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int smem = 4 * TA_TILE_BYTES + TA_B * TA_DS_PITCH * 2 + 2 * TA_B * 4 + 3 * TA_B * 4;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce smem_opt_in;
+  smem_opt_in([smem] {
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(train_attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  });
   train_attn_bwd_kernel<<<dim3(p.nt, p.hkv, p.B), 128, smem, cur_stream()>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

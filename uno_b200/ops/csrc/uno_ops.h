@@ -9,6 +9,7 @@
 #include <torch/extension.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 namespace uno {
@@ -61,6 +62,35 @@ void pick_tile(int M, int N, int K, int epi, int forced_bn, int forced_splits, i
 void gemm_wgrad_dispatch(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams& p, int bn,
                          cudaStream_t stream);
 int num_sms();
+
+// Output tiles a split-K launch of tile width bn can index: 128-row tiles, or
+// 256-row CTA pairs counted as two 128-row tiles (M = 384 uses four).  The
+// split-K scratch holds tiles * splits * 128 * bn partials and one counter per
+// tile, so every scratch-size check uses this count.
+inline int64_t splitk_tiles(int M, int N, int bn) {
+  const int64_t m_tiles = std::max<int64_t>((M + 127) / 128, (int64_t)((M + 255) / 256) * 2);
+  return m_tiles * ((N + bn - 1) / bn);
+}
+
+// Runs a set-up step once per CUDA device.  Function attributes such as the
+// dynamic shared-memory opt-in belong to (function, device): a process that
+// launches on several devices must set them on each one.
+class PerDeviceOnce {
+ public:
+  template <class F>
+  void operator()(F&& f) {
+    int dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    TORCH_CHECK(dev >= 0 && dev < 64, "device index ", dev, " out of range");
+    const uint64_t bit = uint64_t(1) << dev;
+    if (done_.load(std::memory_order_acquire) & bit) return;
+    f();
+    done_.fetch_or(bit, std::memory_order_acq_rel);
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+};
 
 // Per-device scratch shared by the GEMM split-K path (fp32 partials and
 // self-resetting tile counters) and the device error word.
