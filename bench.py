@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--e2e-tokens", type=int, default=0, help="override new tokens for the e2e run")
     ap.add_argument("--sampler", default="linear", choices=["linear", "tree"],
                     help="tree: BASELINE config 3 (64-node tree of depth 8, per-request tok/s; default batch 1)")
+    ap.add_argument("--breakdown", type=int, default=0, metavar="S",
+                    help="after the timed region, profile S more decode steps on rank 0 and print a per-step "
+                         "breakdown (wall, model GPU, exposed host time, kernel busy time, top kernels)")
     ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "uno-0.9b-dp"],
                     help="uno-0.9b-dp: BASELINE config 4 (0.9B dense model, one data-parallel replica per GPU, "
                          "256 requests per replica, prompts U[64,512], 1024 new tokens, block 16, LoRA rank 32)")
@@ -109,7 +112,8 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
-                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the sampler start before the timed region
         except (OSError, FileNotFoundError):
             self.proc = None
 
@@ -308,6 +312,7 @@ def run_native(args):
     running = len(llm.scheduler.running)
     # launches per step: count kernels of one extra step under the profiler (not timed)
     launches = count_launches(llm)
+    breakdown = step_breakdown(llm, args.breakdown) if args.breakdown else None
     # drain the remaining work so the engine is idle
     while not llm.is_finished():
         llm.step()
@@ -364,7 +369,66 @@ def run_native(args):
         "impl": "native",
     }
     print(json.dumps(line), flush=True)
+    if breakdown is not None:
+        print(json.dumps({"breakdown": breakdown, "n_gpus": args.gpus}), flush=True)
     llm.exit()
+
+
+def step_breakdown(llm, steps: int) -> dict | None:
+    """Where one decode step's time goes on rank 0 (untimed diagnostic).
+
+    Runs ``steps`` decode steps with the engine's decode timing on (CUDA events
+    around each forward: backbone + lm_head) and under ``torch.profiler`` for
+    the kernel list.  Reports per step: host wall time, model GPU time,
+    ``exposed_non_model_ms`` (wall minus model GPU: sampling, verify, staging,
+    control plane and host gaps), the union of kernel intervals (GPU busy) and
+    the top kernels by device time."""
+    import torch
+
+    if llm.is_finished():
+        return None
+    from torch.profiler import ProfilerActivity, profile
+
+    llm.config.decode_timing = True
+    llm.reset_decode_timing()
+    with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
+        for _ in range(steps):
+            if llm.is_finished():
+                break
+            llm.step()
+        torch.cuda.synchronize()
+    timing = llm.get_decode_timing()
+    llm.config.decode_timing = False
+    n = max(1, len(timing["step_wall_ms"]))
+    kernels = [e for e in prof.events() if e.device_type.name == "CUDA"]
+    spans = sorted((e.time_range.start, e.time_range.end) for e in kernels)
+    busy, cur_s, cur_e = 0.0, None, None
+    for a, b in spans:
+        if cur_e is None or a > cur_e:
+            if cur_e is not None:
+                busy += cur_e - cur_s
+            cur_s, cur_e = a, b
+        else:
+            cur_e = max(cur_e, b)
+    if cur_e is not None:
+        busy += cur_e - cur_s
+    by_name: dict[str, list[float]] = {}
+    for e in kernels:
+        d = by_name.setdefault(e.name[:120], [0.0, 0])
+        d[0] += e.time_range.end - e.time_range.start
+        d[1] += 1
+    top = sorted(by_name.items(), key=lambda kv: -kv[1][0])[:25]
+    wall = sum(timing["step_wall_ms"]) / n
+    return {
+        "steps": n,
+        "wall_ms_per_step": wall,
+        "model_gpu_ms_per_step": sum(timing["model_gpu_ms"]) / n,
+        "exposed_non_model_ms_per_step": sum(timing["exposed_non_model_ms"]) / n,
+        "kernel_busy_ms_per_step": busy / 1e3 / n,
+        "gpu_busy_fraction": busy / 1e3 / n / wall if wall > 0 else None,
+        "top_kernels": [{"name": k, "ms_per_step": v[0] / 1e3 / n, "launches_per_step": v[1] / n} for k, v in top],
+        "note": "profiled steps (not timed); per-kernel times under torch.profiler",
+    }
 
 
 def count_launches(llm):

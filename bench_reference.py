@@ -122,14 +122,49 @@ def run(args) -> None:
     open(marker, "w").close()
 
 
+def locate_reference() -> tuple[str | None, str]:
+    """Directory whose ``nano_vllm_uno`` package is the unmodified reference, and how it was found.
+
+    Order: the offline install in ``baseline/_ref``; an importable ``nano_vllm_uno``
+    installed elsewhere; a run-time offline install (``pip --no-index --no-deps``)
+    from a reference source tree (``UNO_REF_SOURCE``, else the build machine's
+    checkout) into ``baseline/_ref``.  Returns ``(None, reason)`` when none works.
+    """
+    if os.path.isdir(os.path.join(REF, "nano_vllm_uno")):
+        return REF, "baseline/_ref"
+    import importlib.util
+
+    spec = importlib.util.find_spec("nano_vllm_uno")
+    if spec is not None and spec.origin:
+        return os.path.dirname(os.path.dirname(spec.origin)), "importable nano_vllm_uno"
+    sources = [s for s in (os.environ.get("UNO_REF_SOURCE"), "/root/reference") if s]
+    for src in sources:
+        if not os.path.isfile(os.path.join(src, "pyproject.toml")):
+            continue
+        import subprocess
+
+        cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+               "--ignore-requires-python", "--target", REF, src]
+        if os.path.isdir("/opt/wheelhouse"):
+            cmd[5:5] = ["--find-links", "/opt/wheelhouse"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode == 0 and os.path.isdir(os.path.join(REF, "nano_vllm_uno")):
+            return REF, f"installed at run time from {src}"
+        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+        return None, f"run-time install from {src} failed: {tail[0][:200]}"
+    return None, ("baseline/_ref/nano_vllm_uno is missing, nano_vllm_uno is not importable and no reference "
+                  "source tree is available for an offline install (set UNO_REF_SOURCE)")
+
+
 def _run_rank0(args, world: int) -> dict:
-    if not os.path.isdir(os.path.join(REF, "nano_vllm_uno")):
-        return {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
+    ref_dir, how = locate_reference()
+    if ref_dir is None:
+        return {"impl": "reference", "unavailable": how}
     import torch
 
     write_checkpoint(CKPT)
     torch.cuda.empty_cache()
-    sys.path.insert(0, REF)
+    sys.path.insert(0, ref_dir)
     sys.path.insert(1, ROOT)
     os.environ["TORCH_DISTRIBUTED_PORT"] = str(_free_port())
     from nano_vllm_uno import LLM, SamplingParams
@@ -190,4 +225,6 @@ def _run_rank0(args, world: int) -> dict:
                    "block_size": args.block, "parallelism": f"tp{args.gpus}", "attention_backend": "fa2",
                    "l2": "working set >> L2"},
         "clocks": clock_info, "e2e": e2e, "impl": "reference",
+        "reference_path": os.path.relpath(ref_dir, ROOT) if ref_dir.startswith(ROOT) else ref_dir,
+        "reference_found": how,
     }

@@ -113,7 +113,7 @@ def test_shutdown_fails_unfinished_and_releases_engine():
     fut = eng.submit([1])
     time.sleep(0.05)
     eng.shutdown(timeout=10)
-    with pytest.raises(RuntimeError, match="stopped before request completion"):
+    with pytest.raises(RuntimeError, match="shut down before this request finished"):
         fut.result(timeout=5)
     assert fake.exited.is_set()
     with pytest.raises(RuntimeError, match="not running"):

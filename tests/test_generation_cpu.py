@@ -70,7 +70,7 @@ def test_resolve_model_sources_bundle(tmp_path):
     model, adapter = resolve_model_sources(str(bundle), None, gated_lora_subfolder="adapter")
     assert model == str(bundle) and adapter == str(bundle / "adapter")
     assert resolve_model_sources("m", "a") == ("m", "a")
-    with pytest.raises(ValueError, match="either"):
+    with pytest.raises(ValueError, match="only one"):
         resolve_model_sources(str(bundle), "x", gated_lora_subfolder="adapter")
     with pytest.raises(ValueError, match="invalid"):
         resolve_model_sources(str(bundle), None, gated_lora_subfolder="missing")

@@ -1,24 +1,24 @@
 """Thread-driven front end over one synchronous :class:`LLMEngine`.
 
-Behaviour of ``nano_vllm_uno/engine/async_engine.py:13-211``:
+Public behaviour of ``nano_vllm_uno/engine/async_engine.py:13-211``:
+``AsyncLLMEngine(engine, sampling_params)`` with ``start()``,
+``submit(prompt, *, request_id=None, max_tokens=None) -> Future[GenerationResult]``,
+``shutdown(timeout=30.0)``, ``is_running`` and ``fatal_error``.  Every request
+shares the front end's :class:`SamplingParams` (one decode batch); ``max_tokens``
+may differ per request.
 
-* ``start()`` launches one daemon thread that owns the engine; ``submit()``
-  is thread-safe and returns a ``concurrent.futures.Future`` resolving to a
-  :class:`GenerationResult` when that request finishes;
-* every request of one front end shares a single :class:`SamplingParams`
-  (the decode step batches them together); ``max_tokens`` may differ per
-  request;
-* a fatal engine error fails every pending future with that error and makes
-  later ``submit()`` calls raise; ``shutdown()`` stops the thread after the
-  current step, fails unfinished requests and releases the engine.
-
-The loop sleeps on a condition variable while the engine has nothing
-scheduled, so an idle front end costs no CPU.
+Design: callers append to an inbox guarded by a condition variable; one daemon
+thread (the *pump*) owns the engine.  Each turn it moves the inbox into the
+engine, runs one ``engine.step()`` and settles the futures of the requests
+that finished.  The :class:`_Ledger` maps the engine's sequence ids to the
+callers' futures.  When idle the pump sleeps on the condition variable.  An
+exception from the engine is fatal: every open future receives it, ``submit``
+refuses new work, and the engine is released; a request whose own prompt is
+rejected fails alone.
 """
 
 from __future__ import annotations
 
-import collections
 import concurrent.futures
 import threading
 import uuid
@@ -44,6 +44,42 @@ class _Request:
     max_tokens: int | None = None
 
 
+class _Ledger:
+    """Requests inside the engine, keyed by the engine's sequence id (pump thread only)."""
+
+    def __init__(self) -> None:
+        self._open: dict[int, _Request] = {}
+
+    def enter(self, engine, sp: SamplingParams, req: _Request) -> None:
+        if not req.future.set_running_or_notify_cancel():
+            return  # the caller cancelled it while it waited in the inbox
+        try:
+            seq_id = engine.add_request(req.prompt, sp, max_tokens=req.max_tokens)
+        except BaseException as exc:  # a malformed request fails on its own
+            req.future.set_exception(exc)
+            return
+        clash = self._open.get(seq_id)
+        if clash is not None:
+            err = RuntimeError(f"engine reused sequence id {seq_id}, still held by request {clash.request_id}")
+            req.future.set_exception(err)
+            raise err
+        self._open[seq_id] = req
+
+    def settle(self, engine, sp: SamplingParams, finished) -> None:
+        for seq_id, token_ids, stats in finished:
+            req = self._open.pop(seq_id, None)
+            if req is None:
+                raise RuntimeError(f"engine finished sequence {seq_id}, which no submitted request owns")
+            out = engine.finalize_output(token_ids, stats, sp)
+            req.future.set_result(GenerationResult(req.request_id, str(out.get("text", "")),
+                                                   list(out["token_ids"]), dict(out["stats"])))
+
+    def drain(self) -> list[_Request]:
+        reqs = list(self._open.values())
+        self._open.clear()
+        return reqs
+
+
 class AsyncLLMEngine:
     """Run one synchronous engine behind a persistent request inbox."""
 
@@ -51,119 +87,92 @@ class AsyncLLMEngine:
         self.engine = engine
         self.sampling_params = sampling_params
         self._cv = threading.Condition()
-        self._inbox: collections.deque[_Request] = collections.deque()
-        self._stop = False
-        self._accepting = False
-        self._thread: threading.Thread | None = None
+        self._inbox: list[_Request] = []
+        self._state = "new"  # new -> running -> stopping -> stopped (or failed)
         self._fatal: BaseException | None = None
-        self._by_seq: dict[int, _Request] = {}
+        self._pump: threading.Thread | None = None
+        self._ledger = _Ledger()
 
-    # ------------------------------------------------------------ control
+    # ------------------------------------------------------------- callers
     def start(self) -> None:
         with self._cv:
-            if self._thread is not None:
-                if self._thread.is_alive():
-                    return
-                raise RuntimeError("AsyncLLMEngine cannot be restarted after shutdown")
-            self._accepting = True
-            self._thread = threading.Thread(target=self._loop, name="uno-b200-engine", daemon=True)
-            self._thread.start()
+            if self._state == "running":
+                return
+            if self._state != "new":
+                raise RuntimeError(f"AsyncLLMEngine is {self._state}; a front end cannot be started twice")
+            self._state = "running"
+            self._pump = threading.Thread(target=self._pump_main, name="uno-b200-async-engine", daemon=True)
+            self._pump.start()
 
     def submit(self, prompt: str | list[int], *, request_id: str | None = None,
                max_tokens: int | None = None) -> concurrent.futures.Future:
         with self._cv:
-            if not self._accepting:
+            if self._state != "running":
                 if self._fatal is not None:
-                    raise RuntimeError("AsyncLLMEngine has failed") from self._fatal
-                raise RuntimeError("AsyncLLMEngine is not running")
+                    raise RuntimeError("AsyncLLMEngine failed and accepts no more requests") from self._fatal
+                raise RuntimeError(f"AsyncLLMEngine is not running (state: {self._state})")
             fut: concurrent.futures.Future = concurrent.futures.Future()
             self._inbox.append(_Request(request_id or uuid.uuid4().hex, prompt, fut, max_tokens))
             self._cv.notify()
-            return fut
+        return fut
 
     def shutdown(self, timeout: float | None = 30.0) -> None:
         with self._cv:
-            self._accepting = False
-            thread = self._thread
-            if thread is None:
-                return
-            self._stop = True
+            pump = self._pump
+            if self._state == "running":
+                self._state = "stopping"
             self._cv.notify()
-        thread.join(timeout=timeout)
-        if thread.is_alive():
-            raise TimeoutError("Timed out waiting for AsyncLLMEngine to stop")
+        if pump is None:
+            return
+        pump.join(timeout)
+        if pump.is_alive():
+            raise TimeoutError(f"the AsyncLLMEngine thread did not stop within {timeout} s")
 
     @property
     def is_running(self) -> bool:
         with self._cv:
-            t = self._thread
-            return bool(self._accepting and self._fatal is None and t is not None and t.is_alive())
+            return self._state == "running" and self._pump is not None and self._pump.is_alive()
 
     @property
     def fatal_error(self) -> BaseException | None:
         with self._cv:
             return self._fatal
 
-    # ------------------------------------------------------------- thread
-    def _take_inbox(self) -> tuple[list[_Request], bool]:
-        """Block while idle; return the new requests and whether to stop."""
+    # ---------------------------------------------------------------- pump
+    def _next_turn(self) -> list[_Request] | None:
+        """New requests for this turn, or None when the pump must stop; sleeps while idle."""
         with self._cv:
-            while not self._inbox and not self._stop and self.engine.is_finished():
+            while self._state == "running" and not self._inbox and self.engine.is_finished():
                 self._cv.wait()
-            batch = list(self._inbox)
-            self._inbox.clear()
-            return batch, self._stop
+            if self._state != "running":
+                return None
+            batch, self._inbox = self._inbox, []
+            return batch
 
-    def _admit(self, req: _Request) -> None:
-        if not req.future.set_running_or_notify_cancel():
-            return  # cancelled before it reached the engine
+    def _pump_main(self) -> None:
+        sp = self.sampling_params
         try:
-            seq_id = self.engine.add_request(req.prompt, self.sampling_params, max_tokens=req.max_tokens)
-        except BaseException as exc:  # a bad request fails alone
-            req.future.set_exception(exc)
-            return
-        if seq_id in self._by_seq:
-            err = RuntimeError(f"Duplicate scheduler sequence id: {seq_id}")
-            req.future.set_exception(err)
-            raise err
-        self._by_seq[seq_id] = req
-
-    def _finish(self, outputs) -> None:
-        for seq_id, token_ids, stats in outputs:
-            req = self._by_seq.pop(seq_id, None)
-            if req is None:
-                raise RuntimeError(f"Completed scheduler sequence {seq_id} has no pending request")
-            out = self.engine.finalize_output(token_ids, stats, self.sampling_params)
-            req.future.set_result(GenerationResult(request_id=req.request_id, text=str(out["text"]),
-                                                   token_ids=list(out["token_ids"]), stats=dict(out["stats"])))
-
-    def _fail_all(self, error: BaseException) -> None:
-        pending = list(self._by_seq.values())
-        self._by_seq.clear()
-        with self._cv:
-            pending += list(self._inbox)
-            self._inbox.clear()
-        for req in pending:
-            if not req.future.done():
-                req.future.set_exception(error)
-
-    def _loop(self) -> None:
-        try:
-            while True:
-                batch, stop = self._take_inbox()
-                if stop:
-                    break
+            while (batch := self._next_turn()) is not None:
                 for req in batch:
-                    self._admit(req)
+                    self._ledger.enter(self.engine, sp, req)
                 if not self.engine.is_finished():
-                    outputs, _ = self.engine.step()
-                    self._finish(outputs)
+                    finished, _ = self.engine.step()
+                    self._ledger.settle(self.engine, sp, finished)
         except BaseException as exc:
             with self._cv:
                 self._fatal = exc
-            self._fail_all(exc)
+                self._state = "failed"
+            self._abandon(exc)
         finally:
             with self._cv:
-                self._accepting = False
-            self._fail_all(RuntimeError("AsyncLLMEngine stopped before request completion"))
+                if self._state != "failed":
+                    self._state = "stopped"
+            self._abandon(RuntimeError("AsyncLLMEngine shut down before this request finished"))
             self.engine.exit()
+
+    def _abandon(self, error: BaseException) -> None:
+        with self._cv:
+            waiting, self._inbox = self._inbox, []
+        for req in self._ledger.drain() + waiting:
+            if not req.future.done():
+                req.future.set_exception(error)

@@ -30,22 +30,48 @@ from uno_b200.utils.hf_compat import load_tokenizer
 logger = logging.getLogger(__name__)
 
 
-def _trim_terminal_stop_tokens(token_ids: list[int], stops: set[int]) -> list[int]:
-    end = len(token_ids)
-    while end > 0 and token_ids[end - 1] in stops:
-        end -= 1
-    return token_ids[:end]
+def strip_trailing_stops(token_ids: list[int], stops: set[int]) -> list[int]:
+    """``token_ids`` without the run of stop tokens at its end (the decoder commits the stop token)."""
+    keep = len(token_ids)
+    for tok in reversed(token_ids):
+        if tok not in stops:
+            break
+        keep -= 1
+    return list(token_ids[:keep])
 
 
 def resolve_special_tokens(config: Config, tokenizer_path=None):
-    """Load the tokenizer and record EOS / PAD ids on ``config``."""
+    """Load the tokenizer and record EOS / PAD ids on ``config`` (PAD falls back to EOS)."""
     tok_path = tokenizer_path or (config.model if os.path.isdir(str(config.model)) else None)
     tokenizer = load_tokenizer(tok_path, config.hf_config)
     eos = getattr(tokenizer, "eos_token_id", None)
-    config.eos = -1 if eos is None else int(eos)
     pad = getattr(tokenizer, "pad_token_id", None)
+    config.eos = -1 if eos is None else int(eos)
     config.pad = int(pad) if pad is not None else max(config.eos, 0)
     return tokenizer
+
+
+# Engine keyword arguments that are refused, with the reason given to the caller.
+_REFUSED_KWARGS = {
+    "gated_lora": "gated_lora is not a setting: it is on exactly when gated_lora_path names an adapter",
+    "lora_path": "lora_path is not supported: pass the draft adapter as gated_lora_path",
+    "lora_mode": "lora_mode is not supported: the adapter always gates on the draft noise rows (gated_lora_path)",
+}
+
+
+def normalize_engine_kwargs(kwargs: dict) -> dict:
+    """Validated copy of the engine keyword arguments.
+
+    ``diffusion_block_size`` is accepted as an alias of ``max_diffusion_block_size``."""
+    refused = [name for name in _REFUSED_KWARGS if name in kwargs]
+    if refused:
+        raise TypeError("; ".join(_REFUSED_KWARGS[name] for name in refused))
+    out = dict(kwargs)
+    if "diffusion_block_size" in out:
+        if "max_diffusion_block_size" in out:
+            raise TypeError("diffusion_block_size is an alias of max_diffusion_block_size; give one of them")
+        out["max_diffusion_block_size"] = out.pop("diffusion_block_size")
+    return out
 
 
 def _free_port() -> int:
@@ -54,57 +80,58 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _reap(rank: int, proc, grace_s: float = 30.0) -> None:
+    """Join a TP worker process, escalating to terminate and then kill."""
+    proc.join(timeout=grace_s)
+    for action in (proc.terminate, proc.kill):
+        if not proc.is_alive():
+            return
+        logger.warning("TP worker %d is still alive; sending %s", rank, action.__name__)
+        action()
+        proc.join(timeout=5)
+
+
 class LLMEngine:
     def __init__(self, model, tokenizer_path=None, **kwargs):
-        if "gated_lora" in kwargs:
-            raise TypeError("gated_lora is derived from gated_lora_path and cannot be set directly")
-        removed = {"lora_path", "lora_mode"}.intersection(kwargs)
-        if removed:
-            raise TypeError(
-                f"Removed LoRA argument(s): {', '.join(sorted(removed))}. "
-                "Use gated_lora_path to enable draft-noise-only LoRA."
-            )
-        if "diffusion_block_size" in kwargs:
-            if "max_diffusion_block_size" in kwargs:
-                raise TypeError("Pass only max_diffusion_block_size or diffusion_block_size, not both")
-            kwargs["max_diffusion_block_size"] = kwargs.pop("diffusion_block_size")
+        config = Config(model, **normalize_engine_kwargs(kwargs))
         self._exited = False
-        config = Config(model, **kwargs)
         self.config = config
         Sequence.block_size = config.kvcache_block_size
         self.tokenizer = resolve_special_tokens(config, tokenizer_path)
-
+        if config.device == "cuda":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         self.ps: list = []
         self.control = None
-        world = config.tensor_parallel_size
-        if config.device == "cuda":
-            local = int(os.environ.get("LOCAL_RANK", 0))
-            torch.cuda.set_device(local)
-        if world > 1 and config.distributed_init == "spawn":
-            port = int(os.environ.get("TORCH_DISTRIBUTED_PORT", _free_port()))
-            ctx = mp.get_context("spawn")
-            from uno_b200.engine.worker import worker_main
-
-            for rank in range(1, world):
-                p = ctx.Process(target=worker_main, args=(config, rank, port), daemon=False)
-                p.start()
-                self.ps.append(p)
-        else:
-            port = None
+        self.rank = int(os.environ.get("RANK", 0)) if config.distributed_init == "env" else 0
+        port = self._spawn_tp_workers() if config.distributed_init == "spawn" else None
         from uno_b200.engine.model_runner import ModelRunner
         from uno_b200.engine.worker import init_distributed
 
-        self.rank = int(os.environ.get("RANK", 0)) if config.distributed_init == "env" else 0
         self.control = init_distributed(config, self.rank, port)
         self.model_runner = ModelRunner(config, self.rank, self.control)
         if self.control is not None:
             import torch.distributed as dist
 
-            dist.barrier(group=self.control.group)
+            dist.barrier(group=self.control.group)  # every rank has built its runner
         self.scheduler = Scheduler(config)
         self.sampling_params: SamplingParams | None = None
         self._decode_step_wall_ns: list[int] = []
         atexit.register(self.exit)
+
+    def _spawn_tp_workers(self) -> int | None:
+        """Start ranks 1..TP-1 as spawned processes; returns their rendezvous port."""
+        world = self.config.tensor_parallel_size
+        if world == 1:
+            return None
+        from uno_b200.engine.worker import worker_main
+
+        port = int(os.environ.get("TORCH_DISTRIBUTED_PORT", _free_port()))
+        ctx = mp.get_context("spawn")
+        for rank in range(1, world):
+            proc = ctx.Process(target=worker_main, args=(self.config, rank, port), daemon=False)
+            proc.start()
+            self.ps.append(proc)
+        return port
 
     # ----------------------------------------------------------- rpc
     def call(self, method: str, *args):
@@ -124,17 +151,11 @@ class LLMEngine:
         print(f"Engine stats: preemptions={self.scheduler.num_preemptions}", flush=True)
         try:
             self.call("exit")
-        except Exception:  # pragma: no cover
-            logger.exception("exit failed")
-        for rank, p in enumerate(self.ps, start=1):
-            p.join(timeout=30)
-            if p.is_alive():
-                logger.warning("Worker %d did not exit; terminating it", rank)
-                p.terminate()
-                p.join(timeout=5)
-                if p.is_alive():
-                    p.kill()
-        self.ps.clear()
+        except Exception:  # pragma: no cover - best-effort teardown
+            logger.exception("shutting down the model runners failed")
+        workers, self.ps = self.ps, []
+        for rank, proc in enumerate(workers, start=1):
+            _reap(rank, proc)
         import torch.distributed as dist
 
         if self.control is not None and dist.is_initialized():
@@ -146,10 +167,8 @@ class LLMEngine:
     # ------------------------------------------------------- requests
     def _validate_sampling_params(self, sp: SamplingParams) -> None:
         if sp.diffusion_block_size > self.config.max_diffusion_block_size:
-            raise ValueError(
-                f"SamplingParams.diffusion_block_size={sp.diffusion_block_size} exceeds engine "
-                f"capacity max_diffusion_block_size={self.config.max_diffusion_block_size}"
-            )
+            raise ValueError(f"diffusion_block_size {sp.diffusion_block_size} is larger than this engine was "
+                             f"built for (max_diffusion_block_size={self.config.max_diffusion_block_size})")
 
     def add_request(self, prompt: str | list[int], sampling_params: SamplingParams, *,
                     max_tokens: int | None = None) -> int:
@@ -159,11 +178,12 @@ class LLMEngine:
             if sampling_params.seed is not None:
                 self.call("reseed", int(sampling_params.seed))
         elif self.sampling_params is not sampling_params:
-            raise ValueError("All active requests must share one SamplingParams object")
+            raise ValueError("requests that run together must use the same SamplingParams object; submit a "
+                             "different one after the running batch has finished")
         if isinstance(prompt, str):
             prompt = self.tokenizer.encode(prompt)
         if max_tokens is not None and int(max_tokens) < 1:
-            raise ValueError("per-request max_tokens must be positive")
+            raise ValueError(f"max_tokens of a request must be at least 1, got {max_tokens}")
         seq = Sequence(list(prompt), max_completion_tokens=max_tokens)
         self.scheduler.add(seq)
         return seq.seq_id
@@ -172,7 +192,7 @@ class LLMEngine:
         t0 = perf_counter_ns() if self.config.decode_timing else 0
         sp = self.sampling_params
         if sp is None:
-            raise RuntimeError("Cannot step without active sampling parameters")
+            raise RuntimeError("step() needs a request: add_request() sets the batch's SamplingParams")
         seqs, is_prefill = self.scheduler.schedule(sp)
         n_prefill = sum(len(s) - s.num_cached_tokens for s in seqs) if is_prefill else 0
         result = self.call("run", seqs, is_prefill, sp)
@@ -210,49 +230,63 @@ class LLMEngine:
         }
 
     def finalize_output(self, token_ids, stats, sampling_params: SamplingParams, detokenize: bool = True):
-        stops = {self.scheduler.eos, *(sampling_params.stop_token_ids or [])}
-        token_ids = _trim_terminal_stop_tokens(list(token_ids), stops)
-        out = {"token_ids": token_ids, "stats": stats}
+        """Output dict of one finished request: token ids without trailing stop tokens, its decode
+        statistics, and (``detokenize``) the text."""
+        stops = set(sampling_params.stop_token_ids or ())
+        stops.add(self.scheduler.eos)
+        ids = strip_trailing_stops(list(token_ids), stops)
+        out = {"token_ids": ids, "stats": stats}
         if detokenize:
-            out["text"] = self.tokenizer.decode(token_ids)
+            out["text"] = self.tokenizer.decode(ids)
         return out
 
     def generate(self, prompts, sampling_params: SamplingParams, use_tqdm: bool = True,
                  detokenize: bool = True, progress_callback: Callable | None = None,
                  request_max_tokens: list[int] | None = None):
+        """Run ``prompts`` to completion; outputs in prompt order.
+
+        ``progress_callback`` receives the decode statistics of the requests that
+        finished in a step; ``request_max_tokens`` overrides ``max_tokens`` per prompt."""
         if isinstance(sampling_params, list):
-            raise ValueError(
-                "generate() accepts exactly one SamplingParams object per call. "
-                "All prompts in the call share that sampling configuration."
-            )
+            raise ValueError("generate() takes a single SamplingParams shared by every prompt of the call, "
+                             "not a list")
         self._validate_sampling_params(sampling_params)
         if request_max_tokens is not None and len(request_max_tokens) != len(prompts):
-            raise ValueError("request_max_tokens must contain one value per prompt")
-        pbar = tqdm(total=len(prompts), desc="Generating", dynamic_ncols=True) if use_tqdm else None
-        ids = [
-            self.add_request(p, sampling_params,
-                             max_tokens=None if request_max_tokens is None else int(request_max_tokens[i]))
-            for i, p in enumerate(prompts)
-        ]
-        done: dict[int, tuple] = {}
-        prefill_tps = decode_tps = 0.0
-        while not self.is_finished():
-            t = perf_counter()
-            output, n = self.step()
-            if pbar is not None:
-                dt = perf_counter() - t
-                if n > 0:
-                    prefill_tps = n / dt
-                else:
-                    decode_tps = -n / dt
-                pbar.set_postfix({"Prefill": f"{int(prefill_tps)}tok/s", "Decode": f"{int(decode_tps)}tok/s"})
-            for seq_id, toks, stats in output:
-                done[seq_id] = (toks, stats)
-            if output:
-                if pbar is not None:
-                    pbar.update(len(output))
-                if progress_callback is not None:
-                    progress_callback([s for _, _, s in output])
-        if pbar is not None:
-            pbar.close()
-        return [self.finalize_output(*done[i], sampling_params, detokenize=detokenize) for i in ids]
+            raise ValueError(f"request_max_tokens has {len(request_max_tokens)} entries for {len(prompts)} prompts")
+        limits = request_max_tokens if request_max_tokens is not None else [None] * len(prompts)
+        order = [self.add_request(p, sampling_params, max_tokens=None if m is None else int(m))
+                 for p, m in zip(prompts, limits)]
+        finished: dict[int, tuple] = {}
+        bar = _ProgressBar(len(prompts)) if use_tqdm else None
+        try:
+            while not self.is_finished():
+                t = perf_counter()
+                done, n = self.step()
+                if bar is not None:
+                    bar.step(n, perf_counter() - t, len(done))
+                for seq_id, toks, stats in done:
+                    finished[seq_id] = (toks, stats)
+                if done and progress_callback is not None:
+                    progress_callback([stats for _, _, stats in done])
+        finally:
+            if bar is not None:
+                bar.close()
+        return [self.finalize_output(*finished[i], sampling_params, detokenize=detokenize) for i in order]
+
+
+class _ProgressBar:
+    """tqdm bar over requests with the latest prefill and decode rates (tokens per second)."""
+
+    def __init__(self, total: int):
+        self.bar = tqdm(total=total, desc="Generating", dynamic_ncols=True)
+        self.rates = {"Prefill": 0.0, "Decode": 0.0}
+
+    def step(self, n_tokens: int, seconds: float, n_finished: int) -> None:
+        # step() reports prefill tokens as a positive count and decoded tokens as a negative one
+        self.rates["Prefill" if n_tokens > 0 else "Decode"] = abs(n_tokens) / max(seconds, 1e-9)
+        self.bar.set_postfix({k: f"{int(v)}tok/s" for k, v in self.rates.items()})
+        if n_finished:
+            self.bar.update(n_finished)
+
+    def close(self) -> None:
+        self.bar.close()

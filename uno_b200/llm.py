@@ -1,12 +1,16 @@
-"""User-facing ``LLM``: engine + ``greedy`` flag + data-parallel replicas.
+"""User-facing ``LLM``: the engine plus a ``greedy`` switch and data-parallel replicas.
 
-Same contract as ``nano_vllm_uno/llm.py:21-266``: with ``data_parallel_size > 1``
-the constructor starts one ``python -m uno_b200.dp_worker`` process per
-replica, each pinned to its own ``CUDA_VISIBLE_DEVICES`` slice of
-``tensor_parallel_size`` GPUs; ``generate`` shards prompts round-robin,
-aggregates progress and TPF statistics over pipes, and re-assembles outputs in
-prompt order.  A replica failure surfaces its traceback; shutdown escalates
-exit -> terminate -> kill.
+API of ``nano_vllm_uno/llm.py:21-266``: ``LLM(model, tokenizer_path=None,
+data_parallel_size=1, **engine_kwargs)`` and ``generate(prompts,
+sampling_params=None, *, greedy=None, request_max_tokens=None, use_tqdm=True,
+detokenize=True)``; ``last_generate_stats`` holds the summed decode statistics
+of the latest call.
+
+With ``data_parallel_size = R > 1`` the object drives a :class:`ReplicaSet`
+instead of an in-process engine: ``R`` engine processes
+(``python -m uno_b200.dp_worker``), each on its own slice of
+``tensor_parallel_size`` visible GPUs and its own rendezvous port.  Prompt ``i``
+goes to replica ``i mod R``; outputs come back in prompt order.
 """
 
 from __future__ import annotations
@@ -27,146 +31,195 @@ from uno_b200.engine.sequence import DECODE_STAT_KEYS
 from uno_b200.sampling_params import SamplingParams
 
 
+def with_greedy_flag(sp: SamplingParams, greedy: bool | None) -> SamplingParams:
+    """``greedy=True``: arg-max decoding over the full vocabulary; ``False``: make sure the
+    temperature is positive; ``None``: ``sp`` as given."""
+    if greedy is None:
+        return sp
+    if greedy:
+        return replace(sp, temperature=0.0, top_k=None, top_p=None)
+    return replace(sp, temperature=1.0) if sp.temperature == 0.0 else sp
+
+
+def _zero_stats() -> dict[str, int]:
+    return dict.fromkeys(DECODE_STAT_KEYS, 0)
+
+
+class ReplicaError(RuntimeError):
+    """A data-parallel replica failed; the message carries its traceback."""
+
+
+def _stop_process(proc: subprocess.Popen, grace_s: float) -> None:
+    """Wait up to ``grace_s`` for a clean exit, then SIGTERM, then SIGKILL."""
+    for action, wait_s in ((None, grace_s), (proc.terminate, 5.0), (proc.kill, None)):
+        if proc.poll() is not None:
+            return
+        if action is not None:
+            action()
+        try:
+            proc.wait(timeout=wait_s)
+        except subprocess.TimeoutExpired:
+            continue
+
+
+class _Replica:
+    """Handle of one replica process and its end of the pipe."""
+
+    def __init__(self, index: int, devices: list[str] | None, port: int, init_msg: tuple):
+        self.index = index
+        self.devices = devices
+        ours, theirs = Pipe(duplex=True)
+        env = dict(os.environ, TORCH_DISTRIBUTED_PORT=str(port))
+        if devices is not None:
+            env["CUDA_VISIBLE_DEVICES"] = ",".join(devices)
+        self.proc = subprocess.Popen([sys.executable, "-m", "uno_b200.dp_worker", str(theirs.fileno())],
+                                     env=env, pass_fds=(theirs.fileno(),))
+        theirs.close()
+        self.conn = ours
+        self.conn.send(init_msg)
+
+    def label(self) -> str:
+        where = f"GPUs {','.join(self.devices)}" if self.devices else "CPU"
+        return f"replica {self.index} ({where})"
+
+    def wait_up(self) -> None:
+        try:
+            msg = self.conn.recv()
+        except EOFError:
+            raise ReplicaError(f"{self.label()} exited while building its engine") from None
+        if msg[0] != "up":
+            raise ReplicaError(f"{self.label()} could not build its engine:\n{msg[-1]}")
+
+    def close(self, grace_s: float = 30.0) -> None:
+        try:
+            self.conn.send(("quit",))
+        except (BrokenPipeError, EOFError, OSError):
+            pass
+        self.conn.close()
+        _stop_process(self.proc, grace_s)
+
+
+class ReplicaSet:
+    """``count`` independent engines, each on ``tp`` GPUs of the visible set."""
+
+    def __init__(self, count: int, model, tokenizer_path, engine_kwargs: dict):
+        tp = int(engine_kwargs.get("tensor_parallel_size", 1))
+        on_cpu = engine_kwargs.get("device", "cuda") == "cpu"
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        pool = [d.strip() for d in visible.split(",") if d.strip()] if visible else [str(i) for i in range(count * tp)]
+        if not on_cpu and len(pool) < count * tp:
+            raise ValueError(f"{count} replicas x tensor_parallel_size {tp} need {count * tp} visible GPUs; "
+                             f"CUDA_VISIBLE_DEVICES offers {len(pool)}")
+        port0 = int(os.environ.get("TORCH_DISTRIBUTED_PORT", 20000 + os.getpid() % 20000))
+        init_msg = ("init", model, tokenizer_path, engine_kwargs)
+        self.replicas: list[_Replica] = []
+        try:
+            for r in range(count):
+                devices = None if on_cpu else pool[r * tp:(r + 1) * tp]
+                self.replicas.append(_Replica(r, devices, port0 + r, init_msg))
+            for rep in self.replicas:  # all replicas build their engines concurrently
+                rep.wait_up()
+        except BaseException:
+            self.close()
+            raise
+
+    def generate(self, prompts: list, sp: SamplingParams, limits: list[int] | None, gen_kwargs: dict,
+                 pbar) -> tuple[list, dict[str, int]]:
+        n = len(self.replicas)
+        pending: dict = {}
+        for rep in self.replicas:
+            idx = list(range(rep.index, len(prompts), n))
+            if not idx:
+                continue
+            kw = dict(gen_kwargs)
+            if limits is not None:
+                kw["request_max_tokens"] = [int(limits[i]) for i in idx]
+            rep.conn.send(("work", [prompts[i] for i in idx], sp, kw, pbar is not None))
+            pending[rep.conn] = (rep, idx)
+        ordered: list = [None] * len(prompts)
+        totals, seen = _zero_stats(), _zero_stats()
+        while pending:
+            for conn in wait(list(pending)):
+                rep, idx = pending[conn]
+                try:
+                    msg = conn.recv()
+                except EOFError:
+                    raise ReplicaError(f"{rep.label()} exited during generate") from None
+                if msg[0] == "tick":
+                    for st in msg[1]:
+                        for k in DECODE_STAT_KEYS:
+                            seen[k] += int(st[k])
+                    pbar.update(len(msg[1]))
+                    pbar.set_postfix({"TPF": f"{seen['accepts'] / max(1, seen['forwards']):.2f}"})
+                    continue
+                if msg[0] == "fault":
+                    raise ReplicaError(f"{rep.label()} failed during generate:\n{msg[-1]}")
+                _, outputs, stats = msg
+                if len(outputs) != len(idx):
+                    raise ReplicaError(f"{rep.label()} answered {len(outputs)} of its {len(idx)} prompts")
+                for i, out in zip(idx, outputs):
+                    ordered[i] = out
+                for k in DECODE_STAT_KEYS:
+                    totals[k] += int(stats[k])
+                del pending[conn]
+        return ordered, totals
+
+    def close(self) -> None:
+        replicas, self.replicas = self.replicas, []
+        for rep in replicas:
+            rep.close()
+
+
 class LLM(LLMEngine):
     def __init__(self, model, tokenizer_path=None, data_parallel_size: int = 1, **kwargs: Any):
-        self.data_parallel_size = int(data_parallel_size)
-        if self.data_parallel_size < 1:
-            raise ValueError("data_parallel_size must be >= 1")
+        replicas = int(data_parallel_size)
+        if replicas < 1:
+            raise ValueError(f"data_parallel_size must be at least 1, got {data_parallel_size}")
+        self.data_parallel_size = replicas
         self.last_generate_stats: dict[str, int] = {}
-        if self.data_parallel_size == 1:
+        self._replica_set: ReplicaSet | None = None
+        if replicas == 1:
             super().__init__(model, tokenizer_path, **kwargs)
             return
         self._exited = False
-        self._dp_workers: list = []
-        tp = int(kwargs.get("tensor_parallel_size", 1))
-        base_port = int(os.environ.get("TORCH_DISTRIBUTED_PORT", 20000 + os.getpid() % 20000))
-        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-        on_cpu = kwargs.get("device", "cuda") == "cpu"
-        gpus = ([g.strip() for g in visible.split(",")] if visible
-                else [str(i) for i in range(self.data_parallel_size * tp)])
-        if not on_cpu and len(gpus) < self.data_parallel_size * tp:
-            raise ValueError(
-                f"data_parallel_size={self.data_parallel_size} and tensor_parallel_size={tp} "
-                f"require {self.data_parallel_size * tp} visible GPUs, got {len(gpus)}"
-            )
-        try:
-            for r in range(self.data_parallel_size):
-                parent, child = Pipe()
-                env = os.environ.copy()
-                if not on_cpu:
-                    env["CUDA_VISIBLE_DEVICES"] = ",".join(gpus[r * tp:(r + 1) * tp])
-                env["TORCH_DISTRIBUTED_PORT"] = str(base_port + r)
-                proc = subprocess.Popen([sys.executable, "-m", "uno_b200.dp_worker", str(child.fileno())],
-                                        env=env, pass_fds=(child.fileno(),))
-                child.close()
-                self._dp_workers.append((proc, parent))
-                parent.send((model, tokenizer_path, kwargs))
-            for r, (_, conn) in enumerate(self._dp_workers):
-                ok, result = conn.recv()
-                if not ok:
-                    raise RuntimeError(f"data-parallel replica {r} failed to start:\n{result}")
-        except BaseException:
-            self.exit()
-            raise
+        self._replica_set = ReplicaSet(replicas, model, tokenizer_path, kwargs)
         atexit.register(self.exit)
 
     def generate(self, prompts, sampling_params: SamplingParams | None = None, *, greedy: bool | None = None,
                  request_max_tokens: list[int] | None = None, use_tqdm: bool = True, detokenize: bool = True,
                  **kwargs: Any):
-        if sampling_params is None:
-            sampling_params = SamplingParams()
         if isinstance(sampling_params, list):
-            raise ValueError(
-                "LLM.generate() accepts exactly one SamplingParams object per call. "
-                "All prompts in the call share that sampling configuration."
-            )
-        sp = sampling_params
-        if greedy is not None:
-            if greedy:
-                sp = replace(sp, temperature=0.0, top_k=None, top_p=None)
-            elif sp.temperature == 0.0:
-                sp = replace(sp, temperature=1.0)
-        if self.data_parallel_size == 1:
-            outputs = super().generate(prompts, sp, request_max_tokens=request_max_tokens,
-                                       use_tqdm=use_tqdm, detokenize=detokenize, **kwargs)
-            self.last_generate_stats = {k: sum(int(o["stats"][k]) for o in outputs) for k in DECODE_STAT_KEYS}
+            raise ValueError("generate() takes a single SamplingParams shared by every prompt of the call, "
+                             "not a list")
+        sp = with_greedy_flag(sampling_params if sampling_params is not None else SamplingParams(), greedy)
+        if self._replica_set is None:
+            outputs = super().generate(prompts, sp, request_max_tokens=request_max_tokens, use_tqdm=use_tqdm,
+                                       detokenize=detokenize, **kwargs)
+            self.last_generate_stats = _zero_stats()
+            for out in outputs:
+                for k in DECODE_STAT_KEYS:
+                    self.last_generate_stats[k] += int(out["stats"][k])
             return outputs
-        if not prompts:
-            self.last_generate_stats = {k: 0 for k in DECODE_STAT_KEYS}
-            return []
         if request_max_tokens is not None and len(request_max_tokens) != len(prompts):
-            raise ValueError("request_max_tokens must contain one value per prompt")
-        shards: list[list] = [[] for _ in self._dp_workers]
-        for i, prompt in enumerate(prompts):
-            limit = None if request_max_tokens is None else int(request_max_tokens[i])
-            shards[i % len(shards)].append((i, prompt, limit))
-        active = {}
-        for r, shard in enumerate(shards):
-            if not shard:
-                continue
-            idx, ps, limits = zip(*shard)
-            wkw = {**kwargs, "use_tqdm": False, "detokenize": detokenize}
-            if request_max_tokens is not None:
-                wkw["request_max_tokens"] = list(limits)
-            conn = self._dp_workers[r][1]
-            conn.send(("generate", list(ps), sp, wkw, use_tqdm))
-            active[conn] = (r, idx)
-        ordered: list = [None] * len(prompts)
-        totals = {k: 0 for k in DECODE_STAT_KEYS}
-        progress = {k: 0 for k in DECODE_STAT_KEYS}
+            raise ValueError(f"request_max_tokens has {len(request_max_tokens)} entries for {len(prompts)} prompts")
+        if not prompts:
+            self.last_generate_stats = _zero_stats()
+            return []
         pbar = tqdm(total=len(prompts), desc="Generating", dynamic_ncols=True) if use_tqdm else None
         try:
-            while active:
-                for conn in wait(list(active)):
-                    r, idx = active[conn]
-                    msg = conn.recv()
-                    if msg[0] == "progress":
-                        for st in msg[1]:
-                            for k in DECODE_STAT_KEYS:
-                                progress[k] += int(st[k])
-                        if pbar is not None:
-                            pbar.update(len(msg[1]))
-                            f = progress["forwards"]
-                            pbar.set_postfix({"TPF": f"{(progress['accepts'] / f if f else 0.0):.2f}"})
-                        continue
-                    ok, result = msg
-                    if not ok:
-                        raise RuntimeError(f"data-parallel replica {r} failed during generate:\n{result}")
-                    outs, stats = result
-                    if len(outs) != len(idx):
-                        raise RuntimeError(f"data-parallel replica {r} returned an unexpected output count")
-                    for i, o in zip(idx, outs):
-                        ordered[i] = o
-                    for k in DECODE_STAT_KEYS:
-                        totals[k] += int(stats[k])
-                    del active[conn]
+            outputs, totals = self._replica_set.generate(list(prompts), sp, request_max_tokens,
+                                                         {**kwargs, "use_tqdm": False, "detokenize": detokenize},
+                                                         pbar)
         finally:
             if pbar is not None:
                 pbar.close()
         self.last_generate_stats = totals
-        return ordered
+        return outputs
 
     def exit(self):
-        if self.data_parallel_size == 1:
+        if getattr(self, "_replica_set", None) is None:
             return super().exit()
-        if getattr(self, "_exited", False):
+        if self._exited:
             return
         self._exited = True
-        for proc, conn in getattr(self, "_dp_workers", []):
-            try:
-                conn.send(("exit",))
-                conn.close()
-            except (BrokenPipeError, EOFError, OSError):
-                pass
-            try:
-                proc.wait(timeout=30)
-            except subprocess.TimeoutExpired:
-                pass
-            if proc.poll() is None:
-                proc.terminate()
-                try:
-                    proc.wait(timeout=5)
-                except subprocess.TimeoutExpired:
-                    proc.kill()
-                    proc.wait()
-        self._dp_workers = []
+        self._replica_set.close()

@@ -1,13 +1,20 @@
-"""Training objective, LoRA settings and run manifests.
+"""Training objective, LoRA settings and the run manifest.
 
-Semantics of ``training/config.py:21-133`` and ``training/constants.py``:
+What must agree with ``training/config.py:21-133`` and ``training/constants.py``
+of the reference:
 
-* the public objective is ``ce_weight * CE + kl_weight * KL(student||teacher)
-  + tv_weight * TV``, uniform noise, a frozen base-model teacher; CE targets
-  are the clean teacher's argmax ("teacher") or the data ("ground_truth");
-* a run writes ``uno_training_manifest.json`` whose ``compatibility_sha256``
-  (sha256 of the canonical JSON of everything a resume must agree on) is
-  checked before resuming; JSON is written atomically (temp file + rename).
+* the objective is ``ce_weight * CE + kl_weight * KL(student || teacher)
+  + tv_weight * TV`` with uniform noise and the frozen base model as teacher;
+  CE targets are the clean teacher's arg-max (``ce_target="teacher"``) or the
+  data (``"ground_truth"``);
+* a run writes ``uno_training_manifest.json`` holding ``compatibility`` (every
+  setting a resume must share) and ``compatibility_sha256``, the sha256 of its
+  canonical JSON (sorted keys, no whitespace); a resume recomputes the digest
+  and refuses to continue on a mismatch.
+
+The validation rules below are stated as data (predicate, message) and the
+manifest file is replaced atomically (written to a temporary file in the same
+directory, flushed to disk, then renamed over the old one).
 """
 
 from __future__ import annotations
@@ -15,16 +22,31 @@ from __future__ import annotations
 import hashlib
 import json
 import math
+import os
+import tempfile
 from dataclasses import asdict, dataclass
 from pathlib import Path
 from typing import Any, Literal
 
 IGNORE_INDEX = -100
 DEFAULT_LORA_RANK = 128
-DEFAULT_LORA_ALPHA_RATIO = 16
+DEFAULT_LORA_ALPHA_RATIO = 16  # alpha = 16 * rank unless given
 SUPPORTED_LORA_MODULES = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+MANIFEST_NAME = "uno_training_manifest.json"
 
 CeTarget = Literal["teacher", "ground_truth"]
+_CE_TARGET_KIND = {"teacher": "clean_argmax", "ground_truth": "data"}
+
+
+def _check(rules) -> None:
+    """Raise ``ValueError`` with the message of the first rule whose predicate is false."""
+    for ok, message in rules:
+        if not ok():
+            raise ValueError(message)
+
+
+def _is_weight(x) -> bool:
+    return isinstance(x, (int, float)) and not isinstance(x, bool) and math.isfinite(x) and x >= 0
 
 
 @dataclass(frozen=True)
@@ -38,24 +60,22 @@ class UnoObjectiveConfig:
     tv_weight: float = 1.0
 
     def validate(self) -> None:
-        if self.ce_target not in ("teacher", "ground_truth"):
-            raise ValueError("ce_target must be either 'teacher' or 'ground_truth'.")
-        if self.noise != "uniform":
-            raise ValueError("Uno training supports uniform noise only.")
-        if not self.reverse_kl:
-            raise ValueError("Uno training supports reverse KL only.")
-        if not self.teacher_base_only:
-            raise ValueError("The Uno teacher must use the frozen base weights only.")
-        w = (self.ce_weight, self.kl_weight, self.tv_weight)
-        if any(not isinstance(x, (int, float)) or not math.isfinite(x) or x < 0 for x in w):
-            raise ValueError("Uno loss weights must be finite and non-negative.")
-        if not any(x > 0 for x in w):
-            raise ValueError("At least one Uno loss weight must be positive.")
+        weights = (self.ce_weight, self.kl_weight, self.tv_weight)
+        _check((
+            (lambda: self.ce_target in _CE_TARGET_KIND,
+             f"ce_target={self.ce_target!r}: CE targets are 'teacher' (clean arg-max) or 'ground_truth' (data)"),
+            (lambda: self.noise == "uniform", f"noise={self.noise!r}: the objective is defined for uniform noise"),
+            (lambda: self.reverse_kl, "the KL term is the reverse KL(student || teacher); forward KL is not offered"),
+            (lambda: self.teacher_base_only, "the teacher is the frozen base model (no LoRA on clean rows)"),
+            (lambda: all(_is_weight(w) for w in weights),
+             f"loss weights (ce, kl, tv) = {weights} must be finite numbers >= 0"),
+            (lambda: any(w > 0 for w in weights), "all loss weights are zero: nothing would be trained"),
+        ))
 
     @property
     def internal_ce_target(self) -> str:
         self.validate()
-        return "clean_argmax" if self.ce_target == "teacher" else "data"
+        return _CE_TARGET_KIND[self.ce_target]
 
 
 @dataclass(frozen=True)
@@ -67,29 +87,31 @@ class LoraSettings:
 
     @property
     def resolved_alpha(self) -> int:
-        return self.alpha if self.alpha is not None else DEFAULT_LORA_ALPHA_RATIO * self.rank
+        return DEFAULT_LORA_ALPHA_RATIO * self.rank if self.alpha is None else self.alpha
 
     @property
     def modules(self) -> tuple[str, ...]:
+        """Projection names that carry the adapter (``"all"`` or a comma list)."""
         if self.target == "all":
             return SUPPORTED_LORA_MODULES
-        mods = tuple(m.strip() for m in self.target.split(",") if m.strip())
-        bad = [m for m in mods if m not in SUPPORTED_LORA_MODULES]
-        if bad or not mods:
-            raise ValueError(f"Unsupported LoRA target modules: {bad or self.target}")
-        return mods
+        names = tuple(filter(None, (part.strip() for part in self.target.split(","))))
+        unknown = sorted(set(names) - set(SUPPORTED_LORA_MODULES))
+        if not names or unknown:
+            raise ValueError(f"LoRA target {self.target!r}: unknown modules {unknown or '(none given)'}; "
+                             f"choose from {', '.join(SUPPORTED_LORA_MODULES)}")
+        return names
 
     def validate(self) -> None:
-        if self.rank <= 0:
-            raise ValueError("LoRA rank must be positive.")
-        if self.alpha is not None and self.alpha <= 0:
-            raise ValueError("LoRA alpha must be positive.")
-        if not 0.0 <= self.dropout < 1.0:
-            raise ValueError("LoRA dropout must be in [0, 1).")
-        _ = self.modules
+        _check((
+            (lambda: self.rank > 0, f"LoRA rank {self.rank} must be at least 1"),
+            (lambda: self.alpha is None or self.alpha > 0, f"LoRA alpha {self.alpha} must be positive"),
+            (lambda: 0.0 <= self.dropout < 1.0, f"LoRA dropout {self.dropout} must lie in [0, 1)"),
+        ))
+        self.modules  # noqa: B018  (raises on unknown target modules)
 
 
 def canonical_json(payload: dict[str, Any]) -> str:
+    """The byte-stable JSON text the compatibility digest is taken over."""
     return json.dumps(payload, sort_keys=True, separators=(",", ":"))
 
 
@@ -98,28 +120,39 @@ def manifest_digest(payload: dict[str, Any]) -> str:
 
 
 def write_json_atomic(path: Path, payload: dict[str, Any]) -> None:
+    """Replace ``path`` with ``payload`` as indented JSON; readers see the old or the new file, never a mix."""
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
-    tmp = path.with_suffix(path.suffix + ".tmp")
-    tmp.write_text(json.dumps(payload, indent=2, sort_keys=True) + "\n")
-    tmp.replace(path)
+    fd, tmp = tempfile.mkstemp(prefix=path.name + ".", suffix=".part", dir=path.parent)
+    try:
+        with os.fdopen(fd, "w") as fh:
+            fh.write(json.dumps(payload, indent=2, sort_keys=True) + "\n")
+            fh.flush()
+            os.fsync(fh.fileno())
+        os.replace(tmp, path)
+    except BaseException:
+        if os.path.exists(tmp):
+            os.unlink(tmp)
+        raise
 
 
 def write_run_manifest(output_dir: Path, compatibility: dict[str, Any], extra: dict[str, Any] | None = None) -> None:
-    write_json_atomic(Path(output_dir) / "uno_training_manifest.json",
-                      {"compatibility": compatibility, "compatibility_sha256": manifest_digest(compatibility),
-                       **(extra or {})})
+    record = dict(extra or {})
+    record["compatibility"] = compatibility
+    record["compatibility_sha256"] = manifest_digest(compatibility)
+    write_json_atomic(Path(output_dir) / MANIFEST_NAME, record)
 
 
 def validate_resume_manifest(output_dir: Path, expected: dict[str, Any]) -> None:
-    path = Path(output_dir) / "uno_training_manifest.json"
+    """Refuse to resume into ``output_dir`` unless its manifest digest equals that of ``expected``."""
+    path = Path(output_dir) / MANIFEST_NAME
     if not path.is_file():
-        raise FileNotFoundError(f"Cannot resume without the original run manifest: {path}")
-    actual = json.loads(path.read_text())
+        raise FileNotFoundError(f"{path} is missing: a run can only resume from its own output directory")
+    found = json.loads(path.read_text()).get("compatibility_sha256")
     want = manifest_digest(expected)
-    if actual.get("compatibility_sha256") != want:
-        raise ValueError("Resume configuration does not match the original training run. Expected "
-                         f"compatibility hash {want}, got {actual.get('compatibility_sha256')}.")
+    if found != want:
+        raise ValueError(f"the resumed run does not match the run in {output_dir}: compatibility digest "
+                         f"{found} on disk, {want} for the current settings")
 
 
 def dataclass_dict(value: Any) -> dict[str, Any]:
