@@ -21,7 +21,8 @@ def run(fsdp: bool, group):
     from uno_b200.train.forward import uno_hidden_states
     from uno_b200.train.native import build_projections
 
-    model, lora, opt, ub = _setup()
+    # every projection's output rows split into 64-row multiples over up to 8 ranks
+    model, lora, opt, ub = _setup(head_dim=128, hidden=512, heads=8, kv_heads=4, inter=1024)
     proj, sharded = build_projections(model, lora, group=group, fsdp=fsdp)
     for layer in proj:
         for p in layer.values():

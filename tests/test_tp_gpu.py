@@ -31,8 +31,11 @@ def _run(world: int, comm: str, eager: bool = False) -> dict:
     return json.loads(line)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world", [2])
+WORLDS = [pytest.param(w, marks=pytest.mark.skipif(torch.cuda.device_count() < w, reason=f"needs {w} GPUs"))
+          for w in (2, 4, 8)]
+
+
+@pytest.mark.parametrize("world", WORLDS)
 def test_fused_tp_matches_nccl_and_single_gpu(world):
     one = _run(1, "fused")
     nccl = _run(world, "nccl")
@@ -62,28 +65,27 @@ def _run_vp(world: int) -> str:
     return out.stdout
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", WORLDS)
 def test_vocab_parallel_sampling_matches_full_vocab(world):
     """Each rank holds a vocab shard; the exchanged results equal the single-GPU kernels on the full rows."""
     out = _run_vp(world)
     assert "VP_OK" in out, out[-3000:]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_zero2_adamw_matches_torch_adamw():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_zero2_adamw_matches_torch_adamw(world):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", TORCH_DISTRIBUTED_TIMEOUT_MINUTES="2")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "optim_worker.py")]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "OPT_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fsdp_sharded_projection_gemms_match_replicated():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fsdp_sharded_projection_gemms_match_replicated(world):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", TORCH_DISTRIBUTED_TIMEOUT_MINUTES="2",
                PYTHONPATH=HERE + os.pathsep + os.environ.get("PYTHONPATH", ""))
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "fsdp_worker.py")]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "FSDP_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]

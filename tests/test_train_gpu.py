@@ -6,15 +6,15 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _setup(seed=0, head_dim=64):
+def _setup(seed=0, head_dim=64, hidden=256, heads=4, kv_heads=2, inter=768):
     from uno_b200.models.decoder import build_model
     from uno_b200.train import LoraSettings, TrainableLoRA, build_uno_batch
     from uno_b200.train.optim import ShardedLoraAdamW
     from uno_b200.utils.hf_compat import ModelConfig
     from uno_b200.utils.loader import dummy_init
 
-    cfg = ModelConfig(model_type="qwen3", vocab_size=4096, hidden_size=256, intermediate_size=768,
-                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=head_dim,
+    cfg = ModelConfig(model_type="qwen3", vocab_size=4096, hidden_size=hidden, intermediate_size=inter,
+                      num_hidden_layers=2, num_attention_heads=heads, num_key_value_heads=kv_heads, head_dim=head_dim,
                       max_position_embeddings=2048, mask_token_id=4095, rope_theta=1e6)
     torch.set_default_dtype(torch.bfloat16)
     with torch.device("cuda"):

@@ -17,8 +17,9 @@ from uno_b200.utils.hf_compat import ModelConfig  # noqa: E402
 
 
 def main():
+    # 8 KV heads so that the model shards over up to 8 ranks
     cfg = ModelConfig(model_type="qwen3", vocab_size=4096, hidden_size=1024, intermediate_size=2048,
-                      num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=4, head_dim=128,
+                      num_hidden_layers=3, num_attention_heads=16, num_key_value_heads=8, head_dim=128,
                       max_position_embeddings=2048, eos_token_id=None, mask_token_id=4000)
     eager = os.environ.get("TP_TEST_EAGER", "0") == "1"
     kw = dict(max_num_seqs=4, max_model_len=512, kvcache_block_size=64, dummy_lora_rank=64,
