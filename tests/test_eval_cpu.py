@@ -260,3 +260,44 @@ def test_ifeval_grade_strict_loose_and_scoring(tmp_path):
     assert g["loose_inst_follow"] == [True, True] and g["loose_prompt_follow"] and g["correct"] is False
     row = {"generation": "hello bye", "ground_truth": truth}
     assert grade_row(row, None, task="ifeval", parser="passthrough")["correct"] is True
+
+
+def test_lcb_grader_stdin_functional_and_failures():
+    import json
+
+    from uno_b200.eval.lcb import extract_python_code, pass_at_k, score_lcb
+
+    assert extract_python_code("text\n```python\nprint(1)\n```\nmore ```py\nprint(2)\n```") == "print(2)"
+    assert extract_python_code("no fences") == "no fences"
+    stdin = json.dumps([{"input": "3 4\n", "output": "7\n", "testtype": "stdin"},
+                        {"input": "1.5 2\n", "output": "3.50\n", "testtype": "stdin"}])
+    func = json.dumps([{"input": "[1,2]\n3", "output": "[1, 2, 3]", "testtype": "functional", "method_name": "f"}])
+    rows = [
+        {"ground_truth": stdin, "generations": [
+            "```python\na, b = map(float, input().split())\nr = a + b\nprint(int(r) if r == int(r) else r)\n```",
+            "print(5)",                                    # wrong answer
+            "```python\nwhile True:\n    pass\n```",       # time limit
+            "```python\nraise ValueError()\n```"]},        # runtime error
+        {"ground_truth": func, "generation": "class Solution:\n    def f(self, a, b):\n        return tuple(a + [b])\n"},
+    ]
+    graded, summary = score_lcb(rows, timeout=2, workers=4)
+    assert graded[0]["correct"] == [True, False, False, False]
+    assert graded[0]["test_results"][1:] == [[-2], [-3], [-4]]
+    assert graded[1]["correct"] == [True]
+    assert summary["num_correct"] == 2 and abs(summary["pass@1"] - (0.25 + 1.0) / 2) < 1e-9
+    assert pass_at_k(5, 0, 1) == 0.0 and pass_at_k(5, 5, 5) == 1.0 and abs(pass_at_k(4, 1, 1) - 0.25) < 1e-12
+
+
+def test_lcr_grader_parses_json_grade():
+    from uno_b200.eval.graders import grade_lcr
+
+    seen = []
+
+    def judge(payload):
+        seen.append(payload)
+        return 'Reasoning... {"GRADE": "CORRECT"}' if "Paris" in payload["messages"][0]["content"] else "{}"
+
+    assert grade_lcr("Capital of France?", "<think>hmm</think>Paris", "Paris", transport=judge, model="m")["correct"]
+    assert not grade_lcr("Capital of France?", "Lyon", "Lyon is wrong", transport=lambda p: "INCORRECT",
+                         model="m")["correct"]
+    assert seen[0]["model"] == "m" and seen[0]["temperature"] == 0

@@ -45,15 +45,41 @@ def test_sequence_rollback_bounds():
     assert s.num_cached_tokens == 4
 
 
-def test_sequence_worker_state_roundtrip():
-    s = Sequence([5, 6, 7, 8, 9])
-    s.block_table = [3, 1]
-    s.num_cached_tokens = 4
-    st = s.to_worker_state(include_token_ids=False)
-    t = Sequence.from_worker_state(st)
-    assert len(t) == 5 and t.last_token == 9 and t.block_table == [3, 1] and t.num_cached_tokens == 4
-    st = s.to_worker_state(include_token_ids=True)
-    assert Sequence.from_worker_state(st).token_ids == s.token_ids
+def test_run_command_roundtrip_through_the_channel():
+    """A packed ``run`` command rebuilds the follower's view of every sequence."""
+    from uno_b200.engine.control import CommandChannel, RunDecoder, RunEncoder, TokenTail
+    from uno_b200.sampling_params import SamplingParams
+
+    a = Sequence([5, 6, 7, 8, 9], max_completion_tokens=7)
+    a.block_table = [3, 1]
+    a.num_cached_tokens = 4
+    b = Sequence(list(range(1, 300)))
+    b.block_table = [0, 2, 4]
+    b.num_cached_tokens = 298
+    sp = SamplingParams(temperature=1.0, max_tokens=8, diffusion_block_size=4, mask_token_id=90,
+                        noise_mode="deterministic_uniform")
+    ch = CommandChannel(None, 0, 1, size=1 << 16)
+    try:
+        enc, dec = RunEncoder(), RunDecoder()
+        for prefill in (True, False, False):
+            n = enc.encode(ch.begin_write(), [a, b], prefill, sp)
+            seqs, is_prefill, sp2 = dec.decode(bytes(ch.payload[:n]))
+            assert is_prefill == prefill and sp2 == sp
+            for src, got in zip((a, b), seqs):
+                assert (got.seq_id, len(got), got.last_token, got.num_cached_tokens, got.block_table,
+                        got.num_prompt_tokens, got.max_completion_tokens) == \
+                       (src.seq_id, len(src), src.last_token, src.num_cached_tokens, src.block_table,
+                        src.num_prompt_tokens, src.max_completion_tokens)
+                assert got.noise_seed == src.noise_seed is not None  # deterministic noise needs the prompt hash
+                if prefill:
+                    assert got.token_ids == src.token_ids
+                else:
+                    assert isinstance(got.token_ids, TokenTail)
+        tail = TokenTail(3, 7)
+        tail.extend([8, 9])
+        assert len(tail) == 5 and tail[-1] == 9
+    finally:
+        ch.close()
 
 
 def test_prefix_cache_hit_and_reactivation():

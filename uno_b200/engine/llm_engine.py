@@ -137,11 +137,7 @@ class LLMEngine:
     def call(self, method: str, *args):
         """Run ``method`` on every TP rank (rank 0 broadcasts the command)."""
         if self.control is not None and self.rank == 0:
-            payload = args
-            if method == "run":
-                seqs, is_prefill, sp = args
-                payload = ([s.to_worker_state(include_token_ids=is_prefill) for s in seqs], is_prefill, sp)
-            self.control.send(method, payload)
+            self.control.send(method, args)
         return getattr(self.model_runner, method)(*args)
 
     def exit(self) -> None:
@@ -158,8 +154,10 @@ class LLMEngine:
             _reap(rank, proc)
         import torch.distributed as dist
 
-        if self.control is not None and dist.is_initialized():
-            dist.destroy_process_group()
+        if self.control is not None:
+            self.control.close()
+            if dist.is_initialized():
+                dist.destroy_process_group()
 
     def get_stats(self) -> dict[str, int]:
         return {"preemptions": self.scheduler.num_preemptions}

@@ -385,7 +385,8 @@ class ModelRunner:
 
         cfg = self.config.hf_config
         cuda_ops.reserve_attention_scratch(self.device, ws.max_tokens,
-                                           cfg.num_attention_heads // self.world_size, 16)
+                                           cfg.num_attention_heads // self.world_size, 16,
+                                           max(1, cfg.num_key_value_heads // self.world_size))
         torch.cuda.synchronize()
         free0 = torch.cuda.mem_get_info()[0]
         pool = torch.cuda.graph_pool_handle()

@@ -124,41 +124,6 @@ class Sequence:
             )
         self.num_cached_tokens = target
 
-    # ------------------------------------------------- TP wire representation
-    def to_worker_state(self, include_token_ids: bool) -> tuple:
-        """Compact state for TP follower ranks (tokens only for prefill)."""
-        return (
-            self.seq_id,
-            self.status.value,
-            self.token_ids if include_token_ids else None,
-            self.token_ids[-1],
-            len(self.token_ids),
-            self.num_prompt_tokens,
-            self.num_cached_tokens,
-            self.block_table,
-            self.max_completion_tokens,
-        )
-
-    @classmethod
-    def from_worker_state(cls, state: tuple) -> "Sequence":
-        (seq_id, status, token_ids, last_token, num_tokens, num_prompt,
-         num_cached, block_table, max_completion) = state
-        seq = object.__new__(cls)
-        seq.seq_id = seq_id
-        seq.status = SequenceStatus(status)
-        if token_ids is None:
-            # Followers only need the length and the seed token; keep a list
-            # of the right length whose last element is the seed.
-            token_ids = [0] * (num_tokens - 1) + [last_token]
-        seq.token_ids = list(token_ids)
-        seq.num_prompt_tokens = num_prompt
-        seq.num_cached_tokens = num_cached
-        seq.block_table = list(block_table)
-        seq.stats = new_decode_stats()
-        seq.max_completion_tokens = max_completion
-        seq.noise_seed = None
-        return seq
-
     def __repr__(self) -> str:  # pragma: no cover - debugging aid
         return (
             f"Sequence(id={self.seq_id}, len={len(self)}, cached={self.num_cached_tokens}, "

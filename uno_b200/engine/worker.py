@@ -1,12 +1,13 @@
-"""Tensor-parallel worker processes and the rank-0 -> followers control plane.
+"""Tensor-parallel worker processes and their set-up.
 
 Reference: followers block on an ``mp.Event`` and read pickled commands from a
 64 MiB POSIX shared-memory segment (``nano_vllm_uno/engine/model_runner.py:154-255``).
-Here the command channel is a gloo process group on the host: rank 0 calls
-``broadcast_object_list`` with ``(method, args)`` and every follower executes
-the same method on its own :class:`ModelRunner`.  The data plane (activations,
-logits) stays on NCCL.  The same code path serves engines that spawn their
-own ranks and jobs started by ``torchrun`` (``distributed_init="env"``).
+Here rank 0 writes each command into a fixed-layout shared-memory slot
+(``engine/control.py``) and every follower executes the same method on its own
+:class:`ModelRunner`; a gloo group carries set-up and barriers, the data plane
+(activations, logits) stays on NCCL and the fused peer-memory kernels.  The
+same code path serves engines that spawn their own ranks and jobs started by
+``torchrun`` (``distributed_init="env"``).
 """
 
 from __future__ import annotations
@@ -18,25 +19,10 @@ import traceback
 import torch
 import torch.distributed as dist
 
-from uno_b200.engine.sequence import Sequence
+from uno_b200.engine.control import ChannelControlPlane
 from uno_b200.parallel import state as tp
 
 logger = logging.getLogger(__name__)
-
-
-class ControlPlane:
-    def __init__(self, group, rank: int, world: int):
-        self.group = group
-        self.rank = rank
-        self.world = world
-
-    def send(self, method: str, args: tuple) -> None:
-        dist.broadcast_object_list([method, args], src=0, group=self.group)
-
-    def recv(self):
-        box = [None, None]
-        dist.broadcast_object_list(box, src=0, group=self.group)
-        return box[0], box[1]
 
 
 def init_distributed(config, rank: int, port: int | None = None):
@@ -56,19 +42,19 @@ def init_distributed(config, rank: int, port: int | None = None):
     backend = "nccl" if on_gpu else "gloo"
     tp.init_tp(world, rank, backend=backend, init_method=init_method)
     control = dist.new_group(backend="gloo") if on_gpu else dist.group.WORLD
-    return ControlPlane(control, rank, world)
+    minutes = float(os.environ.get("TORCH_DISTRIBUTED_TIMEOUT_MINUTES", "10"))
+    return ChannelControlPlane.create(control, rank, world, timeout_s=60.0 * minutes)
 
 
-def follower_loop(runner, control: ControlPlane) -> None:
-    while True:
-        method, args = control.recv()
-        if method == "run":
-            states, is_prefill, sp = args
-            args = ([Sequence.from_worker_state(s) for s in states], is_prefill, sp)
-        fn = getattr(runner, method)
-        fn(*args)
-        if method == "exit":
-            break
+def follower_loop(runner, control: ChannelControlPlane) -> None:
+    try:
+        while True:
+            method, args = control.recv()
+            getattr(runner, method)(*args)
+            if method == "exit":
+                break
+    finally:
+        control.close()
 
 
 def worker_main(config, rank: int, port: int, ready=None) -> None:

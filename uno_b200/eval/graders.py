@@ -171,3 +171,38 @@ def grade_with_judge(question: str, answer: Any, response: str, *, model: str, t
                    question=question, answer=answer, response=strip_reasoning(response))}]}
     verdict = transport(payload).strip().upper()
     return {"judge": verdict[:64], "correct": verdict.startswith("CORRECT")}
+
+
+# ------------------------------------------------------------------ AA-LCR
+# Behaviour of ``evaluation/graders/lcr.py``: a judge model sees the question,
+# the candidate answer and the reference answer and must reply with a JSON
+# grade; anything without a parsable ``"GRADE"`` counts as incorrect.  The
+# endpoint and model come from UNO_LCR_JUDGE_URL / UNO_LCR_JUDGE_MODEL (key:
+# UNO_LCR_JUDGE_API_KEY); a base URL without ``/v1`` gets it appended.
+LCR_TEMPLATE = ("Decide whether the candidate answer to the question below is semantically correct, using the "
+                "reference answer as ground truth. Respond with only {{\"GRADE\":\"CORRECT\"}} or "
+                "{{\"GRADE\":\"INCORRECT\"}}.\n\nQuestion:\n{question}\n\nCandidate answer:\n{answer}\n\n"
+                "Reference answer:\n{reference}")
+_LCR_GRADE = re.compile(r'"GRADE"\s*:\s*"(CORRECT|INCORRECT)"', re.IGNORECASE)
+
+
+def lcr_transport_from_env() -> Callable:
+    url = os.environ.get("UNO_LCR_JUDGE_URL")
+    if not url or not os.environ.get("UNO_LCR_JUDGE_MODEL"):
+        raise RuntimeError("AA-LCR grading needs UNO_LCR_JUDGE_URL and UNO_LCR_JUDGE_MODEL")
+    url = url.rstrip("/")
+    if not url.endswith("/v1"):
+        url += "/v1"
+    return http_chat_transport(url, os.environ.get("UNO_LCR_JUDGE_API_KEY"))
+
+
+def grade_lcr(question: str, answer: str, reference: Any, *, transport: Callable | None = None,
+              model: str | None = None) -> dict:
+    transport = transport or lcr_transport_from_env()
+    model = model or os.environ.get("UNO_LCR_JUDGE_MODEL", "judge")
+    payload = {"model": model, "temperature": 0, "max_tokens": 32,
+               "messages": [{"role": "user", "content": LCR_TEMPLATE.format(
+                   question=question, answer=strip_reasoning(answer), reference=reference)}]}
+    reply = transport(payload)
+    m = _LCR_GRADE.search(reply or "")
+    return {"judge": (reply or "")[:256], "correct": bool(m) and m.group(1).upper() == "CORRECT"}

@@ -2,6 +2,8 @@
 
 Routing by task: multiple-choice parsers grade letters; ``humaneval`` /
 ``mbpp`` (and any ``code_completion`` parser) run the sandboxed code grader;
+LiveCodeBench rows run their stdin / functional tests (``eval/lcb.py``);
+AA-LCR asks its judge for a JSON grade;
 benchmarks with a judge use the LLM judge when a transport is given (else the
 rows are reported as ungraded); ``ifeval`` uses the instruction checkers of ``eval/ifeval.py``;
 everything else is graded as math (boxed answer equivalence).  Scores are
@@ -30,6 +32,18 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
 
         prompt = row.get("question") or (record or {}).get("prompt", "")
         return grade_ifeval(gen, truth if truth is not None else (record or {}), prompt)
+    if task in ("lcb", "lcbv6", "livecodebench"):
+        from uno_b200.eval.lcb import extract_python_code, generation_passed, parse_tests, run_generation
+
+        codes = run_generation(extract_python_code(gen), parse_tests(truth), int(timeout))
+        return {"correct": generation_passed(codes), "test_results": codes}
+    if task == "aa_lcr":
+        from uno_b200.eval.graders import grade_lcr
+
+        if judge is None:
+            return {"correct": None, "status": "ungraded: no judge endpoint"}
+        question = row.get("question") or row.get("completion_input") or (record or {}).get("question", "")
+        return grade_lcr(question, gen, truth, transport=judge, model=judge_model)
     if parser == "mc_answer":
         return grade_multiple_choice(parse_generation("mc_answer", gen), truth)
     if parser == "code_completion" or task in ("humaneval", "mbpp"):
@@ -47,10 +61,10 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
 def score_file(generations: str | Path, *, benchmark: str | None = None, data: str | Path | None = None,
                parser: str | None = None, grades_out: str | Path | None = None,
                scores_out: str | Path | None = None, summary: str | Path | None = None,
-               judge: Callable | None = None) -> dict[str, Any]:
+               judge: Callable | None = None, task: str | None = None) -> dict[str, Any]:
     rows = read_jsonl(generations)
     bench = get_benchmark(benchmark) if benchmark else None
-    task = bench.task if bench else "math"
+    task = task or (bench.task if bench else "math")
     parser = parser or (bench.parser if bench else "passthrough")
     records = {}
     if data is not None:

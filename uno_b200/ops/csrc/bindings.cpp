@@ -272,11 +272,96 @@ static void attention(const at::Tensor& q, at::Tensor& o, const at::Tensor& k_ca
   paged_attention_launch(a, cur_stream());
 }
 
+static void attention_tc(const at::Tensor& q, at::Tensor& o, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                         const at::Tensor& block_tables, c10::optional<at::Tensor> prefix_lens,
+                         c10::optional<at::Tensor> suffix_mask, c10::optional<at::Tensor> cu_q,
+                         c10::optional<at::Tensor> cu_k, int64_t mode, int64_t B, int64_t Q, double scale,
+                         at::Tensor& o_part, at::Tensor& lse_part, at::Tensor& counters,
+                         c10::optional<at::Tensor> trace) {
+  check_dev(q, "q");
+  check_dev(o, "attention output");
+  check_dev(k_cache, "k_cache");
+  check_dev(v_cache, "v_cache");
+  check_dev(block_tables, "block_tables");
+  check_dev(o_part, "attention o_part");
+  check_dev(lse_part, "attention lse_part");
+  check_dev(counters, "attention counters");
+  UNO_CHECK_BF16(q);
+  UNO_CHECK_CONTIG(q);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "KV cache must be contiguous");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt, "block_tables must be int32");
+  TORCH_CHECK(o.is_contiguous() && o.numel() == q.numel(), "attention output must match q");
+  TORCH_CHECK(counters.scalar_type() == at::kInt, "attention counters must be int32");
+  const int rows = attention_tc_rows();
+  const int64_t slots = 2LL * num_sms();
+  TORCH_CHECK(o_part.scalar_type() == at::kFloat && o_part.numel() >= slots * rows * 128,
+              "attention o_part needs ", slots * rows * 128, " floats");
+  TORCH_CHECK(lse_part.scalar_type() == at::kFloat && lse_part.numel() >= slots * rows,
+              "attention lse_part needs ", slots * rows, " floats");
+  TORCH_CHECK(counters.numel() >= q.size(0) * k_cache.size(1), "attention counters need T * kv_heads ints");
+  if (mode == 0) {
+    TORCH_CHECK(prefix_lens.has_value() && suffix_mask.has_value(), "decode attention needs prefix_lens and masks");
+    TORCH_CHECK(prefix_lens->scalar_type() == at::kInt && suffix_mask->scalar_type() == at::kLong,
+                "prefix_lens int32, suffix_mask int64");
+    TORCH_CHECK(prefix_lens->numel() >= B && suffix_mask->numel() >= B * Q && q.size(0) >= B * Q,
+                "decode attention metadata too short");
+    check_dev(*prefix_lens, "prefix_lens");
+    check_dev(*suffix_mask, "suffix_mask");
+  } else {
+    TORCH_CHECK(cu_q.has_value() && cu_k.has_value(), "prefill attention needs cu_seqlens");
+    TORCH_CHECK(cu_q->scalar_type() == at::kInt && cu_k->scalar_type() == at::kInt, "cu_seqlens must be int32");
+    TORCH_CHECK(cu_q->numel() >= B + 1 && cu_k->numel() >= B + 1, "cu_seqlens too short");
+    check_dev(*cu_q, "cu_seqlens_q");
+    check_dev(*cu_k, "cu_seqlens_k");
+  }
+  AttnLaunch a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.o_part = o_part.data_ptr<float>();
+  a.lse_part = lse_part.data_ptr<float>();
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.num_pages = k_cache.size(0);
+  a.hkv = k_cache.size(1);
+  a.page = k_cache.size(2);
+  a.head_dim = k_cache.size(3);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = block_tables.stride(0);
+  a.prefix_lens = ptr_or_null<const int>(prefix_lens);
+  a.suffix_mask = ptr_or_null<const int64_t>(suffix_mask);
+  a.cu_q = ptr_or_null<const int>(cu_q);
+  a.cu_k = ptr_or_null<const int>(cu_k);
+  a.B = B;
+  a.Q = Q;
+  a.T = q.size(0);
+  a.max_q = Q;
+  a.hq = q.size(1);
+  a.scale = scale;
+  a.mode = mode;
+  a.num_splits = 1;
+  a.keys_per_split = 0;
+  a.err = device_error_flag();
+  if (a.T == 0 || B == 0) return;
+  unsigned long long* tr = nullptr;
+  if (trace.has_value()) {
+    check_dev(*trace, "attention trace");
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 10 * 64, "trace needs 640 int64");
+    tr = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
+  attention_tc_launch(a, counters.data_ptr<int>(), cur_stream(), tr);
+}
+
 }  // namespace uno
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &uno::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("rms_norm", &uno::rms_norm);
+  m.def("attention_tc", &uno::attention_tc, "tcgen05 paged attention (persistent, balanced tile ranges)",
+        py::arg("q"), py::arg("o"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_tables"),
+        py::arg("prefix_lens"), py::arg("suffix_mask"), py::arg("cu_q"), py::arg("cu_k"), py::arg("mode"),
+        py::arg("B"), py::arg("Q"), py::arg("scale"), py::arg("o_part"), py::arg("lse_part"), py::arg("counters"),
+        py::arg("trace") = py::none());
+  m.def("attention_tc_rows", &uno::attention_tc_rows);
   m.def("embedding", &uno::embedding_launch);
   m.def("silu_mul", &uno::silu_mul_launch);
   m.def("qk_norm_rope_store", &uno::qk_norm_rope_store_launch);

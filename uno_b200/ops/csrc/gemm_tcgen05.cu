@@ -846,6 +846,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride
 // `ld` elements; box = [64 cols, box_rows rows], 128-byte swizzle.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return get_encode(); }
+
 CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");

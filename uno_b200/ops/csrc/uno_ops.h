@@ -125,6 +125,13 @@ struct AttnLaunch {
   int* err;
 };
 void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream);
+// tcgen05 paged attention (attention_tc.cu): one persistent CTA per SM; o_part
+// holds 2 * SMs * rows * 128 floats, lse_part 2 * SMs * rows, counters T * hkv
+// ints that are zero between launches (the kernel resets the ones it uses).
+void attention_tc_launch(const AttnLaunch& a, int* counters, cudaStream_t stream,
+                         unsigned long long* trace = nullptr);
+int attention_tc_rows();
+int num_sms();
 
 // Control block at the start of every rank's symmetric workspace (comm.cu):
 // u64 epoch, u32 CTA counter, u32 pad, u64 arrive[8], u64 done[8].

@@ -240,10 +240,12 @@ def _scratch(device, numel: int, name: str) -> torch.Tensor:
     return buf[:numel]
 
 
-def reserve_attention_scratch(device, max_tokens: int, num_heads: int, max_splits: int) -> None:
-    """Pre-size the split-K scratch so graph capture never reallocates it."""
+def reserve_attention_scratch(device, max_tokens: int, num_heads: int, max_splits: int,
+                              num_kv_heads: int = 8) -> None:
+    """Pre-size the attention scratch so graph capture never reallocates it."""
     _scratch(device, max_splits * max_tokens * num_heads * 128, "o_part")
     _scratch(device, max_splits * max_tokens * num_heads, "lse")
+    _attention_scratch(device, max_tokens * num_kv_heads)
 
 
 def plan_splits(B: int, hkv: int, qblocks: int, max_kv: int, sms: int = 148):
@@ -259,9 +261,41 @@ def plan_splits(B: int, hkv: int, qblocks: int, max_kv: int, sms: int = 148):
     return splits, kps
 
 
+_ATT_IMPL = os.environ.get("UNO_ATTN_IMPL", "mma")
+
+
+def _attention_scratch(device, rows_needed: int):
+    """Partials (two slots per SM), their log-sum-exps and the per-segment arrival counters."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    rows = ext().attention_tc_rows() if hasattr(ext(), "attention_tc_rows") else 32
+    o_part = _scratch(device, 2 * sms * rows * 128, "att_o_part")
+    lse = _scratch(device, 2 * sms * rows, "att_lse")
+    key = (device, "att_counters")
+    cnt = _SCRATCH.get(key)
+    if cnt is None or cnt.numel() < rows_needed:
+        cnt = torch.zeros(max(rows_needed, 1), device=device, dtype=torch.int32)
+        _SCRATCH[key] = cnt
+    return o_part, lse, cnt
+
+
 def attention(q, k_cache, v_cache, meta: ForwardMeta, scale):
     T, hq, d = q.shape
     o = torch.empty(T, hq * d, device=q.device, dtype=torch.bfloat16)
+    hkv = k_cache.shape[1]
+    if _ATT_IMPL == "mma":
+        return _attention_mma(q, k_cache, v_cache, meta, scale, o)
+    o_part, lse, cnt = _attention_scratch(q.device, T * hkv)
+    if meta.mode is Mode.PREFILL:
+        ext().attention_tc(q, o, k_cache, v_cache, meta.block_tables, None, None, meta.cu_seqlens_q,
+                           meta.cu_seqlens_k, 1, meta.batch_size, 0, float(scale), o_part, lse, cnt)
+    else:
+        ext().attention_tc(q, o, k_cache, v_cache, meta.block_tables, meta.prefix_lens, meta.suffix_mask, None,
+                           None, 0, meta.batch_size, meta.seqlen_q, float(scale), o_part, lse, cnt)
+    return o
+
+
+def _attention_mma(q, k_cache, v_cache, meta, scale, o):
+    T, hq, d = q.shape
     hkv = k_cache.shape[1]
     if meta.mode is Mode.PREFILL:
         ext().attention(q, o, k_cache, v_cache, meta.block_tables, None, None, meta.cu_seqlens_q,
