@@ -301,3 +301,55 @@ def test_lcr_grader_parses_json_grade():
     assert not grade_lcr("Capital of France?", "Lyon", "Lyon is wrong", transport=lambda p: "INCORRECT",
                          model="m")["correct"]
     assert seen[0]["model"] == "m" and seen[0]["temperature"] == 0
+
+
+def test_prepare_installs_pinned_artifact_and_rejects_mismatch(tmp_path, monkeypatch):
+    import hashlib
+
+    from uno_b200.eval import benchmarks as B
+    from uno_b200.eval.prepare import prepare_benchmark_data
+
+    body = "".join('{"row": %d, "ground_truth": "1"}\n' % i for i in range(30)).encode()
+    sha = hashlib.sha256(body).hexdigest()
+    cfg = B.BENCHMARKS["aime24"]
+    monkeypatch.setitem(B.BENCHMARKS, "aime24", type(cfg)(**{**cfg.__dict__, "data_sha256": sha}))
+    src = tmp_path / "src"
+    (src / "aime-2024").mkdir(parents=True)
+    (src / "aime-2024" / "aime-2024.jsonl").write_bytes(body)     # repository-shaped bundle
+    out = prepare_benchmark_data("aime-24", output_dir=tmp_path / "out", source_dir=src)
+    assert out.read_bytes() == body
+    assert prepare_benchmark_data("aime24", output_dir=tmp_path / "out") == out   # re-validated, not rebuilt
+    (src / "aime24.jsonl").write_bytes(body.replace(b'"1"', b'"2"'))              # flat bundle wins, wrong bytes
+    with pytest.raises(ValueError, match="sha256"):
+        prepare_benchmark_data("aime24", output_dir=tmp_path / "o2", source_dir=src)
+
+
+def test_prepare_builders_render_protocol_prompts():
+    import base64
+    import json
+    import pickle
+    import zlib
+
+    from uno_b200.eval.prepare import build_gpqa, build_lcb, build_mbpp, decode_lcb_tests, gpqa_order
+
+    row = {"Question": "What is 2+2?", "Correct Answer": "4", "Incorrect Answer 1": "3",
+           "Incorrect Answer 2": "5", "Incorrect Answer 3": "22"}
+    rec = build_gpqa([row])[0]
+    order = gpqa_order(row["Question"])
+    assert sorted(order) == [0, 1, 2, 3] and order == gpqa_order(row["Question"])
+    assert rec["ground_truth"] == "ABCD"[order.index(0)]
+    assert f"{rec['ground_truth']}) 4" in rec["completion_input"]
+    shots = [{"task_id": t, "text": f"task {t}", "test_list": [f"assert f{t}()"], "code": f"def f{t}(): return 1"}
+             for t in (2, 3, 4)]
+    mb = build_mbpp([{"task_id": 11, "text": "do it", "test_list": ["assert g()"]}], shots)[0]
+    assert mb["completion_input"].count("[DONE]") == 3 and mb["completion_input"].endswith("assert g()\n[BEGIN]\n")
+    tests = [{"input": "1\n", "output": "1\n", "testtype": "stdin"}]
+    packed = base64.b64encode(zlib.compress(pickle.dumps(json.dumps(tests)))).decode()
+    assert decode_lcb_tests(packed) == tests
+    evil = base64.b64encode(zlib.compress(pickle.dumps(OSError("x")))).decode()
+    with pytest.raises(pickle.UnpicklingError):
+        decode_lcb_tests(evil)
+    lcb = build_lcb([{"question_content": "Sum.", "public_test_cases": json.dumps(tests),
+                      "private_test_cases": packed, "metadata": json.dumps({"func_name": "f"}), "starter_code": "x"}])[0]
+    assert len(json.loads(lcb["ground_truth"])) == 2 and json.loads(lcb["ground_truth"])[0]["method_name"] == "f"
+    assert lcb["chat_input"][0]["role"] == "system" and "```python\nx\n```" in lcb["chat_input"][1]["content"]

@@ -384,3 +384,33 @@ def test_data_parallel_resume_from_boundary_matches_uninterrupted(tmp_path):
         p.join(30)
     assert (tmp_path / "checkpoint-2" / "trainer_state_rank1.pt").is_file()
     assert all(same for _, same, _ in out), out
+
+
+def test_openthoughts_encoding_budget_alignment_and_hash(tmp_path):
+    import json
+
+    from uno_b200.train.prepare import corpus_hash, encode_conversation, prepare, split_budget
+
+    class Tok:  # one token per character; pad id 0
+        pad_token_id = 0
+
+        def encode(self, text, add_special_tokens=False):
+            return [1 + (ord(c) % 200) for c in text]
+
+    assert split_budget(10, 10, 100) == (10, 10)
+    assert split_budget(10, 80, 100) == (10, 80)       # prompt under half: the answer gets the rest
+    assert split_budget(80, 80, 100) == (50, 50)       # proportional split
+    conv = [{"from": "human", "value": "hi"}, {"from": "gpt", "value": "yo"}]
+    enc = encode_conversation(conv, Tok(), cutoff=4096, align=3)
+    n_src = len("<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n")
+    assert enc["labels"][:n_src] == [-100] * n_src and len(enc["input_ids"]) % 3 == 0
+    assert enc["labels"][n_src:n_src + len("<think>\n")] == Tok().encode("<think>\n")   # empty think block added
+    long = [{"from": "human", "value": "q" * 5000}, {"from": "gpt", "value": "a" * 5000}]
+    assert len(encode_conversation(long, Tok(), cutoff=4096, align=3)["input_ids"]) <= 4095
+    h1 = corpus_hash([enc])
+    assert h1["row_count"] == 1 and h1["supervised_token_count"] == sum(t != -100 for t in enc["labels"])
+    src = tmp_path / "src.jsonl"
+    src.write_text("\n".join(json.dumps({"conversations": conv}) for _ in range(3)) + "\n")
+    man = prepare(str(src), tmp_path / "out", Tok())
+    assert man["hash"]["row_count"] == 3
+    prepare(str(src), tmp_path / "again", Tok(), verify_against=tmp_path / "out")   # same corpus verifies

@@ -52,26 +52,34 @@ namespace {
 constexpr int TD = 128;                  // head dim
 constexpr int TBK = 128;                 // keys per tile
 constexpr int TR = 32;                   // rows (query, head) per segment
-constexpr int TSTAGES = 3;
+constexpr int KSTAGES = 2;               // K tiles in flight (freed when S = K.Q^T completes)
+constexpr int VSTAGES = 3;               // V tiles in flight (freed when O += V^T.P completes)
 constexpr int REGION = TBK * 128;        // 128 keys x 64 dims (128 B rows): 16 KB
 constexpr int KV_BYTES = 2 * REGION;     // one K or V tile (two 64-dim regions)
-constexpr int STAGE_BYTES = 2 * KV_BYTES;
-constexpr int QP_REGION = TR * 128;      // 32 rows x 64 dims (or 64 keys)
+constexpr int QP_REGION = TR * 128;      // 32 rows x 64 dims (Q) or 32 rows x 64 keys (P)
 constexpr int QP_BYTES = 2 * QP_REGION;
 constexpr int TMAX_B = 256;
-constexpr int NTHREADS = 192;
+constexpr int HR = TR / 2;               // rows per softmax warp (two warps share a TMEM lane quarter)
+constexpr int NTHREADS = 480;            // producer, S issuer, 8 softmax, 4 epilogue warps, P.V issuer
 constexpr int TMEM_COLS = 128;           // S[2] and O[2], TR columns each
 
-constexpr int OFF_KV = 0;
-constexpr int OFF_Q = OFF_KV + TSTAGES * STAGE_BYTES;
+constexpr int OFF_K = 0;
+constexpr int OFF_V = OFF_K + KSTAGES * KV_BYTES;
+constexpr int OFF_Q = OFF_V + VSTAGES * KV_BYTES;
 constexpr int OFF_P = OFF_Q + 2 * QP_BYTES;
-constexpr int OFF_BAR = OFF_P + QP_BYTES;
-constexpr int NUM_BARS = 2 * TSTAGES + 4 + 4 + 2 + 4;
-constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;      // tmem base, abort, last flag
-constexpr int OFF_RED = OFF_MISC + 16;                 // float [4][TR]
-constexpr int OFF_FIN = OFF_RED + 4 * TR * 4;          // float [TR]
-constexpr int OFF_MASK = OFF_FIN + TR * 4;             // int64 [TR]
-constexpr int OFF_PREFIX = OFF_MASK + TR * 8;          // int [TMAX_B + 1]
+constexpr int OFF_BAR = OFF_P + 2 * QP_BYTES;
+constexpr int NUM_BARS = 2 * KSTAGES + 2 * VSTAGES + 7 * 4 + 2;
+constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;       // tmem base, abort, last flag
+constexpr int OFF_RED = OFF_MISC + 16;                 // float [8 warps][HR] per-warp row maxima / sums
+constexpr int OFF_MSM = OFF_RED + 8 * HR * 4;          // float [TR] running row maxima
+constexpr int OFF_CSM = OFF_MSM + TR * 4;              // float [TR] last correction factors
+constexpr int OFF_LFIN = OFF_CSM + TR * 4;             // float [2][TR] row sums per O buffer
+constexpr int OFF_MFIN = OFF_LFIN + 2 * TR * 4;        // float [2][TR] row maxima per O buffer
+constexpr int OFF_COL = OFF_MFIN + 2 * TR * 4;         // u32 [2 halves][64] rows that see suffix key j
+constexpr int OFF_SMASK = OFF_COL + 2 * 64 * 4;        // int64 [2][TR] suffix masks of a piece's queries
+constexpr int OFF_TROWS = OFF_SMASK + 2 * TR * 8;      // int2 [8] cache rows of queued tiles (K -> V)
+constexpr int OFF_CMB = OFF_TROWS + 8 * 8;             // float [2][TR] merge maxima / inverse sums
+constexpr int OFF_PREFIX = OFF_CMB + 2 * TR * 4;       // int [TMAX_B + 1]
 constexpr int SMEM_USED = OFF_PREFIX + (TMAX_B + 1) * 4;
 constexpr int SMEM_TOTAL = SMEM_USED + 1024;           // alignment slack
 static_assert(SMEM_TOTAL <= 232448, "attention shared memory budget");
@@ -89,6 +97,7 @@ struct TcParams {
   const int* cu_q;
   const int* cu_k;
   int B, Q, T, hq, hkv, group, page, mode, qpb;
+  int group_shift;  // log2(group): rows are (query << group_shift) | head-in-group
   float scale_log2;
   int* err;
   unsigned long long* trace;  // optional timeline of CTA 0: [event][tile] globaltimer stamps
@@ -256,6 +265,18 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
                "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
@@ -290,23 +311,6 @@ __device__ __forceinline__ void bar_named(int id, int nthreads) {
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// After the call, lane l holds the sum (or max) over the warp of v[l].
-template <bool MAX>
-__device__ __forceinline__ float transpose_reduce32(float (&v)[TR], int lane) {
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) {
-    const bool upper = (lane & s) != 0;
-#pragma unroll
-    for (int i = 0; i < s; ++i) {
-      const float send = upper ? v[i] : v[i + s];
-      const float keep = upper ? v[i + s] : v[i];
-      const float got = __shfl_xor_sync(0xffffffff, send, s);
-      v[i] = MAX ? fmaxf(keep, got) : keep + got;
-    }
-  }
-  return v[0];
-}
-
 // MN-major (V^T) operand: 64-dim groups REGION bytes apart, 8-key groups 1024 B apart.
 __device__ __forceinline__ uint64_t desc_v_mn(const void* smem) {
   uint64_t addr = smem_u32(smem);
@@ -325,29 +329,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const __grid_constant__ CUtensorMap tmQ, TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sKV = smem + OFF_KV;
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
   uint8_t* sQ = smem + OFF_Q;
   uint8_t* sP = smem + OFF_P;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = bars + TSTAGES;
-  uint64_t* q_full = bars + 2 * TSTAGES;
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = k_full + KSTAGES;
+  uint64_t* v_full = k_empty + KSTAGES;
+  uint64_t* v_empty = v_full + VSTAGES;
+  uint64_t* q_full = v_empty + VSTAGES;
   uint64_t* q_empty = q_full + 2;
   uint64_t* s_full = q_empty + 2;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
-  uint64_t* p_empty = p_full + 1;
-  uint64_t* o_full = p_empty + 1;
+  uint64_t* p_empty = p_full + 2;
+  uint64_t* o_full = p_empty + 2;
   uint64_t* o_empty = o_full + 2;
+  uint64_t* l_full = o_empty + 2;
+  uint64_t* drain_bar = l_full + 2;  // [0] S issuer, [1] P.V issuer: final commit before TMEM is freed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
   float* red = reinterpret_cast<float*>(smem + OFF_RED);
-  float* fin = reinterpret_cast<float*>(smem + OFF_FIN);
-  int64_t* rmask = reinterpret_cast<int64_t*>(smem + OFF_MASK);
+  float* msm = reinterpret_cast<float*>(smem + OFF_MSM);
+  float* csm = reinterpret_cast<float*>(smem + OFF_CSM);
+  float* lfin = reinterpret_cast<float*>(smem + OFF_LFIN);
+  float* mfin = reinterpret_cast<float*>(smem + OFF_MFIN);
+  uint32_t* colmask = reinterpret_cast<uint32_t*>(smem + OFF_COL);
+  int64_t* smask_sm = reinterpret_cast<int64_t*>(smem + OFF_SMASK);
+  int2* trows = reinterpret_cast<int2*>(smem + OFF_TROWS);
+  float* cmb = reinterpret_cast<float*>(smem + OFF_CMB);
   int* prefix = reinterpret_cast<int*>(smem + OFF_PREFIX);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0 && p.trace != nullptr) p.trace[1024 + 4 * blockIdx.x] = globaltimer_ns();
 
   // ---- tile counts per request and their prefix sums
   for (int b = threadIdx.x; b < p.B; b += NTHREADS) {
@@ -364,20 +380,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     prefix[0] = 0;
     *abort_flag = 0;
-    for (int s = 0; s < TSTAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KSTAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VSTAGES; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], 8);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&p_empty[i], 1);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 4);
+      mbar_init(&l_full[i], 2);
+      mbar_init(&drain_bar[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -395,6 +417,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int G = (int)min((long long)gridDim.x, max(TT, 1LL));
   const bool active = (int)blockIdx.x < G;
   if (threadIdx.x == 0) ATT_TRACE(9, 0);
+  if (threadIdx.x == 0 && p.trace != nullptr) p.trace[1024 + 4 * blockIdx.x + 1] = globaltimer_ns();
   const long long x_begin = active ? range_begin(blockIdx.x, TT, G) : 0;
   const long long x_end = active ? range_begin(blockIdx.x + 1, TT, G) : 0;
 
@@ -404,88 +427,138 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmQ);
+      // K loads run ahead of V loads: the K cursor walks the pieces (loading Q and the
+      // piece metadata first) and queues each tile's cache rows; the V cursor follows.
       Walker w;
       w.init(p, prefix, x_begin, x_end);
-      int stage = 0;
-      uint32_t phase = 0;
-      int qn = 0;
-      int pt = 0;
-      uint32_t issued = 0, issued_phase = 0;  // bit s: stage s has a load in flight / its phase
+      const long long n_tiles = x_end - x_begin;
+      int kn = 0, vn = 0, qn = 0;
+      int t_cur = 0, t_end = 0, cur_b = 0, cur_h = 0, cur_len = 0;  // K cursor inside the current piece
+      const int* bt = nullptr;
+      uint32_t kin = 0, vin = 0;  // bit s: a load into stage s may still be in flight
+      uint64_t idle_since = 0;
       bool ok = true;
-      while (ok && !w.done()) {
-        const Piece pc = w.next(p, prefix);
-        const ReqGeo g = req_geo(p, pc.b);
-        // Q rows of this segment: queries i0.., heads h*group..
-        const int qb = qn & 1;
-        if (!wait_or_abort(&q_empty[qb], ((qn >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
-        mbar_arrive_expect_tx(&q_full[qb], QP_BYTES);
-        const int z = g.q_begin + pc.rb * p.qpb;
-        tma_load_3d(sQ + qb * QP_BYTES, &tmQ, &q_full[qb], 0, pc.h * p.group, z);
-        tma_load_3d(sQ + qb * QP_BYTES + QP_REGION, &tmQ, &q_full[qb], 64, pc.h * p.group, z);
-        ++qn;
-        const int* bt = p.block_tables + (size_t)pc.b * p.bt_stride;
-        for (int t = pc.t0; t < pc.t1; ++t) {
-          if (!wait_or_abort(&kv_empty[stage], phase ^ 1, abort_flag, p.err)) { ok = false; break; }
-          ATT_TRACE(0, pt);
-          const int k0 = t * TBK;
-          int rows[2];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            int k = k0 + hh * 64;
-            if (k >= g.kv_len) k = k0;  // keys past the end: reload a valid box (masked later)
-            const int page_id = bt[k / p.page];
-            rows[hh] = (page_id * p.hkv + pc.h) * p.page + (k % p.page);
+      while (ok && vn < n_tiles) {
+        bool progressed = false;
+        // ---- K side: next tile (and the piece's Q tile when a piece starts)
+        if (kn < n_tiles && kn - vn < 8) {
+          if (t_cur == t_end) {  // start the next piece
+            const Piece pc = w.next(p, prefix);
+            const ReqGeo g = req_geo(p, pc.b);
+            const int qb = qn & 1;
+            if (!wait_or_abort(&q_empty[qb], ((qn >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+            if (p.mode == M_SUFFIX) {  // suffix masks of this piece's queries (0 past the request's last)
+              const int i0 = pc.rb * p.qpb;
+              const int64_t* src = p.suffix_mask + (size_t)pc.b * p.Q;
+#pragma unroll 8
+              for (int qi = 0; qi < p.qpb; ++qi) smask_sm[qb * TR + qi] = (i0 + qi < g.nq) ? src[i0 + qi] : 0;
+            }
+            mbar_arrive_expect_tx(&q_full[qb], QP_BYTES);  // releases the masks with the Q tile
+            const int z = g.q_begin + pc.rb * p.qpb;
+            tma_load_3d(sQ + qb * QP_BYTES, &tmQ, &q_full[qb], 0, pc.h * p.group, z);
+            tma_load_3d(sQ + qb * QP_BYTES + QP_REGION, &tmQ, &q_full[qb], 64, pc.h * p.group, z);
+            ++qn;
+            t_cur = pc.t0;
+            t_end = pc.t1;
+            cur_b = pc.b;
+            cur_h = pc.h;
+            cur_len = g.kv_len;
+            bt = p.block_tables + (size_t)cur_b * p.bt_stride;
           }
-          uint8_t* sk = sKV + stage * STAGE_BYTES;
-          uint8_t* sv = sk + KV_BYTES;
-          mbar_arrive_expect_tx(&kv_full[stage], STAGE_BYTES);
-#pragma unroll
-          for (int dh = 0; dh < 2; ++dh)
+          const int ks = kn % KSTAGES;
+          if (mbar_try_wait(&k_empty[ks], ((kn / KSTAGES) & 1) ^ 1)) {
+            const int k0 = t_cur * TBK;
+            int rows[2];
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              tma_load_2d(sk + dh * REGION + hh * (REGION / 2), &tmK, &kv_full[stage], dh * 64, rows[hh]);
-              tma_load_2d(sv + dh * REGION + hh * (REGION / 2), &tmV, &kv_full[stage], dh * 64, rows[hh]);
+              int k = k0 + hh * 64;
+              if (k >= cur_len) k = k0;  // keys past the end: reload a valid box (masked later)
+              rows[hh] = (bt[k / p.page] * p.hkv + cur_h) * p.page + (k % p.page);
             }
-          ATT_TRACE(1, pt);
-          ++pt;
-          issued |= 1u << stage;
-          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == TSTAGES) { stage = 0; phase ^= 1; }
+            ATT_TRACE(0, kn);
+            mbar_arrive_expect_tx(&k_full[ks], KV_BYTES);
+#pragma unroll
+            for (int dh = 0; dh < 2; ++dh)
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)
+                tma_load_2d(sK + ks * KV_BYTES + dh * REGION + hh * (REGION / 2), &tmK, &k_full[ks], dh * 64,
+                            rows[hh]);
+            trows[kn & 7] = make_int2(rows[0], rows[1]);
+            kin |= 1u << ks;
+            ++kn;
+            ++t_cur;
+            progressed = true;
+          }
+        }
+        // ---- V side
+        if (vn < kn) {
+          const int vs = vn % VSTAGES;
+          if (mbar_try_wait(&v_empty[vs], ((vn / VSTAGES) & 1) ^ 1)) {
+            const int2 rows = trows[vn & 7];
+            ATT_TRACE(1, vn);
+            mbar_arrive_expect_tx(&v_full[vs], KV_BYTES);
+#pragma unroll
+            for (int dh = 0; dh < 2; ++dh) {
+              tma_load_2d(sV + vs * KV_BYTES + dh * REGION, &tmV, &v_full[vs], dh * 64, rows.x);
+              tma_load_2d(sV + vs * KV_BYTES + dh * REGION + REGION / 2, &tmV, &v_full[vs], dh * 64, rows.y);
+            }
+            vin |= 1u << vs;
+            ++vn;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else {  // nothing ready: keep polling both rings, within the wait limit
+          const uint64_t now = globaltimer_ns();
+          if (idle_since == 0) idle_since = now;
+          if (*abort_flag) { ok = false; break; }
+          if (now - idle_since > kWaitLimitNs) {
+            set_error(p.err, 1);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
         }
       }
       if (!ok) {  // let copies in flight land before the CTA exits
-        for (int s = 0; s < TSTAGES; ++s)
-          if ((issued >> s) & 1) mbar_wait(&kv_full[s], (issued_phase >> s) & 1, nullptr);
+        for (int i = 1; i <= KSTAGES && i <= kn; ++i) {
+          const int n = kn - i;
+          if ((kin >> (n % KSTAGES)) & 1) mbar_wait(&k_full[n % KSTAGES], (n / KSTAGES) & 1, nullptr);
+        }
+        for (int i = 1; i <= VSTAGES && i <= vn; ++i) {
+          const int n = vn - i;
+          if ((vin >> (n % VSTAGES)) & 1) mbar_wait(&v_full[n % VSTAGES], (n / VSTAGES) & 1, nullptr);
+        }
       }
     }
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer
+  } else if (warp == 1 || warp == 14) {
+    // ================================================================ MMA issuers
+    // warp 1 issues S^T = K.Q^T as soon as a K tile and an S buffer are free;
+    // warp 14 issues O^T += V^T.P^T as soon as a V tile and a P tile are ready.
+    // Each tracks its own tcgen05 operations, so neither waits for the other's.
     if (lane == 0 && x_begin < x_end) {
       constexpr uint32_t idesc_s = idesc_bf16(128, TR);
       constexpr uint32_t idesc_o = idesc_bf16(128, TR) | (1u << 15);  // A (V^T) MN-major
+      const bool is_s = (warp == 1);
       Walker w;
       w.init(p, prefix, x_begin, x_end);
-      int stage = 0;
-      uint32_t phase = 0;
-      int qn = 0, pn = 0, tn = 0;  // pieces, P buffers used, tiles
+      int qn = 0, tn = 0;  // pieces, tiles
       bool ok = true;
       while (ok && !w.done()) {
         const Piece pc = w.next(p, prefix);
         const int qb = qn & 1, ob = qn & 1;
-        if (!wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
-        tc_fence_after();
-        const uint64_t qdesc = smem_desc_sw128(sQ + qb * QP_BYTES);
-        const uint32_t o_tm = tmem + 2 * TR + ob * TR;
-        int prev_stage = -1;
-        for (int t = pc.t0; t <= pc.t1 && ok; ++t) {
-          if (t < pc.t1) {
-            // S^T(t) = K_t . Q^T into S buffer tn % 2
-            const int sb = tn & 1;
-            if (!wait_or_abort(&kv_full[stage], phase, abort_flag, p.err)) { ok = false; break; }
+        if (is_s) {
+          if (!wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t qdesc = smem_desc_sw128(sQ + qb * QP_BYTES);
+          for (int t = pc.t0; t < pc.t1; ++t, ++tn) {
+            const int sb = tn & 1, ks = tn % KSTAGES;
+            if (!wait_or_abort(&k_full[ks], (tn / KSTAGES) & 1, abort_flag, p.err)) { ok = false; break; }
             if (!wait_or_abort(&s_empty[sb], ((tn >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
             ATT_TRACE(2, tn);
             tc_fence_after();
-            const uint64_t kdesc = smem_desc_sw128(sKV + stage * STAGE_BYTES);
+            const uint64_t kdesc = smem_desc_sw128(sK + ks * KV_BYTES);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint64_t off_a = (uint64_t)((k >> 2) * (REGION >> 4) + (k & 3) * 2);
@@ -493,50 +566,52 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               tc_mma_bf16(tmem + sb * TR, kdesc + off_a, qdesc + off_b, idesc_s, k > 0);
             }
             tc_commit(&s_full[sb]);
+            tc_commit(&k_empty[ks]);
             if (t + 1 == pc.t1) tc_commit(&q_empty[qb]);
-            ++tn;
           }
-          if (t > pc.t0) {
-            // O^T += V_{t-1}^T . P^T(t-1)
-            const int st = prev_stage;
-            if (!wait_or_abort(p_full, pn & 1, abort_flag, p.err)) { ok = false; break; }
-            ATT_TRACE(3, pn);
-            if (t - 1 == pc.t0) {
+        } else {
+          const uint32_t o_tm = tmem + 2 * TR + ob * TR;
+          for (int t = pc.t0; t < pc.t1; ++t, ++tn) {
+            const int vs = tn % VSTAGES, pb = tn & 1;
+            if (!wait_or_abort(&v_full[vs], (tn / VSTAGES) & 1, abort_flag, p.err)) { ok = false; break; }
+            if (!wait_or_abort(&p_full[pb], (tn >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            if (t == pc.t0) {
               if (!wait_or_abort(&o_empty[ob], ((qn >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
             }
+            ATT_TRACE(3, tn);
             tc_fence_after();
-            const uint64_t vdesc = desc_v_mn(sKV + st * STAGE_BYTES + KV_BYTES);
-            const uint64_t pdesc = smem_desc_sw128(sP);
+            const uint64_t vdesc = desc_v_mn(sV + vs * KV_BYTES);
+            const uint64_t pdesc = smem_desc_sw128(sP + pb * QP_BYTES);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint64_t off_a = (uint64_t)(k * (2048 >> 4));  // 16 keys = 2 KB
               const uint64_t off_b = (uint64_t)((k >> 2) * (QP_REGION >> 4) + (k & 3) * 2);
-              tc_mma_bf16(o_tm, vdesc + off_a, pdesc + off_b, idesc_o, (t - 1 > pc.t0) || k > 0);
+              tc_mma_bf16(o_tm, vdesc + off_a, pdesc + off_b, idesc_o, (t > pc.t0) || k > 0);
             }
-            tc_commit(&kv_empty[st]);
-            tc_commit(p_empty);
-            ATT_TRACE(4, pn);
-            ++pn;
+            tc_commit(&v_empty[vs]);
+            tc_commit(&p_empty[pb]);
+            ATT_TRACE(4, tn);
           }
-          if (t < pc.t1) {
-            prev_stage = stage;
-            if (++stage == TSTAGES) { stage = 0; phase ^= 1; }
-          }
+          if (ok) tc_commit(&o_full[ob]);
         }
-        if (!ok) break;
-        tc_commit(&o_full[ob]);
         ++qn;
       }
       // drain: wait for every MMA this thread issued before TMEM is released
-      tc_commit(p_empty);
-      mbar_wait(p_empty, pn & 1, nullptr);
+      uint64_t* drain = &drain_bar[is_s ? 0 : 1];
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr);
     }
-  } else {
-    // ================================================================ softmax + epilogue
+  } else if (warp < 10) {
+    // ================================================================ softmax
+    // 8 warps: warp w reads TMEM lane quarter w % 4 (keys 32q..32q+31 of a tile)
+    // and rows [HR*half, HR*half + HR) of S; the two halves are independent.
     const int quarter = warp & 3;
-    const int key = quarter * 32 + lane;        // this thread's key within a tile / dim of O
-    const int sidx = (warp - 2) * 32 + lane;    // 0..127 within the softmax group
+    const int half = (warp - 2) >> 2;
+    const int key = quarter * 32 + lane;        // this thread's key within a tile
+    const int hidx = ((warp - 2) & 3) * 32 + lane;  // 0..127 within this half
+    const int r0 = half * HR;                   // first row of this half
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int bar_half = 1 + half;              // named barriers 1 and 2 (128 threads each)
     if (x_begin < x_end) {
       Walker w;
       w.init(p, prefix, x_begin, x_end);
@@ -545,209 +620,274 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const Piece pc = w.next(p, prefix);
         const ReqGeo g = req_geo(p, pc.b);
         const int i0 = pc.rb * p.qpb;
-        const int ob = qn & 1;
-        // rows valid in this segment (query < nq)
-        uint32_t valid = 0;
+        const int ob = qn & 1, qb = qn & 1;
+        uint32_t valid = 0;  // rows of this half whose query exists
 #pragma unroll
-        for (int r = 0; r < TR; ++r)
-          if (i0 + r / p.group < g.nq) valid |= 1u << r;
-        if (p.mode == M_SUFFIX && sidx < TR) {
-          const int i = i0 + sidx / p.group;
-          rmask[sidx] = (i < g.nq) ? p.suffix_mask[(size_t)pc.b * p.Q + i] : 0;
+        for (int r = 0; r < HR; ++r)
+          if (i0 + ((r0 + r) >> p.group_shift) < g.nq) valid |= 1u << r;
+        if (hidx == 0 && half == 0) ATT_TRACE(13, qn);
+        // piece metadata (suffix masks) arrives with the Q tile
+        wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err);
+        if (hidx == 0 && half == 0) ATT_TRACE(14, qn);
+        if (p.mode == M_SUFFIX && hidx < p.Q) {
+          uint32_t cm = 0;  // rows of this half that see suffix key j = hidx
+          for (int r = 0; r < HR; ++r)
+            if ((smask_sm[qb * TR + ((r0 + r) >> p.group_shift)] >> hidx) & 1) cm |= 1u << r;
+          colmask[half * 64 + hidx] = cm & valid;
         }
-        bar_named(2, 128);
-        float m_run[TR], l_run[TR];
+        if (hidx < HR) msm[r0 + hidx] = -INFINITY;
+        bar_named(bar_half, 128);
+        if (hidx == 0 && half == 0) ATT_TRACE(15, qn);
+        if (hidx == 0 && half == 0) mbar_arrive(&q_empty[qb]);  // masks consumed (with the MMA's commit)
+        float m_run[HR], l_run[HR];
 #pragma unroll
-        for (int r = 0; r < TR; ++r) {
+        for (int r = 0; r < HR; ++r) {
           m_run[r] = -INFINITY;
           l_run[r] = 0.f;
         }
         for (int t = pc.t0; t < pc.t1; ++t) {
-          const int sb = tn & 1;
-          const int k0 = t * TBK;
-          const int kg = k0 + key;
+          const int sb = tn & 1, pb = pn & 1;
+          const int kg = t * TBK + key;
           wait_or_abort(&s_full[sb], (tn >> 1) & 1, abort_flag, p.err);
-          if (sidx == 0) ATT_TRACE(5, tn);
+          if (hidx == 0 && half == 0) ATT_TRACE(5, tn);
           tc_fence_after();
-          float s[TR];
-          tmem_ld32(lane_base + sb * TR, s);
+          float s[HR];
+          tmem_ld16(lane_base + sb * TR + r0, s);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s_empty[sb]);
           ++tn;
-          // ---- visibility + scale
-          bool full_tile;
-          if (p.mode == M_SUFFIX) full_tile = (k0 + TBK <= g.prefix);
-          else full_tile = (k0 + TBK - 1 <= g.prefix + i0);
-          if (full_tile) {
-#pragma unroll
-            for (int r = 0; r < TR; ++r) s[r] = ((valid >> r) & 1) ? s[r] * p.scale_log2 : -INFINITY;
+          // ---- rows of this half that see this key
+          uint32_t vm;
+          if (p.mode == M_SUFFIX) {
+            vm = kg < g.prefix ? valid : (kg < g.kv_len ? colmask[half * 64 + kg - g.prefix] : 0u);
           } else {
-#pragma unroll
-            for (int r = 0; r < TR; ++r) {
-              bool vis = (valid >> r) & 1;
-              if (p.mode == M_SUFFIX) {
-                const int j = kg - g.prefix;
-                vis = vis && kg < g.kv_len && (j < 0 || ((rmask[r] >> j) & 1));
-              } else {
-                vis = vis && kg <= g.prefix + i0 + r / p.group;
-              }
-              s[r] = vis ? s[r] * p.scale_log2 : -INFINITY;
-            }
+            const int d = kg - g.prefix - i0;  // rows of queries >= d see the key
+            const int first = (d <= 0 ? 0 : d << p.group_shift) - r0;
+            vm = first <= 0 ? valid : (first >= HR ? 0u : (valid & (~0u << first)));
           }
           bool exceed = false;
 #pragma unroll
-          for (int r = 0; r < TR; ++r) exceed |= ((valid >> r) & 1) && (s[r] > m_run[r] + 8.f);
-          exceed = bar_red_or(1, 128, exceed);
-          // P buffer free (the previous P . V finished)
-          if (sidx == 0) ATT_TRACE(6, pn);
-          wait_or_abort(p_empty, (pn & 1) ^ 1, abort_flag, p.err);
-          if (sidx == 0) ATT_TRACE(7, pn);
-          ++pn;
+          for (int r = 0; r < HR; ++r) {
+            s[r] = ((vm >> r) & 1) ? s[r] * p.scale_log2 : -INFINITY;
+            exceed |= s[r] > m_run[r] + 8.f;
+          }
+          exceed = bar_red_or(bar_half, 128, exceed);
+          // the P buffer of two tiles ago has been consumed
+          if (hidx == 0 && half == 0) ATT_TRACE(6, pn);
+          wait_or_abort(&p_empty[pb], ((pn >> 1) & 1) ^ 1, abort_flag, p.err);
+          if (hidx == 0 && half == 0) ATT_TRACE(7, pn);
           if (exceed) {
-            float mx[TR];
+            // row maxima: warp reduce (order-preserving int encoding), then across the half's 4 warps
 #pragma unroll
-            for (int r = 0; r < TR; ++r) mx[r] = s[r];
-            const float wm = transpose_reduce32<true>(mx, lane);
-            red[(warp - 2) * TR + lane] = wm;
-            bar_named(2, 128);
-            // mx[] now holds each row's correction factor
+            for (int r = 0; r < HR; ++r) {
+              int v = __float_as_int(s[r]);
+              v = v >= 0 ? v : v ^ 0x7fffffff;
+              v = __reduce_max_sync(0xffffffff, v);
+              if (lane == r) red[(warp - 2) * HR + r] = __int_as_float(v >= 0 ? v : v ^ 0x7fffffff);
+            }
+            bar_named(bar_half, 128);
+            if (hidx < HR) {
+              const int w0 = half * 4;
+              const float tm = fmaxf(fmaxf(red[(w0 + 0) * HR + hidx], red[(w0 + 1) * HR + hidx]),
+                                     fmaxf(red[(w0 + 2) * HR + hidx], red[(w0 + 3) * HR + hidx]));
+              const float mo = msm[r0 + hidx];
+              const float mn = tm > mo + 8.f ? tm : mo;
+              msm[r0 + hidx] = mn;
+              csm[r0 + hidx] = mo == -INFINITY ? 0.f : ex2(mo - mn);
+            }
+            bar_named(bar_half, 128);
             bool any_corr = false;
 #pragma unroll
-            for (int r = 0; r < TR; ++r) {
-              const float tm = fmaxf(fmaxf(red[r], red[TR + r]), fmaxf(red[2 * TR + r], red[3 * TR + r]));
-              const float mn = (tm > m_run[r] + 8.f) ? tm : m_run[r];
-              mx[r] = (m_run[r] == -INFINITY) ? 0.f : ex2(m_run[r] - mn);
-              any_corr |= (mn != m_run[r]) && (m_run[r] != -INFINITY);
-              m_run[r] = mn;
-              l_run[r] *= mx[r];
+            for (int r = 0; r < HR; ++r) {
+              const float c = csm[r0 + r];
+              m_run[r] = msm[r0 + r];
+              l_run[r] *= c;
+              any_corr |= c != 1.f;
             }
             if (t > pc.t0 && any_corr) {
+              // O holds the products of tiles < t: wait for the last one, then rescale in place
+              const int prev = pn - 1;
+              wait_or_abort(&p_empty[prev & 1], (prev >> 1) & 1, abort_flag, p.err);
               tc_fence_after();
-              const uint32_t oaddr = lane_base + 2 * TR + ob * TR;
+              const uint32_t oaddr = lane_base + 2 * TR + ob * TR + r0;
 #pragma unroll
-              for (int c = 0; c < TR; c += 8) {
+              for (int c = 0; c < HR; c += 8) {
                 float ov[8];
                 tmem_ld8(oaddr + c, ov);
 #pragma unroll
-                for (int r = 0; r < 8; ++r) ov[r] *= mx[c + r];
+                for (int r = 0; r < 8; ++r) ov[r] *= csm[r0 + c + r];
                 tmem_st8(oaddr + c, ov);
               }
             }
           }
           // ---- P = exp2(S - m), row sums, P^T into shared memory (K-major, 128-byte swizzle)
-          uint8_t* prow = sP + (key >> 6) * QP_REGION;
+          uint8_t* prow = sP + pb * QP_BYTES + (key >> 6) * QP_REGION + r0 * 128;
           const int kc = (key & 63) >> 3, kb = (key & 7) * 2;
 #pragma unroll
-          for (int r = 0; r < TR; ++r) {
+          for (int r = 0; r < HR; ++r) {
             const float m = (m_run[r] == -INFINITY) ? 0.f : m_run[r];
             const float pv = ex2(s[r] - m);
             l_run[r] += pv;
-            *reinterpret_cast<__nv_bfloat16*>(prow + r * 128 + ((kc ^ (r & 7)) << 4) + kb) = __float2bfloat16(pv);
+            *reinterpret_cast<__nv_bfloat16*>(prow + r * 128 + ((kc ^ ((r0 + r) & 7)) << 4) + kb) =
+                __float2bfloat16(pv);
           }
           fence_async_smem();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(p_full);
-          if (sidx == 0) ATT_TRACE(8, pn - 1);
+          if (lane == 0) mbar_arrive(&p_full[pb]);
+          if (hidx == 0 && half == 0) ATT_TRACE(8, pn);
+          ++pn;
         }
-        // ---- end of piece: O^T from TMEM, row sums, output or partial
+        // ---- end of piece: row sums and maxima for the epilogue warps
+#pragma unroll
+        for (int r = 0; r < HR; ++r) {
+          float v = l_run[r];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+          l_run[r] = v;
+        }
+        if (hidx == 0 && half == 0) ATT_TRACE(10, qn);
+        // lfin/mfin[ob] and red[] are free once the epilogue released this O buffer's previous piece
+        wait_or_abort(&o_empty[ob], ((qn >> 1) & 1) ^ 1, abort_flag, p.err);
+        if (hidx == 0 && half == 0) ATT_TRACE(11, qn);
+        bar_named(bar_half, 128);  // red[] of the last rescale has been read
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < HR; ++r) red[(warp - 2) * HR + r] = l_run[r];
+        }
+        bar_named(bar_half, 128);
+        if (hidx < HR) {
+          const int w0 = half * 4;
+          lfin[ob * TR + r0 + hidx] = red[(w0 + 0) * HR + hidx] + red[(w0 + 1) * HR + hidx] +
+                                      red[(w0 + 2) * HR + hidx] + red[(w0 + 3) * HR + hidx];
+          mfin[ob * TR + r0 + hidx] = msm[r0 + hidx];
+        }
+        bar_named(bar_half, 128);
+        if (hidx == 0) mbar_arrive(&l_full[ob]);  // one arrival per half
+        if (hidx == 0 && half == 0) ATT_TRACE(12, qn);
+        ++qn;
+      }
+    }
+  } else if (warp < 14) {
+    // ================================================================ epilogue
+    const int quarter = warp & 3;
+    const int dim = quarter * 32 + lane;        // this thread's output dimension
+    const int eidx = (warp - 10) * 32 + lane;   // 0..127 within the epilogue group
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    if (x_begin < x_end) {
+      Walker w;
+      w.init(p, prefix, x_begin, x_end);
+      int qn = 0;
+      while (!w.done()) {
+        const Piece pc = w.next(p, prefix);
+        const ReqGeo g = req_geo(p, pc.b);
+        const int i0 = pc.rb * p.qpb;
+        const int ob = qn & 1;
         wait_or_abort(&o_full[ob], (qn >> 1) & 1, abort_flag, p.err);
+        wait_or_abort(&l_full[ob], (qn >> 1) & 1, abort_flag, p.err);
         tc_fence_after();
         float ov[TR];
         tmem_ld32(lane_base + 2 * TR + ob * TR, ov);
+        const float mrow_e = eidx < TR ? mfin[ob * TR + eidx] : 0.f;
+        const float lrow_e = eidx < TR ? lfin[ob * TR + eidx] : 0.f;
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[ob]);
         ++qn;
-        bar_named(2, 128);  // every thread is done reading red[] of the last rescale
-        {
-          const float ws = transpose_reduce32<false>(l_run, lane);
-          red[(warp - 2) * TR + lane] = ws;
-        }
-        bar_named(2, 128);
-        if (sidx < TR) fin[sidx] = red[sidx] + red[TR + sidx] + red[2 * TR + sidx] + red[3 * TR + sidx];
-        bar_named(2, 128);
         const bool complete = (pc.t0 == 0 && pc.t1 == pc.nt);
         const bool aborted = *abort_flag != 0;
+        const size_t row0 = (size_t)(g.q_begin + i0) * p.hq + pc.h * p.group;  // row of r = 0
         if (complete) {
           if (!aborted) {
 #pragma unroll
             for (int r = 0; r < TR; ++r) {
-              if (!((valid >> r) & 1)) continue;
-              const float l = fin[r];
-              const float inv = l > 0.f ? 1.f / l : 0.f;
-              const size_t row = (size_t)(g.q_begin + i0 + r / p.group) * p.hq + pc.h * p.group + r % p.group;
-              p.o[row * TD + key] = __float2bfloat16(ov[r] * inv);
+              if (i0 + (r >> p.group_shift) < g.nq) {
+                const float l = lfin[ob * TR + r];
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
+                p.o[row * TD + dim] = __float2bfloat16(ov[r] * inv);
+              }
             }
           }
         } else {
-          const int slot = 2 * blockIdx.x + (pc.x0 == x_begin ? 0 : 1);
-          float* dst = p.o_part + (size_t)slot * TR * TD;
+        const int slot = 2 * blockIdx.x + (pc.x0 == x_begin ? 0 : 1);
+        float* dst = p.o_part + (size_t)slot * TR * TD;
 #pragma unroll
-          for (int r = 0; r < TR; ++r) {
-            const float l = fin[r];
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            dst[r * TD + key] = ov[r] * inv;
-          }
-          {
-            float mr = 0.f;  // m_run[sidx] without a dynamic register index
-#pragma unroll
-            for (int r = 0; r < TR; ++r)
-              if (r == sidx) mr = m_run[r];
-            if (sidx < TR) {
-              const float l = fin[sidx];
-              p.lse_part[(size_t)slot * TR + sidx] = l > 0.f ? mr + __log2f(l) : -INFINITY;
-            }
-          }
+        for (int r = 0; r < TR; ++r) {
+          const float l = lfin[ob * TR + r];
+          dst[r * TD + dim] = ov[r] * (l > 0.f ? 1.f / l : 0.f);
+        }
+        if (eidx < TR)
+          p.lse_part[(size_t)slot * TR + eidx] = lrow_e > 0.f ? mrow_e + __log2f(lrow_e) : -INFINITY;
+        __threadfence();
+        bar_named(4, 128);
+        const long long seg_x0 = pc.x0 - pc.t0;  // the segment's first global tile
+        const int c_first = tile_owner(seg_x0, TT, G);
+        const int c_last = tile_owner(seg_x0 + pc.nt - 1, TT, G);
+        const int n_pieces = c_last - c_first + 1;
+        const size_t cidx = (size_t)(g.q_begin + i0) * p.hkv + pc.h;
+        if (eidx == 0) *last_flag = aborted ? 0 : (atomicAdd(p.counters + cidx, 1) == n_pieces - 1);
+        bar_named(4, 128);
+        if (*last_flag) {
           __threadfence();
-          bar_named(2, 128);
-          // segment's first global tile and its pieces' owners
-          const long long seg_x0 = pc.x0 - pc.t0;
-          const int c_first = tile_owner(seg_x0, TT, G);
-          const int c_last = tile_owner(seg_x0 + pc.nt - 1, TT, G);
-          const int n_pieces = c_last - c_first + 1;
-          const size_t cidx = (size_t)(g.q_begin + i0) * p.hkv + pc.h;
-          if (sidx == 0) {
-            int last = 0;
-            if (!aborted) last = (atomicAdd(p.counters + cidx, 1) == n_pieces - 1);
-            *last_flag = last;
-          }
-          bar_named(2, 128);
-          if (*last_flag) {
-            __threadfence();
-            for (int r = 0; r < TR; ++r) {
-              if (!((valid >> r) & 1)) continue;
-              float m = -INFINITY;
+          // merge the segment's pieces: per-row maxima and weight sums first (one row per thread),
+          // then every thread accumulates its dimension of all rows with independent loads
+          if (eidx < TR) {
+            float m = -INFINITY;
+            for (int c = c_first; c <= c_last; ++c) {
+              const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
+              m = fmaxf(m, __ldcg(p.lse_part + (size_t)sl * TR + eidx));
+            }
+            float tot = 0.f;
+            if (m != -INFINITY) {
               for (int c = c_first; c <= c_last; ++c) {
                 const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
-                m = fmaxf(m, __ldcg(p.lse_part + (size_t)sl * TR + r));
+                const float lse = __ldcg(p.lse_part + (size_t)sl * TR + eidx);
+                tot += lse == -INFINITY ? 0.f : ex2(lse - m);
               }
-              float acc = 0.f, tot = 0.f;
-              if (m != -INFINITY) {
-                for (int c = c_first; c <= c_last; ++c) {
-                  const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
-                  const float lse = __ldcg(p.lse_part + (size_t)sl * TR + r);
-                  if (lse == -INFINITY) continue;
-                  const float wgt = ex2(lse - m);
-                  tot += wgt;
-                  acc += wgt * __ldcg(p.o_part + ((size_t)sl * TR + r) * TD + key);
-                }
-              }
-              const size_t row = (size_t)(g.q_begin + i0 + r / p.group) * p.hq + pc.h * p.group + r % p.group;
-              p.o[row * TD + key] = __float2bfloat16(tot > 0.f ? acc / tot : 0.f);
             }
-            if (sidx == 0) p.counters[cidx] = 0;
+            cmb[eidx] = m == -INFINITY ? 0.f : m;
+            cmb[TR + eidx] = tot > 0.f ? 1.f / tot : 0.f;
           }
+          bar_named(4, 128);
+          float acc[TR];
+#pragma unroll
+          for (int r = 0; r < TR; ++r) acc[r] = 0.f;
+          for (int c = c_first; c <= c_last; ++c) {
+            const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
+            const float* lse = p.lse_part + (size_t)sl * TR;
+            const float* op = p.o_part + (size_t)sl * TR * TD + dim;
+#pragma unroll
+            for (int r = 0; r < TR; ++r) {
+              const float l = __ldcg(lse + r);
+              const float wgt = l == -INFINITY ? 0.f : ex2(l - cmb[r]);
+              acc[r] += wgt * __ldcg(op + r * TD);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < TR; ++r) {
+            if (i0 + (r >> p.group_shift) < g.nq) {
+              const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
+              p.o[row * TD + dim] = __float2bfloat16(acc[r] * cmb[TR + r]);
+            }
+          }
+          if (eidx == 0) p.counters[cidx] = 0;
         }
+        bar_named(4, 128);  // last_flag is rewritten by the next partial piece
+        }
+        // O buffer ob and lfin/mfin[ob] may be reused (by the piece after next)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[ob]);
       }
     }
   }
+  __syncwarp();  // single-lane roles rejoin their warps before the CTA barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    if (lane == 0 && p.trace != nullptr) p.trace[1024 + 4 * blockIdx.x + 2] = globaltimer_ns();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+    if (lane == 0 && p.trace != nullptr) p.trace[1024 + 4 * blockIdx.x + 3] = globaltimer_ns();
   }
 }
 
@@ -778,8 +918,8 @@ void attention_tc_launch(const AttnLaunch& a, int* counters, cudaStream_t stream
   TORCH_CHECK(a.head_dim == TD, "tcgen05 attention supports head_dim 128");
   TORCH_CHECK(a.page % 64 == 0, "page size must be a multiple of 64");
   const int group = a.hq / a.hkv;
-  TORCH_CHECK(group >= 1 && group <= TR && TR % group == 0 && a.hq == group * a.hkv,
-              "GQA group must divide ", TR);
+  TORCH_CHECK(group >= 1 && group <= TR && (group & (group - 1)) == 0 && a.hq == group * a.hkv,
+              "GQA group must be a power of two <= ", TR);
   TORCH_CHECK(a.B <= TMAX_B, "at most ", TMAX_B, " requests per attention call");
   TORCH_CHECK(a.o_part && a.lse_part && counters, "attention scratch missing");
   const int64_t cache_rows = (int64_t)a.num_pages * a.hkv * a.page;
@@ -808,6 +948,7 @@ void attention_tc_launch(const AttnLaunch& a, int* counters, cudaStream_t stream
   p.page = a.page;
   p.mode = a.mode;
   p.qpb = qpb;
+  p.group_shift = __builtin_ctz(group);
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = a.err;
   p.trace = trace;

@@ -345,7 +345,8 @@ static void attention_tc(const at::Tensor& q, at::Tensor& o, const at::Tensor& k
   unsigned long long* tr = nullptr;
   if (trace.has_value()) {
     check_dev(*trace, "attention trace");
-    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 10 * 64, "trace needs 640 int64");
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 1024 + 4 * num_sms(),
+                "trace needs 1024 + 4 * SMs int64");
     tr = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
   attention_tc_launch(a, counters.data_ptr<int>(), cur_stream(), tr);

@@ -576,6 +576,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   if (EPI == EPI_STORE && p.rs_enable) __threadfence_system();  // peer stores visible before the reduce
+  __syncwarp();  // the single-lane producer / MMA roles rejoin their warps before the CTA barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -821,6 +822,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   if (EPI == EPI_STORE && p.rs_enable) __threadfence_system();
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // the peer is done with the leader's barriers and TMEM

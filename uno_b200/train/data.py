@@ -68,6 +68,10 @@ def pack_rows(rows: list[dict], seq_len: int, pad_id: int = 0) -> list[dict[str,
 
 
 def load_jsonl(path: str | Path) -> list[dict]:
+    """Token rows from a JSONL file, or from ``rows.jsonl`` of a prepared corpus directory."""
+    path = Path(path)
+    if path.is_dir():
+        path = path / "rows.jsonl"
     with open(path, encoding="utf-8") as fh:
         return [json.loads(line) for line in fh if line.strip()]
 
