@@ -227,6 +227,31 @@ def test_attention_prefill(C):
     assert rel_err(o, ref) < 1e-2
 
 
+def test_attention_prefill_many_short_and_long_requests(C):
+    """Engine-shaped prefill: many requests of mixed length (pieces of one to many tiles per CTA)."""
+    from uno_b200.layers.meta import ForwardMeta, Mode
+    from uno_b200.ops import reference as R
+
+    hq, hkv, page = 32, 8, 256
+    g = torch.Generator().manual_seed(11)
+    B = 24
+    nq = torch.randint(1, 700, (B,), generator=g).tolist()
+    cached = [0 if i % 3 else int(x) for i, x in enumerate(torch.randint(0, 300, (B,), generator=g))]
+    nk = [a + b for a, b in zip(nq, cached)]
+    pages = sum(-(-k // page) for k in nk) + 4
+    kc, vc, tables, _ = _paged_setup(B, nk, 0, hq, hkv, page, pages, seed=12)
+    q = torch.randn(sum(nq), hq, 128, generator=g).bfloat16().to(DEV)
+    cu_q = torch.tensor([0] + list(torch.tensor(nq).cumsum(0)), dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0] + list(torch.tensor(nk).cumsum(0)), dtype=torch.int32, device=DEV)
+    meta = ForwardMeta(mode=Mode.PREFILL, positions=None, slot_mapping=None, block_tables=tables,
+                       cu_seqlens_q=cu_q, cu_seqlens_k=cu_k, max_seqlen_q=max(nq), max_seqlen_k=max(nk))
+    o = C.attention(q, kc, vc, meta, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert C.error_flag() == 0
+    ref = R.attention(q.float(), kc.float(), vc.float(), meta, 128 ** -0.5)
+    assert rel_err(o, ref) < 1e-2
+
+
 @pytest.mark.parametrize("groups", [1, 4])
 def test_rmsnorm(C, groups):
     from uno_b200.ops import reference as R

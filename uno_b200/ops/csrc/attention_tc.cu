@@ -75,11 +75,13 @@ constexpr int OFF_MSM = OFF_RED + 8 * HR * 4;          // float [TR] running row
 constexpr int OFF_CSM = OFF_MSM + TR * 4;              // float [TR] last correction factors
 constexpr int OFF_LFIN = OFF_CSM + TR * 4;             // float [2][TR] row sums per O buffer
 constexpr int OFF_MFIN = OFF_LFIN + 2 * TR * 4;        // float [2][TR] row maxima per O buffer
-constexpr int OFF_COL = OFF_MFIN + 2 * TR * 4;         // u32 [2 halves][64] rows that see suffix key j
+constexpr int OFF_COL = OFF_MFIN + 2 * TR * 4;         // u32 [2 buffers][64] rows (bit r) that see suffix key j
 constexpr int OFF_SMASK = OFF_COL + 2 * 64 * 4;        // int64 [2][TR] suffix masks of a piece's queries
 constexpr int OFF_TROWS = OFF_SMASK + 2 * TR * 8;      // int2 [8] cache rows of queued tiles (K -> V)
-constexpr int OFF_CMB = OFF_TROWS + 8 * 8;             // float [2][TR] merge maxima / inverse sums
-constexpr int OFF_PREFIX = OFF_CMB + 2 * TR * 4;       // int [TMAX_B + 1]
+constexpr int OFF_META = OFF_TROWS + 8 * 8;            // PieceMeta [2] (with the Q double buffer)
+constexpr int OFF_CMB = OFF_META + 2 * 64;             // float [2][TR] merge maxima / inverse sums
+constexpr int OFF_OST = OFF_CMB + 2 * TR * 4;          // float [TR][TD] epilogue staging of O^T (own column)
+constexpr int OFF_PREFIX = OFF_OST + TR * TD * 4;      // int [TMAX_B + 1]
 constexpr int SMEM_USED = OFF_PREFIX + (TMAX_B + 1) * 4;
 constexpr int SMEM_TOTAL = SMEM_USED + 1024;           // alignment slack
 static_assert(SMEM_TOTAL <= 232448, "attention shared memory budget");
@@ -143,6 +145,12 @@ __device__ __forceinline__ int rb_keys(const TcParams& p, const ReqGeo& g, int r
 __device__ __forceinline__ int num_rb(const TcParams& p, const ReqGeo& g) { return (g.nq + p.qpb - 1) / p.qpb; }
 
 __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// Piece geometry that the producer publishes with the piece's Q tile.
+struct PieceMeta {
+  int b, rb, h, t0, t1, nt, q_begin, nq, kv_len, prefix;
+  uint32_t valid[2];  // rows of each 16-row half whose query exists
+};
 
 // A piece: tiles [t0, t1) of segment (b, rb, h), which has nt tiles.
 struct Piece {
@@ -230,7 +238,7 @@ __device__ __forceinline__ int tile_owner(long long x, long long TT, int G) {
 
 // ------------------------------------------------------------------ helpers
 // Bounded wait that also gives up when another role raised the abort flag.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+__device__ __noinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
   if (*abort_flag) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
@@ -352,14 +360,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
   float* red = reinterpret_cast<float*>(smem + OFF_RED);
-  float* msm = reinterpret_cast<float*>(smem + OFF_MSM);
-  float* csm = reinterpret_cast<float*>(smem + OFF_CSM);
   float* lfin = reinterpret_cast<float*>(smem + OFF_LFIN);
   float* mfin = reinterpret_cast<float*>(smem + OFF_MFIN);
   uint32_t* colmask = reinterpret_cast<uint32_t*>(smem + OFF_COL);
   int64_t* smask_sm = reinterpret_cast<int64_t*>(smem + OFF_SMASK);
   int2* trows = reinterpret_cast<int2*>(smem + OFF_TROWS);
   float* cmb = reinterpret_cast<float*>(smem + OFF_CMB);
+  float* msm = reinterpret_cast<float*>(smem + OFF_MSM);  // running row maxima (softmax)
+  float* csm = reinterpret_cast<float*>(smem + OFF_CSM);  // their last correction factors
+  PieceMeta* meta = reinterpret_cast<PieceMeta*>(smem + OFF_META);
+  float* ostage = reinterpret_cast<float*>(smem + OFF_OST);
   int* prefix = reinterpret_cast<int*>(smem + OFF_PREFIX);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -390,7 +400,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 2);
+      mbar_init(&q_empty[i], 3);  // S issuer (commit after the piece's last S), P.V issuer, softmax
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 8);
       mbar_init(&p_full[i], 8);
@@ -433,26 +443,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       w.init(p, prefix, x_begin, x_end);
       const long long n_tiles = x_end - x_begin;
       int kn = 0, vn = 0, qn = 0;
-      int t_cur = 0, t_end = 0, cur_b = 0, cur_h = 0, cur_len = 0;  // K cursor inside the current piece
+      int t_cur = 0, t_end = 0, cur_h = 0, cur_len = 0;  // K cursor inside the current piece
+      Piece nx{};
+      bool have_next = false;
       const int* bt = nullptr;
       uint32_t kin = 0, vin = 0;  // bit s: a load into stage s may still be in flight
       uint64_t idle_since = 0;
       bool ok = true;
       while (ok && vn < n_tiles) {
-        bool progressed = false;
+        bool progressed = false;  // set by any of the three sides below
         // ---- K side: next tile (and the piece's Q tile when a piece starts)
-        if (kn < n_tiles && kn - vn < 8) {
-          if (t_cur == t_end) {  // start the next piece
-            const Piece pc = w.next(p, prefix);
+        if (kn < n_tiles && kn - vn < 8 && t_cur == t_end) {
+          // start the next piece once its Q buffer is free (never block: V loads must keep flowing)
+          if (!have_next) {
+            nx = w.next(p, prefix);
+            have_next = true;
+          }
+          const int qb = qn & 1;
+          if (mbar_try_wait(&q_empty[qb], ((qn >> 1) & 1) ^ 1)) {
+            const Piece pc = nx;
+            have_next = false;
             const ReqGeo g = req_geo(p, pc.b);
-            const int qb = qn & 1;
-            if (!wait_or_abort(&q_empty[qb], ((qn >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+            const int i0 = pc.rb * p.qpb;
+            const int nrows = min(TR, (g.nq - i0) << p.group_shift);
+            const uint32_t valid = nrows >= 32 ? ~0u : ((1u << nrows) - 1);
             if (p.mode == M_SUFFIX) {  // suffix masks of this piece's queries (0 past the request's last)
-              const int i0 = pc.rb * p.qpb;
               const int64_t* src = p.suffix_mask + (size_t)pc.b * p.Q;
 #pragma unroll 8
               for (int qi = 0; qi < p.qpb; ++qi) smask_sm[qb * TR + qi] = (i0 + qi < g.nq) ? src[i0 + qi] : 0;
             }
+            meta[qb] = PieceMeta{pc.b, pc.rb, pc.h, pc.t0, pc.t1, pc.nt, g.q_begin, g.nq, g.kv_len, g.prefix,
+                                 {valid & 0xFFFFu, valid >> 16}};
             mbar_arrive_expect_tx(&q_full[qb], QP_BYTES);  // releases the masks with the Q tile
             const int z = g.q_begin + pc.rb * p.qpb;
             tma_load_3d(sQ + qb * QP_BYTES, &tmQ, &q_full[qb], 0, pc.h * p.group, z);
@@ -460,11 +481,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ++qn;
             t_cur = pc.t0;
             t_end = pc.t1;
-            cur_b = pc.b;
             cur_h = pc.h;
             cur_len = g.kv_len;
-            bt = p.block_tables + (size_t)cur_b * p.bt_stride;
+            bt = p.block_tables + (size_t)pc.b * p.bt_stride;
+            progressed = true;
           }
+        }
+        if (kn < n_tiles && kn - vn < 8 && t_cur < t_end) {
           const int ks = kn % KSTAGES;
           if (mbar_try_wait(&k_empty[ks], ((kn / KSTAGES) & 1) ^ 1)) {
             const int k0 = t_cur * TBK;
@@ -522,6 +545,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       if (!ok) {  // let copies in flight land before the CTA exits
+        for (int i = 1; i <= 2 && i <= qn; ++i) {
+          const int n = qn - i;
+          mbar_wait(&q_full[n & 1], (n >> 1) & 1, nullptr);
+        }
         for (int i = 1; i <= KSTAGES && i <= kn; ++i) {
           const int n = kn - i;
           if ((kin >> (n % KSTAGES)) & 1) mbar_wait(&k_full[n % KSTAGES], (n / KSTAGES) & 1, nullptr);
@@ -541,15 +568,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       constexpr uint32_t idesc_s = idesc_bf16(128, TR);
       constexpr uint32_t idesc_o = idesc_bf16(128, TR) | (1u << 15);  // A (V^T) MN-major
       const bool is_s = (warp == 1);
-      Walker w;
-      w.init(p, prefix, x_begin, x_end);
+      const int n_tiles = (int)(x_end - x_begin);
       int qn = 0, tn = 0;  // pieces, tiles
       bool ok = true;
-      while (ok && !w.done()) {
-        const Piece pc = w.next(p, prefix);
+      while (ok && tn < n_tiles) {
         const int qb = qn & 1, ob = qn & 1;
+        if (!wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        const PieceMeta pc = meta[qb];
         if (is_s) {
-          if (!wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint64_t qdesc = smem_desc_sw128(sQ + qb * QP_BYTES);
           for (int t = pc.t0; t < pc.t1; ++t, ++tn) {
@@ -570,6 +596,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (t + 1 == pc.t1) tc_commit(&q_empty[qb]);
           }
         } else {
+          mbar_arrive(&q_empty[qb]);  // piece geometry read
           const uint32_t o_tm = tmem + 2 * TR + ob * TR;
           for (int t = pc.t0; t < pc.t1; ++t, ++tn) {
             const int vs = tn % VSTAGES, pb = tn & 1;
@@ -613,36 +640,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const int bar_half = 1 + half;              // named barriers 1 and 2 (128 threads each)
     if (x_begin < x_end) {
-      Walker w;
-      w.init(p, prefix, x_begin, x_end);
+      const int n_tiles = (int)(x_end - x_begin);
       int qn = 0, tn = 0, pn = 0;
-      while (!w.done()) {
-        const Piece pc = w.next(p, prefix);
-        const ReqGeo g = req_geo(p, pc.b);
-        const int i0 = pc.rb * p.qpb;
+      while (tn < n_tiles) {
         const int ob = qn & 1, qb = qn & 1;
-        uint32_t valid = 0;  // rows of this half whose query exists
-#pragma unroll
-        for (int r = 0; r < HR; ++r)
-          if (i0 + ((r0 + r) >> p.group_shift) < g.nq) valid |= 1u << r;
         if (hidx == 0 && half == 0) ATT_TRACE(13, qn);
-        // piece metadata (suffix masks) arrives with the Q tile
+        // piece geometry and suffix masks arrive with the Q tile
         wait_or_abort(&q_full[qb], (qn >> 1) & 1, abort_flag, p.err);
         if (hidx == 0 && half == 0) ATT_TRACE(14, qn);
-        if (p.mode == M_SUFFIX && hidx < p.Q) {
-          uint32_t cm = 0;  // rows of this half that see suffix key j = hidx
-          for (int r = 0; r < HR; ++r)
-            if ((smask_sm[qb * TR + ((r0 + r) >> p.group_shift)] >> hidx) & 1) cm |= 1u << r;
-          colmask[half * 64 + hidx] = cm & valid;
+        const PieceMeta pc = meta[qb];
+        struct { int prefix, kv_len; } g{pc.prefix, pc.kv_len};
+        const int i0 = pc.rb * p.qpb;
+        const uint32_t valid = half ? pc.valid[1] : pc.valid[0];
+        // the suffix key (if any) that lands on this thread's TMEM lane: keys of a tile are 128 apart
+        // per lane and a forward has at most 64, so one mask word per thread covers the whole piece
+        const int j1 = ((key - g.prefix) % TBK + TBK) % TBK;
+        uint32_t cm_mine = 0;  // rows of this half that see suffix key j1
+        if (p.mode == M_SUFFIX && j1 < p.Q) {
+          const uint64_t gbits = (1ull << p.group) - 1;
+          for (int qi = r0 >> p.group_shift; qi <= (r0 + HR - 1) >> p.group_shift; ++qi)
+            if ((smask_sm[qb * TR + qi] >> j1) & 1) cm_mine |= (uint32_t)((gbits << (qi << p.group_shift)) >> r0);
+          cm_mine &= valid;
         }
-        if (hidx < HR) msm[r0 + hidx] = -INFINITY;
+        if (hidx < HR) msm[r0 + hidx] = -1e30f;
         bar_named(bar_half, 128);
+        if (hidx == 0 && half == 0) mbar_arrive(&q_empty[qb]);  // the piece's masks are no longer read
         if (hidx == 0 && half == 0) ATT_TRACE(15, qn);
-        if (hidx == 0 && half == 0) mbar_arrive(&q_empty[qb]);  // masks consumed (with the MMA's commit)
-        float m_run[HR], l_run[HR];
+        float m_run[HR], l_run[HR];  // a row max of -1e30 stands for "no key yet" (exp2 of it is 0)
 #pragma unroll
         for (int r = 0; r < HR; ++r) {
-          m_run[r] = -INFINITY;
+          m_run[r] = -1e30f;
           l_run[r] = 0.f;
         }
         for (int t = pc.t0; t < pc.t1; ++t) {
@@ -660,7 +687,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // ---- rows of this half that see this key
           uint32_t vm;
           if (p.mode == M_SUFFIX) {
-            vm = kg < g.prefix ? valid : (kg < g.kv_len ? colmask[half * 64 + kg - g.prefix] : 0u);
+            vm = kg < g.prefix ? valid : (kg < g.kv_len ? cm_mine : 0u);
           } else {
             const int d = kg - g.prefix - i0;  // rows of queries >= d see the key
             const int first = (d <= 0 ? 0 : d << p.group_shift) - r0;
@@ -678,7 +705,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           wait_or_abort(&p_empty[pb], ((pn >> 1) & 1) ^ 1, abort_flag, p.err);
           if (hidx == 0 && half == 0) ATT_TRACE(7, pn);
           if (exceed) {
-            // row maxima: warp reduce (order-preserving int encoding), then across the half's 4 warps
+            // row maxima: warp reduce (order-preserving int encoding), then every thread combines
+            // the 4 warps of its half; a row's running maximum moves when it grew by > 8
 #pragma unroll
             for (int r = 0; r < HR; ++r) {
               int v = __float_as_int(s[r]);
@@ -687,14 +715,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (lane == r) red[(warp - 2) * HR + r] = __int_as_float(v >= 0 ? v : v ^ 0x7fffffff);
             }
             bar_named(bar_half, 128);
-            if (hidx < HR) {
-              const int w0 = half * 4;
-              const float tm = fmaxf(fmaxf(red[(w0 + 0) * HR + hidx], red[(w0 + 1) * HR + hidx]),
-                                     fmaxf(red[(w0 + 2) * HR + hidx], red[(w0 + 3) * HR + hidx]));
+            if (hidx < HR) {  // one thread per row of this half
+              const float* rh = red + half * 4 * HR;
+              const float tm = fmaxf(fmaxf(rh[hidx], rh[HR + hidx]), fmaxf(rh[2 * HR + hidx], rh[3 * HR + hidx]));
               const float mo = msm[r0 + hidx];
               const float mn = tm > mo + 8.f ? tm : mo;
               msm[r0 + hidx] = mn;
-              csm[r0 + hidx] = mo == -INFINITY ? 0.f : ex2(mo - mn);
+              csm[r0 + hidx] = ex2(mo - mn);  // 0 when the row had no key yet
             }
             bar_named(bar_half, 128);
             bool any_corr = false;
@@ -726,8 +753,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int kc = (key & 63) >> 3, kb = (key & 7) * 2;
 #pragma unroll
           for (int r = 0; r < HR; ++r) {
-            const float m = (m_run[r] == -INFINITY) ? 0.f : m_run[r];
-            const float pv = ex2(s[r] - m);
+            const float pv = ex2(s[r] - m_run[r]);
             l_run[r] += pv;
             *reinterpret_cast<__nv_bfloat16*>(prow + r * 128 + ((kc ^ ((r0 + r) & 7)) << 4) + kb) =
                 __float2bfloat16(pv);
@@ -787,35 +813,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         wait_or_abort(&o_full[ob], (qn >> 1) & 1, abort_flag, p.err);
         wait_or_abort(&l_full[ob], (qn >> 1) & 1, abort_flag, p.err);
         tc_fence_after();
-        float ov[TR];
-        tmem_ld32(lane_base + 2 * TR + ob * TR, ov);
+        {
+          // O^T column of this thread's dimension -> shared memory, so the loops below can stay rolled
+          float ov[TR];
+          tmem_ld32(lane_base + 2 * TR + ob * TR, ov);
+#pragma unroll
+          for (int r = 0; r < TR; ++r) ostage[r * TD + dim] = ov[r];
+        }
         const float mrow_e = eidx < TR ? mfin[ob * TR + eidx] : 0.f;
         const float lrow_e = eidx < TR ? lfin[ob * TR + eidx] : 0.f;
+        // normalise the staged column, then hand TMEM O[ob] and lfin/mfin[ob] back right away:
+        // the output writes and any merge below only touch this thread's staging column
+#pragma unroll 4
+        for (int r = 0; r < TR; ++r) {
+          const float l = lfin[ob * TR + r];
+          ostage[r * TD + dim] *= (l > 0.f ? 1.f / l : 0.f);
+        }
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[ob]);
         ++qn;
         const bool complete = (pc.t0 == 0 && pc.t1 == pc.nt);
         const bool aborted = *abort_flag != 0;
         const size_t row0 = (size_t)(g.q_begin + i0) * p.hq + pc.h * p.group;  // row of r = 0
-        if (complete) {
-          if (!aborted) {
-#pragma unroll
-            for (int r = 0; r < TR; ++r) {
-              if (i0 + (r >> p.group_shift) < g.nq) {
-                const float l = lfin[ob * TR + r];
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
-                p.o[row * TD + dim] = __float2bfloat16(ov[r] * inv);
-              }
-            }
-          }
-        } else {
         const int slot = 2 * blockIdx.x + (pc.x0 == x_begin ? 0 : 1);
-        float* dst = p.o_part + (size_t)slot * TR * TD;
-#pragma unroll
+        float* part = p.o_part + (size_t)slot * TR * TD;
+        const int nrows = min(TR, (g.nq - i0) << p.group_shift);  // rows whose query exists
+#pragma unroll 4
         for (int r = 0; r < TR; ++r) {
-          const float l = lfin[ob * TR + r];
-          dst[r * TD + dim] = ov[r] * (l > 0.f ? 1.f / l : 0.f);
+          const float v = ostage[r * TD + dim];
+          if (!complete) {
+            part[r * TD + dim] = v;
+          } else if (r < nrows && !aborted) {
+            const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
+            p.o[row * TD + dim] = __float2bfloat16(v);
+          }
         }
+        if (!complete) {
         if (eidx < TR)
           p.lse_part[(size_t)slot * TR + eidx] = lrow_e > 0.f ? mrow_e + __log2f(lrow_e) : -INFINITY;
         __threadfence();
@@ -830,7 +864,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (*last_flag) {
           __threadfence();
           // merge the segment's pieces: per-row maxima and weight sums first (one row per thread),
-          // then every thread accumulates its dimension of all rows with independent loads
+          // then every thread accumulates its dimension of 8 rows at a time with independent loads
           if (eidx < TR) {
             float m = -INFINITY;
             for (int c = c_first; c <= c_last; ++c) {
@@ -849,34 +883,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             cmb[TR + eidx] = tot > 0.f ? 1.f / tot : 0.f;
           }
           bar_named(4, 128);
-          float acc[TR];
+#pragma unroll 1
+          for (int rb8 = 0; rb8 < nrows; rb8 += 8) {
+            float acc[8];
 #pragma unroll
-          for (int r = 0; r < TR; ++r) acc[r] = 0.f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
-            const float* lse = p.lse_part + (size_t)sl * TR;
-            const float* op = p.o_part + (size_t)sl * TR * TD + dim;
+            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+            for (int c = c_first; c <= c_last; ++c) {
+              const int sl = 2 * c + (range_begin(c, TT, G) >= seg_x0 ? 0 : 1);
+              const float* lse = p.lse_part + (size_t)sl * TR + rb8;
+              const float* op = p.o_part + ((size_t)sl * TR + rb8) * TD + dim;
 #pragma unroll
-            for (int r = 0; r < TR; ++r) {
-              const float l = __ldcg(lse + r);
-              const float wgt = l == -INFINITY ? 0.f : ex2(l - cmb[r]);
-              acc[r] += wgt * __ldcg(op + r * TD);
+              for (int j = 0; j < 8; ++j) {
+                const float l = __ldcg(lse + j);
+                const float wgt = l == -INFINITY ? 0.f : ex2(l - cmb[rb8 + j]);
+                acc[j] += wgt * __ldcg(op + j * TD);
+              }
             }
-          }
 #pragma unroll
-          for (int r = 0; r < TR; ++r) {
-            if (i0 + (r >> p.group_shift) < g.nq) {
-              const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
-              p.o[row * TD + dim] = __float2bfloat16(acc[r] * cmb[TR + r]);
+            for (int j = 0; j < 8; ++j) {
+              const int r = rb8 + j;
+              if (r < nrows) {
+                const size_t row = row0 + (size_t)(r >> p.group_shift) * p.hq + (r & (p.group - 1));
+                p.o[row * TD + dim] = __float2bfloat16(acc[j] * cmb[TR + r]);
+              }
             }
           }
           if (eidx == 0) p.counters[cidx] = 0;
         }
         bar_named(4, 128);  // last_flag is rewritten by the next partial piece
         }
-        // O buffer ob and lfin/mfin[ob] may be reused (by the piece after next)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[ob]);
       }
     }
   }
