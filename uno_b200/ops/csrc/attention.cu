@@ -132,6 +132,8 @@ __global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();     // q and the KV cache writes of the previous kernel are complete
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
@@ -417,6 +419,7 @@ __global__ void __launch_bounds__(32 * (NWR * KS + 1), 1)
 __global__ void attention_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part,
                                          __nv_bfloat16* __restrict__ o, int rows, int splits) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
   if (w >= rows) return;
   float m = -INFINITY;
   for (int s = 0; s < splits; ++s) m = fmaxf(m, lse_part[(size_t)s * rows + w]);
@@ -451,8 +454,7 @@ static void launch_attn(dim3 grid, int smem, const CUtensorMap& tk, const CUtens
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(paged_attention_kernel<NWR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   });
-  paged_attention_kernel<NWR, KS><<<grid, 32 * (NWR * KS + 1), smem, stream>>>(tk, tv, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_pdl(paged_attention_kernel<NWR, KS>, grid, dim3(32 * (NWR * KS + 1)), smem, stream, tk, tv, p);
 }
 
 void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
@@ -508,9 +510,8 @@ void paged_attention_launch(const AttnLaunch& a, cudaStream_t stream) {
   else launch_attn<8, 1>(grid, smem, tk, tv, p, stream);
   if (p.num_splits > 1) {
     const int rows = a.T * a.hq;
-    attention_combine_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(a.o_part, a.lse_part, a.o, rows,
-                                                                          p.num_splits);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    launch_pdl(attention_combine_kernel, dim3((rows * 32 + 255) / 256), dim3(256), 0, stream, a.o_part,
+               a.lse_part, a.o, rows, p.num_splits);
   }
 }
 

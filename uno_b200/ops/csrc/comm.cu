@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(512) reduce_norm_gather_kernel(RsParams p) {
   __shared__ unsigned long long s_epoch;
   __shared__ int s_ok;
   __shared__ float red[64];
+  pdl_wait();  // this rank's GEMM (its partial rows, its fence) has completed
   if (threadIdx.x == 0) {
     const unsigned long long e = *((volatile unsigned long long*)&ctl->epoch);
     s_epoch = e;
@@ -240,6 +241,7 @@ __global__ void __launch_bounds__(512) reduce_norm_gather_kernel(RsParams p) {
 __global__ void embedding_scatter_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                          int64_t start, int64_t rows, int H, RsParams p) {
   const int t = blockIdx.x;
+  pdl_wait();
   const int64_t id = ids[t] - start;
   const bool ok = id >= 0 && id < rows;
   const int owner = t / p.R, lr = t % p.R;
@@ -287,8 +289,7 @@ void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, 
   const int rows = std::max(1, p.R);
   const int grid = std::min(rows, 4 * num_sms());
   const int threads = std::max(64, ((int)(H / 8) + 31) / 32 * 32);
-  reduce_norm_gather_kernel<<<grid, threads, 0, cur_stream()>>>(p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_pdl(reduce_norm_gather_kernel, dim3(grid), dim3(threads), 0, cur_stream(), p);
 }
 
 void embedding_scatter_launch(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& ids,

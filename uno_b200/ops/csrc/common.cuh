@@ -110,6 +110,15 @@ __device__ __forceinline__ bool wait_row_owners(const unsigned long long* done, 
   return true;
 }
 
+// --------------------------------------------- programmatic dependent launch
+// Kernels launched with launch_pdl() may start while the previous kernel of the
+// stream is still running.  pdl_wait() blocks until that kernel has completed
+// and its writes are visible (a no-op without the launch attribute);
+// pdl_trigger() lets the next kernel begin launching once every CTA of this
+// grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {

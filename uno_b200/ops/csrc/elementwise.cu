@@ -21,6 +21,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
   const int tid = threadIdx.x;
   const int nvec = H / 8;
   __shared__ float red[1024 + 32];
+  pdl_wait();
   float v[8];
   bool active = tid < nvec;
   if (active) {
@@ -115,23 +116,24 @@ void rmsnorm_launch(const at::Tensor& x, const c10::optional<at::Tensor>& residu
   if (rows == 0) return;
   int threads = ((H / 8 + 31) / 32) * 32;
   if (residual.has_value()) {
-    rmsnorm_kernel<true><<<rows, threads, 0, cur_stream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
-        reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), H, groups, (float)eps);
+    launch_pdl(rmsnorm_kernel<true>, dim3(rows), dim3(threads), 0, cur_stream(),
+               reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int64_t)x.stride(0),
+               reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()),
+               reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+               H, (int)groups, (float)eps);
   } else {
-    rmsnorm_kernel<false><<<rows, threads, 0, cur_stream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), nullptr,
-        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), H,
-        groups, (float)eps);
+    launch_pdl(rmsnorm_kernel<false>, dim3(rows), dim3(threads), 0, cur_stream(),
+               reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int64_t)x.stride(0),
+               static_cast<__nv_bfloat16*>(nullptr), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+               reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), H, (int)groups, (float)eps);
   }
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Vocab-parallel embedding gather: rows outside [start, start + rows) are zero.
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int T, int H, int64_t start, int64_t rows) {
   const int t = blockIdx.x;
+  pdl_wait();
   const int64_t id = ids[t] - start;
   const bool ok = id >= 0 && id < rows;
   const uint4* src = reinterpret_cast<const uint4*>(table + (ok ? id : 0) * (int64_t)H);
@@ -145,11 +147,9 @@ void embedding_launch(const at::Tensor& ids, const at::Tensor& table, at::Tensor
   check_dev(out, "out");
   const int T = ids.numel(), H = table.size(1);
   if (T == 0) return;
-  embedding_kernel<<<T, 256, 0, cur_stream()>>>(ids.data_ptr<int64_t>(),
-                                                 reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
-                                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H, start,
-                                                 table.size(0));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_pdl(embedding_kernel, dim3(T), dim3(256), 0, cur_stream(), ids.data_ptr<int64_t>(),
+             reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H, (int64_t)start, (int64_t)table.size(0));
 }
 
 // out[t, i] = silu(x[t, i]) * x[t, I + i]

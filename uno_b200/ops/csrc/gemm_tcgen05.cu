@@ -383,6 +383,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();     // the previous kernel's outputs (A operand, residual, split-K counters) are complete
+  pdl_trigger();  // the next kernel may start its own set-up as SMs drain
 
   const int num_tiles = p.num_m * p.num_n;
   const int splits = p.splits;
@@ -642,6 +644,8 @@ __global__ void __launch_bounds__(192, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   const int num_m2 = (p.M + 255) / 256;
   const int num_n = (p.N + BN - 1) / BN;
@@ -865,6 +869,14 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t 
   return m;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("UNO_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
 int num_sms() {
   static std::atomic<int> counts[64];
   int dev = 0;
@@ -889,8 +901,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   });
   const int units = p.num_m * p.num_n * p.splits;
   const int grid = std::min(units, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_bf16_kernel<BN, EPI><<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, ta2, tb2, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_pdl(gemm_bf16_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::SMEM, stream, ta, tb, ta2, tb2, p);
 }
 
 template <int EPI>
@@ -909,13 +920,15 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel<EPI>, ta, tb, ta2, tb2, p));
 }
 

@@ -11,6 +11,8 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 
 namespace uno {
 
@@ -75,6 +77,27 @@ inline int64_t splitk_tiles(int M, int N, int bn) {
 // Runs a set-up step once per CUDA device.  Function attributes such as the
 // dynamic shared-memory opt-in belong to (function, device): a process that
 // launches on several devices must set them on each one.
+// Launch with programmatic stream serialisation (PDL): the kernel may be scheduled while the
+// previous kernel of the stream drains; it must call pdl_wait() before reading what that kernel
+// wrote.  UNO_PDL=0 launches normally (for A/B timing).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 class PerDeviceOnce {
  public:
   template <class F>
