@@ -488,3 +488,47 @@ def test_sparse_top_k_kernel_path_matches_torch(C):
         # bf16 logits tie often: compare the selected values (descending) rather than the ids
         assert torch.equal(x.gather(1, ids).float(), vals)
         assert torch.allclose(probs, want, atol=1e-4)
+
+
+def test_cycle_payload_kernel_matches_eager_assembly(C):
+    """The one-kernel payload (accept prefix, residual token, lookahead, stop truncation) equals the torch path."""
+    from types import SimpleNamespace
+
+    from uno_b200.engine.decoder import TwoPassDecoder
+
+    g = torch.Generator(device="cpu").manual_seed(3)
+    dec = TwoPassDecoder.__new__(TwoPassDecoder)
+    dec.eos_token_id = 7
+    for B, L in ((5, 8), (64, 8), (3, 1), (4, 16)):
+        prop = torch.randint(0, 12, (B, L), generator=g).to(DEV)
+        look = torch.randint(0, 12, (B,), generator=g).to(DEV)
+        acc = (torch.rand(B, max(L - 1, 0), generator=g) < 0.7).to(DEV)
+        corr = torch.randint(0, 12, (B, max(L - 1, 0)), generator=g).to(DEV)
+        for ignore_eos, stop_ids in ((True, None), (False, [3]), (False, None)):
+            sp = SimpleNamespace(ignore_eos=ignore_eos, stop_token_ids=stop_ids)
+            ref = dec.build_payload(prop, acc, corr, look, sp)
+            got = dec._payload_gpu(prop, look, sp, accepted=acc.to(torch.int32), corr=corr)
+            assert torch.equal(got, ref), (B, L, ignore_eos, stop_ids)
+            if L > 1:  # greedy: acceptance by equality with the target
+                tgt = torch.where(acc, prop[:, 1:], corr)
+                got = dec._payload_gpu(prop, look, sp, target=tgt)
+                assert torch.equal(got, dec.build_payload(prop, prop[:, 1:] == tgt, tgt, look, sp))
+
+
+def test_tree_meta_kernel_matches_host_masks(C):
+    from uno_b200.layers.meta import ancestor_masks
+
+    B, Q = 3, 64
+    g = torch.Generator().manual_seed(5)
+    parents = torch.full((B, Q), -1, dtype=torch.int64)
+    depths = torch.zeros(B, Q, dtype=torch.int64)
+    for b in range(B):
+        for i in range(1, Q):
+            parents[b, i] = int(torch.randint(0, i, (1,), generator=g))
+            depths[b, i] = depths[b, parents[b, i]] + 1
+    prefix = torch.tensor([10, 300, 4097], dtype=torch.int32, device=DEV)
+    masks = torch.zeros(B * Q, dtype=torch.int64, device=DEV)
+    pos = torch.zeros(B * Q, dtype=torch.int64, device=DEV)
+    C.tree_meta(parents.to(DEV), depths.to(DEV), prefix, masks, pos)
+    assert torch.equal(masks.view(B, Q).cpu(), ancestor_masks(parents))
+    assert torch.equal(pos.view(B, Q).cpu(), prefix.cpu().long()[:, None] + depths)

@@ -143,11 +143,16 @@ class TwoPassDecoder:
         B, L = proposal.shape
         logits = self.run_block(seqs, proposal, lora=False)
         lookahead, _ = self.sampler.sample(logits[:, -1, :], sp)
+        on_gpu = proposal.is_cuda
         if L == 1:
+            if on_gpu:
+                return self._payload_gpu(proposal, lookahead, sp)
             accepted = torch.ones((B, 0), dtype=torch.bool, device=proposal.device)
             corr = proposal[:, 1:]
         elif sp.greedy:
             target = self._argmax(logits[:, : L - 1, :])
+            if on_gpu:
+                return self._payload_gpu(proposal, lookahead, sp, target=target)
             accepted = proposal[:, 1:] == target
             corr = target
         else:
@@ -164,9 +169,18 @@ class TwoPassDecoder:
                 acc, c = self.sampler.verify_filtered(clean, spec, sp, q_sparse)
             else:
                 acc, c = self.sampler.verify_unfiltered(clean, draft, spec, sp.temperature)
+            if on_gpu:
+                return self._payload_gpu(proposal, lookahead, sp, accepted=acc, corr=c)
             accepted = acc.view(B, L - 1).bool()
             corr = c.view(B, L - 1)
         return self.build_payload(proposal, accepted, corr, lookahead, sp)
+
+    def _payload_gpu(self, proposal, lookahead, sp: SamplingParams, **kw):
+        """Payload assembly and stop truncation in one kernel (``cuda.cycle_payload``)."""
+        from uno_b200.ops import cuda
+
+        stops = () if sp.ignore_eos else tuple([self.eos_token_id] + [int(t) for t in sp.stop_token_ids or []])
+        return cuda.cycle_payload(proposal, lookahead, stops, **kw)
 
     def _argmax(self, logits):
         shape = logits.shape

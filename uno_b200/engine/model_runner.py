@@ -309,14 +309,21 @@ class ModelRunner:
         B, Q = tokens.shape
         _, starts = self._stage_common(seqs, Q)
         T = B * Q
-        d = depths.cpu().numpy()
-        ws.h_pos[:T] = (starts[:, None] + d).reshape(-1)
         logical = starts[:, None] + np.arange(Q, dtype=np.int64)[None, :]
         tables = ws.h_tables[:B].astype(np.int64)
         pages = np.take_along_axis(tables, logical // self.page, axis=1)
         ws.h_slot[:T] = (pages * self.page + logical % self.page).reshape(-1)
-        ws.h_mask[:T] = ancestor_masks(parents.cpu()).numpy().reshape(-1)
-        ws.upload(False, T)
+        if self.device.type == "cuda":
+            # positions (prefix + depth) and ancestor masks stay on the device: no host round trip
+            ws.upload(False, T)
+            from uno_b200.ops import cuda as cuda_ops
+
+            cuda_ops.tree_meta(parents, depths, ws.prefix_lens[:B], ws.suffix_mask_flat[:T], ws.positions[:T])
+        else:
+            d = depths.cpu().numpy()
+            ws.h_pos[:T] = (starts[:, None] + d).reshape(-1)
+            ws.h_mask[:T] = ancestor_masks(parents.cpu()).numpy().reshape(-1)
+            ws.upload(False, T)
         ws.input_ids[:T].copy_(tokens.reshape(-1))
         logits = self._execute(Mode.TREE, B, Q, False)
         for seq, s in zip(seqs, starts):

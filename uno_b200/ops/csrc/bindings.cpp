@@ -352,6 +352,12 @@ static void attention_tc(const at::Tensor& q, at::Tensor& o, const at::Tensor& k
   attention_tc_launch(a, counters.data_ptr<int>(), cur_stream(), tr);
 }
 
+void cycle_payload_launch(const at::Tensor& proposal, c10::optional<at::Tensor> accepted,
+                          c10::optional<at::Tensor> target, c10::optional<at::Tensor> corr, const at::Tensor& lookahead,
+                          const at::Tensor& stops, at::Tensor& payload);
+void tree_meta_launch(const at::Tensor& parents, const at::Tensor& depths, const at::Tensor& prefix, at::Tensor& masks,
+                      at::Tensor& positions);
+
 }  // namespace uno
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -363,6 +369,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("Q"), py::arg("scale"), py::arg("o_part"), py::arg("lse_part"), py::arg("counters"),
         py::arg("trace") = py::none());
   m.def("attention_tc_rows", &uno::attention_tc_rows);
+  m.def("cycle_payload", &uno::cycle_payload_launch, "committed tokens + count of a linear Psi-Spec cycle");
+  m.def("tree_meta", &uno::tree_meta_launch, "draft-tree ancestor masks and node positions");
   m.def("embedding", &uno::embedding_launch);
   m.def("silu_mul", &uno::silu_mul_launch);
   m.def("qk_norm_rope_store", &uno::qk_norm_rope_store_launch);

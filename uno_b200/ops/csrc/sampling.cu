@@ -357,7 +357,128 @@ __global__ void walk_tree_kernel(const int64_t* __restrict__ tok, const int64_t*
   if (lane == 0) lengths[b] = len;
 }
 
+// ----------------------------------------------------------- cycle payload
+// One thread per request: committed tokens of a linear Psi-Spec cycle, then
+// their count, in one [B, L+2] int64 row.  Proposals 1..L-1 are accepted left
+// to right until the first rejection, which is replaced by its residual
+// resample; with every proposal accepted the lookahead sample is the (L+1)-th
+// token.  Acceptance comes from the verify kernel (accepted != 0) or, for
+// greedy decoding, from proposal == target.  Unless ignore_eos, the row ends
+// at its first stop token (kept).  Semantics of the eager assembly it replaces
+// (``engine/two_pass_decoding.py`` payload + stop truncation of the reference).
+__global__ void cycle_payload_kernel(const int64_t* __restrict__ proposal, const int32_t* __restrict__ accepted,
+                                     const int64_t* __restrict__ target, const int64_t* __restrict__ corr,
+                                     const int64_t* __restrict__ lookahead, const int64_t* __restrict__ stops,
+                                     int n_stops, int B, int L, int64_t* __restrict__ payload) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t* prop = proposal + (size_t)b * L;
+  int64_t* out = payload + (size_t)b * (L + 2);
+  int len = L + 1;
+  for (int i = 0; i < L; ++i) out[i] = prop[i];
+  out[L] = lookahead[b];
+  for (int i = 0; i + 1 < L; ++i) {
+    const bool ok = target != nullptr ? prop[i + 1] == target[(size_t)b * (L - 1) + i]
+                                      : accepted[(size_t)b * (L - 1) + i] != 0;
+    if (!ok) {
+      out[i + 1] = target != nullptr ? target[(size_t)b * (L - 1) + i] : corr[(size_t)b * (L - 1) + i];
+      len = i + 2;
+      break;
+    }
+  }
+  for (int j = 0; j < len && n_stops > 0; ++j) {
+    bool hit = false;
+    for (int k = 0; k < n_stops; ++k) hit |= out[j] == stops[k];
+    if (hit) {
+      len = j + 1;
+      break;
+    }
+  }
+  out[L + 1] = len;
+}
+
+// One warp per request: ancestor-or-self bitmasks of a draft tree (parents
+// before children, root parent -1) and node positions prefix + depth, written
+// straight into the forward's metadata buffers.
+__global__ void tree_meta_kernel(const int64_t* __restrict__ parents, const int64_t* __restrict__ depths,
+                                 const int* __restrict__ prefix, int B, int Q, int64_t* __restrict__ masks,
+                                 int64_t* __restrict__ positions) {
+  const int b = blockIdx.x;
+  if (b >= B || threadIdx.x != 0) return;
+  const int64_t* par = parents + (size_t)b * Q;
+  int64_t* m = masks + (size_t)b * Q;
+  for (int i = 0; i < Q; ++i) {
+    const int64_t pa = par[i];
+    uint64_t v = 1ull << i;
+    if (pa >= 0 && pa < i) v |= (uint64_t)m[pa];
+    m[i] = (int64_t)v;
+    positions[(size_t)b * Q + i] = (int64_t)prefix[b] + depths[(size_t)b * Q + i];
+  }
+}
+
 // ------------------------------------------------------------------- host
+void cycle_payload_launch(const at::Tensor& proposal, c10::optional<at::Tensor> accepted,
+                          c10::optional<at::Tensor> target, c10::optional<at::Tensor> corr, const at::Tensor& lookahead,
+                          const at::Tensor& stops, at::Tensor& payload) {
+  check_dev(proposal, "proposal");
+  check_dev(lookahead, "lookahead");
+  check_dev(payload, "payload");
+  const int B = proposal.size(0), L = proposal.size(1);
+  TORCH_CHECK(proposal.scalar_type() == at::kLong && proposal.is_contiguous(), "proposal: contiguous int64 [B, L]");
+  TORCH_CHECK(payload.scalar_type() == at::kLong && payload.is_contiguous() && payload.numel() == (int64_t)B * (L + 2),
+              "payload: contiguous int64 [B, L+2]");
+  TORCH_CHECK(lookahead.scalar_type() == at::kLong && lookahead.numel() == B, "lookahead: int64 [B]");
+  TORCH_CHECK(stops.scalar_type() == at::kLong && (stops.numel() == 0 || stops.is_cuda()), "stops: int64");
+  const int64_t* tgt = nullptr;
+  const int32_t* acc = nullptr;
+  const int64_t* cor = nullptr;
+  if (L > 1) {
+    if (target.has_value()) {
+      check_dev(*target, "target");
+      TORCH_CHECK(target->scalar_type() == at::kLong && target->is_contiguous() && target->numel() == (int64_t)B * (L - 1),
+                  "target: int64 [B, L-1]");
+      tgt = target->data_ptr<int64_t>();
+    } else {
+      TORCH_CHECK(accepted.has_value() && corr.has_value(), "payload needs accepted + corr or a greedy target");
+      check_dev(*accepted, "accepted");
+      check_dev(*corr, "corr");
+      TORCH_CHECK(accepted->scalar_type() == at::kInt && accepted->is_contiguous() &&
+                      accepted->numel() == (int64_t)B * (L - 1), "accepted: int32 [B, L-1]");
+      TORCH_CHECK(corr->scalar_type() == at::kLong && corr->is_contiguous() && corr->numel() == (int64_t)B * (L - 1),
+                  "corr: int64 [B, L-1]");
+      acc = accepted->data_ptr<int32_t>();
+      cor = corr->data_ptr<int64_t>();
+    }
+  }
+  if (B == 0) return;
+  cycle_payload_kernel<<<(B + 127) / 128, 128, 0, cur_stream()>>>(
+      proposal.data_ptr<int64_t>(), acc, tgt, cor, lookahead.data_ptr<int64_t>(),
+      stops.numel() ? stops.data_ptr<int64_t>() : nullptr, (int)stops.numel(), B, L, payload.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tree_meta_launch(const at::Tensor& parents, const at::Tensor& depths, const at::Tensor& prefix, at::Tensor& masks,
+                      at::Tensor& positions) {
+  check_dev(parents, "parents");
+  check_dev(depths, "depths");
+  check_dev(prefix, "prefix_lens");
+  check_dev(masks, "masks");
+  check_dev(positions, "positions");
+  const int B = parents.size(0), Q = parents.size(1);
+  TORCH_CHECK(Q <= 64, "tree masks support at most 64 nodes");
+  TORCH_CHECK(parents.scalar_type() == at::kLong && depths.scalar_type() == at::kLong && parents.is_contiguous() &&
+                  depths.is_contiguous() && depths.numel() == (int64_t)B * Q, "parents / depths: int64 [B, Q]");
+  TORCH_CHECK(prefix.scalar_type() == at::kInt && prefix.numel() >= B, "prefix_lens: int32 [B]");
+  TORCH_CHECK(masks.scalar_type() == at::kLong && positions.scalar_type() == at::kLong &&
+                  masks.numel() >= (int64_t)B * Q && positions.numel() >= (int64_t)B * Q,
+              "masks / positions: int64 [B * Q]");
+  if (B == 0) return;
+  tree_meta_kernel<<<B, 32, 0, cur_stream()>>>(parents.data_ptr<int64_t>(), depths.data_ptr<int64_t>(),
+                                               prefix.data_ptr<int>(), B, Q, masks.data_ptr<int64_t>(),
+                                               positions.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void argmax_launch(const at::Tensor& x, at::Tensor& out) {
   check_dev(x, "logits");
   check_dev(out, "out");

@@ -351,6 +351,31 @@ def sample_gumbel(logits, inv_temp, seed, offset):
     return out
 
 
+_STOPS: dict = {}
+
+
+def cycle_payload(proposal, lookahead, stops: tuple, *, accepted=None, corr=None, target=None):
+    """``[B, L+2]`` committed tokens + count of a linear cycle (one kernel; see ``cycle_payload_kernel``)."""
+    B, L = proposal.shape
+    dev = proposal.device
+    key = (dev, stops)
+    st = _STOPS.get(key)
+    if st is None:
+        st = torch.tensor(list(stops), dtype=torch.int64, device=dev)
+        _STOPS[key] = st
+    out = torch.empty(B, L + 2, dtype=torch.int64, device=dev)
+    ext().cycle_payload(proposal.contiguous(), None if accepted is None else accepted.reshape(-1).to(torch.int32),
+                        None if target is None else target.reshape(-1).to(torch.int64).contiguous(),
+                        None if corr is None else corr.reshape(-1).to(torch.int64).contiguous(),
+                        lookahead.reshape(-1).to(torch.int64).contiguous(), st, out)
+    return out
+
+
+def tree_meta(parents, depths, prefix_lens, masks_out, positions_out) -> None:
+    """Ancestor-or-self masks and positions (prefix + depth) of draft trees, written in place."""
+    ext().tree_meta(parents.contiguous(), depths.to(torch.int64).contiguous(), prefix_lens, masks_out, positions_out)
+
+
 def fused_verify(clean, draft, spec, inv_temp, seed, offset):
     n = _n_rows(clean)
     acc = torch.empty(n, device=clean.device, dtype=torch.int32)
