@@ -147,11 +147,20 @@ class UnoTrainer:
             noised += info["noised"]
         lr = lr_at(self.step, self.base_lr, self.warmup, self.curriculum.max_steps)
         self.optimizer.set_lr(lr)
+        on_gpu = self.device.type == "cuda"
+        if on_gpu:  # the optimizer step holds the exposed communication: gradient reduce-scatter + all-gather
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
         grad_norm = self.optimizer.step()  # DP gradient average, clip, AdamW, parameter all-gather
+        if on_gpu:
+            ev1.record()
         self.step += 1
         metrics = {"step": self.step, "loss": total, "block_size": block, "lr": lr, "grad_norm": grad_norm,
                    "tokens": tokens, "noised_tokens": noised, "seconds": time.perf_counter() - t0,
                    "transformer_forwards": len(micro_batches)}
+        if on_gpu:
+            ev1.synchronize()
+            metrics["optimizer_comm_ms"] = ev0.elapsed_time(ev1)
         self.last_metrics = metrics
         reason = self.curriculum.checkpoint_reasons.get(self.step)
         if reason and self.output_dir is not None:
