@@ -3,13 +3,16 @@
 Every projection weight ``W [N, K]`` is split by output rows across the
 data-parallel ranks: rank ``j`` keeps rows ``[j N/world, (j+1) N/world)`` and
 their transpose in ONE symmetric allocation that the other ranks open over
-CUDA IPC.  Nothing is ever all-gathered into a full copy: the training GEMMs
-(``uno_b200.train.native``) run one launch per owner whose TMA loads read the
-owner's rows directly from its HBM over NVLink (plain tiled loads, no cluster
-multicast), i.e. the FSDP all-gather is fused into the GEMM's operand path.
+CUDA IPC.  Before a projection's GEMM the training code copies every owner's
+block peer-to-local into one reusable buffer (``gather_rows`` / ``gather_cols``
+in ``uno_b200.train.native``: contiguous copies on the copy engines over
+NVLink), so the GEMM reads each weight byte from local HBM once per row tile.
+Streaming the owners' rows straight into the GEMM's TMA loads was measured
+first and re-read the weights over NVLink once per 128-row tile (0.47 / 0.28
+scaling efficiency at 2 / 4 GPUs for 8,192-row training GEMMs).
 
 Per-rank memory for the frozen projections drops to ``2 / world`` of one full
-copy (rows + transposed rows).  The reference does not shard the base
+copy (rows + transposed rows), plus one gathered projection (W and W^T).  The reference does not shard the base
 (DeepSpeed ZeRO-2 over the LoRA parameters only,
 ``training/configs/deepspeed_zero2.json:18-27``); this module is the
 FSDP configuration of the training target.

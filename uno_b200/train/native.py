@@ -95,6 +95,45 @@ def _a_grad_block(segments) -> torch.Tensor:
     return torch.as_strided(g0, (len(segments) * r, K), (K, 1))
 
 
+_GATHER_BUF: dict = {}
+
+
+def _gather_buffer(device, numel: int, name: str) -> torch.Tensor:
+    key = (device, name)
+    buf = _GATHER_BUF.get(key)
+    if buf is None or buf.numel() < numel:
+        buf = torch.empty(numel, device=device, dtype=torch.bfloat16)
+        _GATHER_BUF[key] = buf
+    return buf[:numel]
+
+
+def gather_rows(proj: "ProjectionWeights", device) -> torch.Tensor:
+    """FSDP forward operand: every owner's rows copied into one local ``[N, K]`` weight.
+
+    Each owner block is one contiguous peer-to-local copy (copy engine over NVLink), so the
+    GEMM that follows reads local HBM once per tile instead of streaming the weight over NVLink
+    for every row tile."""
+    N, K = proj.out_features, proj.in_features
+    w = _gather_buffer(device, N * K, "w").view(N, K)
+    for sh in proj.shards:
+        w[sh.r0:sh.r1].copy_(sh.W, non_blocking=True)
+    return w
+
+
+def gather_cols(proj: "ProjectionWeights", device) -> list[torch.Tensor]:
+    """FSDP backward operands: every owner's transposed block ``[K, rows]`` as a local copy."""
+    K = proj.in_features
+    buf = _gather_buffer(device, K * proj.out_features, "wt")
+    out, off = [], 0
+    for sh in proj.shards:
+        n = K * (sh.r1 - sh.r0)
+        blk = buf[off:off + n].view(K, sh.r1 - sh.r0)
+        blk.copy_(sh.Wt, non_blocking=True)
+        out.append(blk)
+        off += n
+    return out
+
+
 class _ProjectionFn(torch.autograd.Function):
     # The LoRA factors are passed as extra inputs only so that autograd records
     # the op when ``x`` itself needs no gradient (the first projection sees the
@@ -110,14 +149,9 @@ class _ProjectionFn(torch.autograd.Function):
         if proj.segments:
             h = torch.empty(M, proj.a_cat.shape[0], device=x.device, dtype=torch.bfloat16)
             C._gemm(x, proj.a_cat, C.EPI_ROWSCALE, c=h, scale=proj.scale, row_mask=mask)
-        if proj.shards is None:
-            C._gemm(x, proj.W, C.EPI_STORE, c=y, a2=h, b2=proj.b_cat if h is not None else None)
-        else:
-            # FSDP all-gather fused into the GEMM: each output column block streams
-            # its weight rows straight from the owner's memory (TMA over NVLink)
-            for sh in proj.shards:
-                C._gemm(x, sh.W, C.EPI_STORE, c=y[:, sh.r0:sh.r1], a2=h,
-                        b2=proj.b_cat[sh.r0:sh.r1] if h is not None else None)
+        # FSDP: gather the owners' rows into a local weight first (peer copies), then one GEMM
+        W = proj.W if proj.shards is None else gather_rows(proj, x.device)
+        C._gemm(x, W, C.EPI_STORE, c=y, a2=h, b2=proj.b_cat if h is not None else None)
         ctx.proj = proj
         ctx.save_for_backward(x, h, mask)
         return y
@@ -141,10 +175,11 @@ class _ProjectionFn(torch.autograd.Function):
         elif proj.shards is None:
             C._gemm(dy, proj.Wt, C.EPI_STORE, c=dx, a2=dh, b2=proj.at_cat if dh is not None else None)
         else:
-            # dx = sum over owners of dy[:, rows_j] W_j; the first block also adds dh A_cat
-            for j, sh in enumerate(proj.shards):
+            # dx = sum over owners of dy[:, rows_j] W_j (local copies of their transposed blocks);
+            # the first block also adds dh A_cat
+            for j, (sh, wt) in enumerate(zip(proj.shards, gather_cols(proj, x.device))):
                 first = j == 0
-                C._gemm(dy[:, sh.r0:sh.r1], sh.Wt, C.EPI_STORE if first else C.EPI_ADD, c=dx,
+                C._gemm(dy[:, sh.r0:sh.r1], wt, C.EPI_STORE if first else C.EPI_ADD, c=dx,
                         r=None if first else dx, a2=dh if first else None,
                         b2=proj.at_cat if (first and dh is not None) else None)
         if proj.segments:
@@ -195,9 +230,9 @@ def build_projections(model, lora, group=None, fsdp: bool = False):
 
     With ``fsdp`` every frozen weight is split by output rows across the ranks
     of ``group`` (:class:`uno_b200.train.fsdp.ShardedWeights`): each rank keeps
-    1/world of the rows (and of their transposes), and the GEMMs stream the
-    other ranks' rows from their memory -- the FSDP all-gather fused into the
-    GEMM's operand loads.  Returns ``(layers, sharded)``.
+    1/world of the rows (and of their transposes); before each projection's
+    GEMM the owners' blocks are copied peer-to-local into one reusable buffer
+    (:func:`gather_rows`, :func:`gather_cols`).  Returns ``(layers, sharded)``.
     """
     scale = float(lora.scaling) if lora is not None else 1.0
     specs = list(_projection_specs(model, lora))
