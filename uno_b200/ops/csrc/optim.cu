@@ -7,6 +7,9 @@
 // 1/world shard.  One kernel does what is otherwise reduce-scatter -> global
 // grad-norm all-reduce -> clip -> AdamW on the shard -> all-gather:
 //
+//   ready    CTA 0 of each rank tells every peer that this rank's gradient for
+//            the step is complete (the backward ran before this kernel on the
+//            same stream); every CTA waits for all ranks before reading;
 //   phase 1  each rank sums its shard of every rank's gradient (P2P loads from
 //            the peers' gradient buffers), scales by 1/world, keeps the result
 //            in local scratch and accumulates its squared norm;
@@ -38,6 +41,7 @@ struct OptCtl {
   double norm_part[OPT_MAX_RANKS];          // written by each rank
   unsigned long long norm_flag[OPT_MAX_RANKS];
   unsigned long long done_flag[OPT_MAX_RANKS];
+  unsigned long long ready_flag[OPT_MAX_RANKS];  // rank j's gradient of step `value` is complete
 };
 
 struct AdamWArgs {
@@ -81,6 +85,19 @@ __global__ void __launch_bounds__(512) fused_adamw_kernel(AdamWArgs a) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   __shared__ double red[32];
   __shared__ float s_coef;
+
+  // ---- ready: no rank reads a peer's gradient before the peer's backward has finished
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int j = 0; j < a.world; ++j) {
+        OptCtl* peer = reinterpret_cast<OptCtl*>(a.ws[j] + a.ctl_off);
+        st_rel_u64(&peer->ready_flag[a.rank], target);
+      }
+    }
+    for (int j = 0; j < a.world; ++j) opt_wait(&ctl->ready_flag[j], target, a.err);
+  }
+  __syncthreads();
 
   // ---- phase 1: reduce-scatter of the gradient + shard sum of squares
   double ss = 0.0;
