@@ -20,22 +20,30 @@
 //
 // Per tile, transposed so that the 128-key dimension is the MMA's M:
 //   S^T[key, row] = K_tile[key, :] . Q[row, :]      (tcgen05, A = K, B = Q, K-major)
-//   P^T = exp2(S^T * scale - m[row])                (4 softmax warps, 1 key per thread)
+//   P^T = exp2(S^T * scale - m[row])                (softmax warps, 1 key per thread)
 //   O^T[dim, row] += V_tile^T[dim, key] . P[row, key] (A = V MN-major, B = P K-major)
 // Both accumulators live in TMEM.  The row max uses a lazy rescale: the running
 // max moves only when a score exceeds it by more than 8 (log2 units), which a
 // 128-thread bar.red.or detects in one barrier; the rare rescale multiplies the
 // TMEM O columns in place.  Row sums stay per thread and are reduced once per
-// piece with a 31-shuffle transpose-reduce.
+// piece with warp shuffles.
 //
-// Warp roles (192 threads): warp 0 issues TMA (K/V tiles from the paged cache
-// through the block table, 64-key boxes; Q rows through a 3-D map), warp 1
-// allocates TMEM and issues tcgen05.mma from one lane, warps 2..5 run the
-// softmax and the epilogue.  Every mbarrier wait is bounded; on expiry the
-// kernel sets error bit 1, raises a CTA-wide abort flag and drains.
+// Warp roles (480 threads):
+//   warp 0      TMA producer (one lane): Q rows of each piece through a 3-D map,
+//               with the piece's geometry and suffix masks published next to
+//               them; K and V tiles from the paged cache through the block table
+//               (64-key boxes) on separate rings, polled without blocking so
+//               that V loads keep flowing while a Q buffer is still in use;
+//   warp 1      allocates TMEM and issues S = K.Q^T (one lane);
+//   warps 2..9  softmax: two warps per TMEM lane quarter, 16 rows each;
+//   warps 10..13 epilogue: O^T from TMEM, normalisation, output or partial
+//               writes and the merge of split segments;
+//   warp 14     issues O^T += V^T.P^T (one lane).
+// Every mbarrier wait is bounded; on expiry the kernel sets error bit 1, raises
+// a CTA-wide abort flag and drains its copies and MMAs before freeing TMEM.
 //
-// Decode attention is bandwidth bound: the K/V ring holds three 64 KB tiles
-// (K + V of 128 keys) so about 128 KB of HBM reads are in flight per SM.
+// Shared memory: K ring 2 x 32 KB, V ring 3 x 32 KB, Q and P double buffers of
+// 8 KB each, plus the epilogue staging of O^T (16 KB).
 //
 // Reference behaviour: nano_vllm_uno/layers/attention.py (FlashAttention varlen
 // prefill, paged block decode with a per-block causal mask, tree prefix + LSE
