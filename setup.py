@@ -10,7 +10,7 @@ CSRC = os.path.join("uno_b200", "ops", "csrc")
 SOURCES = [
     os.path.join(CSRC, name)
     for name in ("bindings.cpp", "gemm_tcgen05.cu", "gemm_noalloc.cu", "attention.cu", "attention_tc.cu", "elementwise.cu",
-                 "sampling.cu", "comm.cu", "vocab_parallel.cu", "optim.cu", "train_loss.cu", "train_attention.cu", "train_elementwise.cu")
+                 "sampling.cu", "filtered.cu", "comm.cu", "vocab_parallel.cu", "optim.cu", "train_loss.cu", "train_attention.cu", "train_elementwise.cu")
 ]
 
 NVCC_FLAGS = [

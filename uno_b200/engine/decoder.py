@@ -122,8 +122,8 @@ class TwoPassDecoder:
             clean, _ = self.sampler.sample(logits[:, 0, :], sp)
             proposal[:, 0] = clean
             if L > 1:
-                spec_rows = logits[:, 1:, :]
-                if not (spec_rows.is_cuda and not sp.filtered(self.sampler.vocab_size(logits))):
+                spec_rows = logits[:, 1:, :]  # strided [B, L-1, V] rows: the CUDA samplers read them in place
+                if not spec_rows.is_cuda:
                     spec_rows = spec_rows.reshape(-1, logits.shape[-1])
                 spec, q_sparse = self.sampler.sample(spec_rows, sp)
                 proposal[:, 1:] = spec.view(B, L - 1)
@@ -160,7 +160,7 @@ class TwoPassDecoder:
             Vs = logits.shape[-1]  # the local vocabulary shard under vocab-parallel sampling
             clean = logits[:, : L - 1, :]
             draft = draft_logits[:, : L - 1, :]
-            if not clean.is_cuda or sp.filtered(V):
+            if not clean.is_cuda:
                 clean, draft = clean.reshape(-1, Vs), draft.reshape(-1, Vs)
             spec = proposal[:, 1:].reshape(-1)
             if sp.filtered(V):

@@ -19,6 +19,14 @@ run the framework's Philox-keyed kernels; on CPU they run here with a torch
 generator.  Randomness is keyed by ``(seed, counter)`` so every TP rank that
 runs the same call draws the same numbers without a broadcast.
 
+Filtered distributions on CUDA (bf16 logits) never leave the device as a
+candidate list: ``cuda.filtered_sample`` selects the top-k / nucleus set of
+each row exactly (radix select over the row) and keeps, per row, the key of
+the last kept token with the row max and kept mass (:class:`FilteredRows`);
+``cuda.filtered_verify`` recomputes the target's set and evaluates p and q
+from those numbers and the two logits rows.  Elsewhere the sparse ``(ids,
+probs)`` form below is used.
+
 Vocab-parallel mode (tensor parallelism with the fused NVLink collectives):
 the lm_head leaves each rank a ``[rows, V/tp]`` logits shard and
 :class:`VocabShard` tells the sampler where it sits.  Greedy, unfiltered
@@ -38,6 +46,32 @@ import torch
 
 from uno_b200.sampling_params import SamplingParams
 from uno_b200.utils.trace import nvtx
+
+
+@dataclass
+class FilteredRows:
+    """A filtered draft distribution on CUDA: the logits rows it was sampled
+    from and the per-row ``(last-kept key, max, kept mass)`` params."""
+
+    rows: torch.Tensor
+    params: torch.Tensor
+
+
+def filter_args(sp: SamplingParams, vocab: int) -> tuple[int, float]:
+    """``(top_k, top_p)`` of a filtered request; 0 and 1.0 switch a filter off."""
+    k = int(sp.top_k) if sp.uses_top_k(vocab) else 0
+    if not k and sp.top_k is not None and sp.uses_top_p():
+        raise ValueError("top_k must be smaller than the model vocabulary")
+    return k, float(sp.top_p) if sp.uses_top_p() else 1.0
+
+
+def native_filtered(logits: torch.Tensor) -> bool:
+    """bf16 logits rows the filtered kernels can read in place."""
+    if not logits.is_cuda or logits.dtype != torch.bfloat16 or logits.dim() not in (2, 3):
+        return False
+    if logits.stride(-1) != 1 or logits.shape[-1] % 8 or logits.data_ptr() % 16:
+        return False
+    return all(st % 8 == 0 for st in logits.stride()[:-1])
 
 
 @dataclass
@@ -104,14 +138,19 @@ class Sampler:
             if not sp.filtered(V):
                 return self.sample_full(logits, sp.temperature), None
             logits = self.full(logits)
-        if sp.uses_top_k(V):
-            ids, probs = sparse_top_k(logits, sp.temperature, int(sp.top_k), sp.top_p)
-            off = self.sample_probs(probs)
-            return ids.gather(1, off[:, None]).view(-1), (ids, probs)
-        if sp.uses_top_p():
-            if sp.top_k is not None:
-                raise ValueError("top_k must be smaller than the model vocabulary")
-            ids, probs = sparse_top_p(logits, sp.temperature, float(sp.top_p))
+        if sp.filtered(V):
+            k, p = filter_args(sp, V)
+            if native_filtered(logits):
+                from uno_b200.ops import cuda
+
+                key = self._next()
+                tokens, params = cuda.filtered_sample(logits, 1.0 / sp.temperature, k, p, self.seed, key)
+                return tokens, FilteredRows(logits, params)
+            rows = logits.reshape(-1, V)
+            if k:
+                ids, probs = sparse_top_k(rows, sp.temperature, k, sp.top_p)
+            else:
+                ids, probs = sparse_top_p(rows, sp.temperature, p)
             off = self.sample_probs(probs)
             return ids.gather(1, off[:, None]).view(-1), (ids, probs)
         return self.sample_full(logits, sp.temperature), None
@@ -160,6 +199,16 @@ class Sampler:
                         draft_distribution):
         clean_logits = self.full(clean_logits)
         V = clean_logits.shape[-1]
+        if isinstance(draft_distribution, FilteredRows):
+            from uno_b200.ops import cuda
+
+            if not native_filtered(clean_logits):
+                raise RuntimeError("the draft was sampled by the filtered kernel; the target rows must be too")
+            k, p = filter_args(sp, V)
+            key = self._next()
+            return cuda.filtered_verify(clean_logits, draft_distribution.rows, draft_distribution.params, spec,
+                                        1.0 / sp.temperature, k, p, self.seed, key)
+        clean_logits = clean_logits.reshape(-1, V)
         if sp.top_k is None:
             clean_ids, clean_probs = sparse_top_p(clean_logits, sp.temperature, float(sp.top_p))
             dense_vocab = V
@@ -233,7 +282,7 @@ def sparse_verify_tensors(clean_ids, clean_probs, draft_ids, draft_probs, spec, 
                                  draft_probs[:, None, :], 0.0).sum(dim=2)
     else:
         q_dense = draft_probs.new_zeros((draft_probs.shape[0], dense_vocab))
-        q_dense.scatter_(1, draft_ids, draft_probs)
+        q_dense.scatter_add_(1, draft_ids, draft_probs)
         q_on_clean = q_dense.gather(1, clean_ids)
     corr = (clean_probs - q_on_clean).clamp_min(0.0)
     total = corr.sum(dim=1, keepdim=True)

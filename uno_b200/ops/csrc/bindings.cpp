@@ -21,6 +21,11 @@ void gumbel_sample_launch(const at::Tensor& x, at::Tensor& out, double inv_temp,
 void fused_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at::Tensor& spec, double inv_temp,
                          int64_t seed, int64_t offset, at::Tensor& accepted, at::Tensor& corr);
 void topk_lse_launch(const at::Tensor& x, int K, double inv_temp, at::Tensor& ids, at::Tensor& lp);
+void filtered_sample_launch(const at::Tensor& x, double inv_temp, int64_t k, double top_p, int64_t seed,
+                            int64_t offset, at::Tensor& tokens, at::Tensor& params);
+void filtered_verify_launch(const at::Tensor& clean, const at::Tensor& draft, const at::Tensor& dparams,
+                            const at::Tensor& spec, double inv_temp, int64_t k, double top_p, int64_t seed,
+                            int64_t offset, at::Tensor& accepted, at::Tensor& corr);
 void build_tree_launch(const at::Tensor& roots, const at::Tensor& ids, const at::Tensor& lp, int Qn, at::Tensor& tok,
                        at::Tensor& par, at::Tensor& dep, at::Tensor& mass, at::Tensor& count);
 void reduce_norm_gather_launch(const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t H,
@@ -380,6 +385,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gumbel_sample", &uno::gumbel_sample_launch);
   m.def("fused_verify", &uno::fused_verify_launch);
   m.def("topk_lse", &uno::topk_lse_launch);
+  m.def("filtered_sample", &uno::filtered_sample_launch);
+  m.def("filtered_verify", &uno::filtered_verify_launch);
   m.def("build_tree", &uno::build_tree_launch);
   m.def("walk_tree", &uno::walk_tree_launch);
   m.def("reduce_norm_gather", &uno::reduce_norm_gather_launch);

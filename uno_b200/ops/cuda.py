@@ -385,6 +385,52 @@ def fused_verify(clean, draft, spec, inv_temp, seed, offset):
     return acc, corr
 
 
+def filtered_sample(logits, inv_temp, top_k, top_p, seed, offset):
+    """Top-k / top-p sample of bf16 ``[N, V]`` or strided ``[B, R, V]`` logits (``filtered.cu``).
+
+    Returns ``(tokens [N] int64, params [N, 2] int64)``: per row the key of the
+    last kept token, and the row max and kept mass packed as two float32.
+    ``top_k == 0`` or ``top_p >= 1`` switches that filter off.
+    """
+    n = _n_rows(logits)
+    tok = torch.empty(n, device=logits.device, dtype=torch.int64)
+    params = torch.empty(n, 2, device=logits.device, dtype=torch.int64)
+    ext().filtered_sample(logits, float(inv_temp), int(top_k), float(top_p), int(seed), int(offset), tok, params)
+    return tok, params
+
+
+def filtered_verify(clean, draft, draft_params, spec, inv_temp, top_k, top_p, seed, offset):
+    """Accept test + residual resample on filtered target / draft distributions (``filtered.cu``)."""
+    n = _n_rows(clean)
+    acc = torch.empty(n, device=clean.device, dtype=torch.int32)
+    corr = torch.empty(n, device=clean.device, dtype=torch.int64)
+    ext().filtered_verify(clean, draft, draft_params, spec.reshape(-1).contiguous(), float(inv_temp), int(top_k),
+                          float(top_p), int(seed), int(offset), acc, corr)
+    return acc, corr
+
+
+def filtered_keys(logits):
+    """Per-token ranking keys of ``filtered.cu`` (value descending, lowest id first) as int64."""
+    x = logits.reshape(-1, logits.shape[-1]).contiguous()
+    bits = x.view(torch.int16).to(torch.int64) & 0xFFFF
+    order = torch.where(bits >= 0x8000, (~bits) & 0xFFFF, bits | 0x8000)
+    ids = torch.arange(x.shape[-1], device=x.device, dtype=torch.int64)
+    return (order << 32) | (0xFFFFFFFF - ids)
+
+
+def filtered_kept(logits, params):
+    """Boolean keep mask of ``filtered_sample`` params."""
+    return filtered_keys(logits) >= params[:, :1]
+
+
+def unpack_filtered_params(params):
+    """``(last-kept key, row max m, kept mass S)`` of ``filtered_sample`` params."""
+    packed = params[:, 1].contiguous()
+    lo = (packed & 0xFFFFFFFF).to(torch.int32)
+    hi = ((packed >> 32) & 0xFFFFFFFF).to(torch.int32)
+    return params[:, 0], lo.view(torch.float32), hi.view(torch.float32)
+
+
 def vp_sample(logits, inv_temp, seed, offset, vocab_start, greedy=False):
     """Sample (or arg-max) from a vocab-parallel logits shard; every rank gets the same global ids."""
     regions, rank, max_rows = _COMM.vp_args()
