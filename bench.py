@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--block", type=int, default=8)
     ap.add_argument("--new-tokens", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--top-k", type=int, default=None, help="filtered sampling (not the headline config)")
+    ap.add_argument("--top-p", type=float, default=None, help="filtered sampling (not the headline config)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-tokens", type=int, default=0, help="override new tokens for the e2e run")
     ap.add_argument("--sampler", default="linear", choices=["linear", "tree"],
@@ -163,6 +165,11 @@ def engine_kwargs(args, tp: int) -> dict:
         gpu_memory_utilization=0.90,
         seed=args.seed,
     ) | ({"tree_verify_size": 64, "tree_candidate_top_k": 4} if getattr(args, "sampler", "linear") == "tree" else {})
+
+
+def _filter_note(args) -> str:
+    parts = ([f"top-k {args.top_k}"] if args.top_k else []) + ([f"top-p {args.top_p}"] if args.top_p else [])
+    return (", " + ", ".join(parts)) if parts else ""
 
 
 def run_dp_replicas(args):
@@ -287,7 +294,7 @@ def run_native(args):
         return
     llm = LLM("preset:qwen3-8b", **kw)
     sp = SamplingParams(temperature=1.0, max_tokens=args.new_tokens, diffusion_block_size=args.block,
-                        mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed)
+                        mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed, top_k=args.top_k, top_p=args.top_p)
     tree = args.sampler == "tree"
     prompts = make_prompts(args.batch, args.seed, 512 if tree else None)
 
@@ -322,7 +329,8 @@ def run_native(args):
     if not args.no_e2e:
         new_tokens = args.e2e_tokens or args.new_tokens
         sp2 = SamplingParams(temperature=1.0, max_tokens=new_tokens, diffusion_block_size=args.block,
-                             mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed + 1)
+                             mask_token_id=MASK_ID, ignore_eos=True, seed=args.seed + 1, top_k=args.top_k,
+                             top_p=args.top_p)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         outs = llm.generate(prompts, sp2, use_tqdm=False, detokenize=False)
@@ -359,7 +367,7 @@ def run_native(args):
                    "seq_len": ("prompt 512 + 4096 new" if tree else "prompt U[128,1024] + 2048 new"),
                    "block_size": args.block,
                    "sampler": ("tree Psi-Spec, 64 nodes, depth 8, top-4 candidates, T=1.0" if tree
-                               else "linear Psi-Spec, T=1.0"), "kv_page": 256,
+                               else "linear Psi-Spec, T=1.0") + _filter_note(args), "kv_page": 256,
                    "parallelism": f"tp{args.gpus}", "l2": "working set >> L2 (16 GB weights + KV per step)",
                    "running_requests": running},
         "tpf": d_acc / max(1, d_fwd),

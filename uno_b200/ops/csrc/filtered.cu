@@ -22,17 +22,20 @@
 // Selection: one CTA of 1024 threads per row, the row re-read from L2.
 //  1. stats: m, Z = sum exp(x/T - m), smallest finite x/T;
 //  2. histogram: 2048 bins of d = m - x/T (bin index never decreases as the
-//     key decreases), with token counts and masses in 2^-40 fixed point.  The
-//     sums are integer atomics, so they do not depend on thread timing and
-//     every tensor-parallel rank that runs the same call selects the same set.
-//     Top-p alone bins only d <= ln(V / (1 - top_p)) + 1: the last kept token
-//     has at least (1 - top_p) Z of mass at or after it spread over at most V
-//     tokens, each <= exp(-d), and Z >= 1, so its d is at most ln(V/(1-top_p));
+//     key decreases), with token counts and, for the top-p criterion, masses
+//     in 2^-40 fixed point held as three 14-bit limbs (native 32-bit shared
+//     atomics, no carries within a row of < 2^18 tokens).  The sums are integer,
+//     so they do not depend on thread timing and every tensor-parallel rank
+//     that runs the same call selects the same set.  Top-p bins only
+//     d <= ln(V / ((1 - top_p) Z)) + 1: the last kept token has at least
+//     (1 - top_p) Z of mass at or after it, spread over at most V tokens of at
+//     most exp(-d) each.  Top-p after top-k bins only the top-k tokens' range;
 //  3. the boundary bin (where the count reaches k, or the last bin whose
 //     preceding mass is <= P) is collected into shared memory, bitonic-sorted
 //     by key and walked; a boundary bin of more than 4096 tokens is re-binned
 //     over its exact key range (at most twice, 16-bit keys), and a single key
 //     shared by many tokens is resolved by counting tied tokens in id order.
+// The kept mass S is an exact integer sum, so every pass that forms it agrees.
 // Randomness: Philox streams 4 (sample), 5 (accept test) and 6 (residual) of
 // the (seed, offset, row, token id) keying used by every sampling kernel.
 #include "common.cuh"
@@ -50,9 +53,9 @@ constexpr float FIX = 1099511627776.f;  // 2^40
 typedef unsigned long long u64;
 
 struct FiltSmem {
-  u64 hmass[NB];
   u64 cand[CAND];
   uint32_t hcnt[NB];
+  uint32_t hm[3][NB];  // mass limbs: bits 0-13, 14-27, 28-41 of the 2^-40 fixed-point weights
   u64 wsum[32];
   uint32_t wcnt[32];
   u64 ctot_w;
@@ -77,20 +80,45 @@ __device__ __forceinline__ u64 make_key(uint32_t o, int i) {
 // never contracted into FMAs, so every pass computes bit-identical values.
 __device__ __forceinline__ float scaled(uint32_t h, float inv_temp) { return __fmul_rn(bits2f(h), inv_temp); }
 __device__ __forceinline__ u64 wfix(float d) { return __float2ull_rz(__fmul_rn(__expf(-d), FIX)); }
+__device__ __forceinline__ void add_mass(FiltSmem& sm, int b, u64 w) {
+  if (!w) return;
+  atomicAdd(&sm.hm[0][b], (uint32_t)(w & 0x3FFFu));
+  atomicAdd(&sm.hm[1][b], (uint32_t)((w >> 14) & 0x3FFFu));
+  atomicAdd(&sm.hm[2][b], (uint32_t)(w >> 28));
+}
+__device__ __forceinline__ u64 bin_mass(const FiltSmem& sm, int b) {
+  return (u64)sm.hm[0][b] + ((u64)sm.hm[1][b] << 14) + ((u64)sm.hm[2][b] << 28);
+}
 
-// Calls f(i, bits) for every token of a row (V % 8 == 0, 16-byte aligned rows).
+// Calls g(v, vector) for every 8-token vector v of a row (V % 8 == 0,
+// 16-byte aligned rows).  A pass is bound by L2 round trips, so each thread
+// issues four 16-byte loads before it processes them.
+template <typename G>
+__device__ __forceinline__ void row_vecs(const uint16_t* row, int V, G g) {
+  const int nvec = V >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(row);
+  int k = threadIdx.x;
+  for (; k + 3 * FT < nvec; k += 4 * FT) {
+    uint4 w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w[u] = src[k + u * FT];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) g(k + u * FT, w[u]);
+  }
+  for (; k < nvec; k += FT) g(k, src[k]);
+}
+
+// Calls f(i, bits) for every token of a row.
 template <typename F>
 __device__ __forceinline__ void row_each(const uint16_t* row, int V, F f) {
-  const int nvec = V >> 3;
-  for (int k = threadIdx.x; k < nvec; k += FT) {
-    const uint4 w = *reinterpret_cast<const uint4*>(row + (int64_t)k * 8);
+  row_vecs(row, V, [&](int v, const uint4& w) {
     const uint32_t p[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      f(k * 8 + 2 * j, p[j] & 0xFFFFu);
-      f(k * 8 + 2 * j + 1, p[j] >> 16);
+      f(v * 8 + 2 * j, p[j] & 0xFFFFu);
+      f(v * 8 + 2 * j + 1, p[j] >> 16);
     }
-  }
+  });
 }
 
 // Block-wide exclusive scan of (count, mass) pairs; also leaves the totals in
@@ -148,7 +176,7 @@ __device__ void scan2(uint32_t c, u64 w, uint32_t& ce, u64& we, FiltSmem& sm) {
 __device__ void find_boundary(int k, u64 P, uint32_t c_base, u64 w_base, FiltSmem& sm) {
   const int b0 = 2 * threadIdx.x, b1 = b0 + 1;
   const uint32_t c0 = sm.hcnt[b0], c1 = sm.hcnt[b1];
-  const u64 w0 = sm.hmass[b0], w1 = sm.hmass[b1];
+  const u64 w0 = k > 0 ? 0ull : bin_mass(sm, b0), w1 = k > 0 ? 0ull : bin_mass(sm, b1);
   if (threadIdx.x == 0) sm.bsel = -1;
   uint32_t ce;
   u64 we;
@@ -183,14 +211,16 @@ __device__ void find_boundary(int k, u64 P, uint32_t c_base, u64 w_base, FiltSme
 __device__ void clear_hist(FiltSmem& sm) {
   for (int b = threadIdx.x; b < NB; b += FT) {
     sm.hcnt[b] = 0;
-    sm.hmass[b] = 0;
+    sm.hm[0][b] = 0;
+    sm.hm[1][b] = 0;
+    sm.hm[2][b] = 0;
   }
   __syncthreads();
 }
 
 struct Sel {
   u64 K;  // key of the last kept token
-  u64 S;  // kept mass, 2^-40 units
+  u64 S;  // kept mass, 2^-40 units (0 when the count criterion chose the set: not formed)
 };
 
 // Sorts sm.cand[0, n) by key descending and picks the last kept token: the
@@ -325,14 +355,13 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
     if (d <= dr) {
       const int b = min((int)__fmul_rn(d, scale), NB - 1);
       atomicAdd(&sm.hcnt[b], 1u);
-      const u64 w = wfix(d);
-      if (w) atomicAdd(&sm.hmass[b], w);
+      if (k == 0) add_mass(sm, b, wfix(d));
     }
   });
   __syncthreads();
   find_boundary(k, P, 0u, 0ull, sm);
   int b = sm.bsel;
-  if (b < 0) return Sel{0ull, sm.ctot_w};  // fewer than k finite tokens: keep them all
+  if (b < 0) return Sel{0ull, k > 0 ? 0ull : sm.ctot_w};  // fewer than k finite tokens: keep them all
   uint32_t n = sm.n_sel, c_above = sm.c_above;
   u64 w_above = sm.w_above;
   if (n <= (uint32_t)CAND) {
@@ -377,14 +406,13 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
       if (o >= lo0 && o <= hi0) {
         const int sb = (int)((hi0 - o) >> shift);
         atomicAdd(&sm.hcnt[sb], 1u);
-        const u64 w = wfix(__fsub_rn(m, scaled(h, inv_temp)));
-        if (w) atomicAdd(&sm.hmass[sb], w);
+        if (k == 0) add_mass(sm, sb, wfix(__fsub_rn(m, scaled(h, inv_temp))));
       }
     });
     __syncthreads();
     find_boundary(k, P, c_above, w_above, sm);
     b = sm.bsel;
-    if (b < 0) return Sel{0ull, sm.ctot_w + w_above};  // unreachable for a consistent histogram: keep all
+    if (b < 0) return Sel{0ull, k > 0 ? 0ull : sm.ctot_w + w_above};  // unreachable for a consistent histogram
     n = sm.n_sel;
     c_above = sm.c_above;
     w_above = sm.w_above;
@@ -409,9 +437,7 @@ struct RowStats {
 __device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp) {
   MaxSum ms{-INFINITY, 0.f};
   float lo = INFINITY;
-  const int nvec = V >> 3;
-  for (int k = threadIdx.x; k < nvec; k += FT) {
-    const uint4 w = *reinterpret_cast<const uint4*>(row + (int64_t)k * 8);
+  row_vecs(row, V, [&](int, const uint4& w) {
     const uint32_t p[4] = {w.x, w.y, w.z, w.w};
     float y[8];
 #pragma unroll
@@ -422,7 +448,7 @@ __device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp) {
     float mx = y[0];
 #pragma unroll
     for (int j = 1; j < 8; ++j) mx = fmaxf(mx, y[j]);
-    if (mx == -INFINITY) continue;
+    if (mx == -INFINITY) return;
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -430,26 +456,52 @@ __device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp) {
       if (y[j] != -INFINITY) lo = fminf(lo, y[j]);
     }
     ms = ms_merge(ms, MaxSum{mx, s});
-  }
+  });
   ms = block_maxsum(ms);
   const float mlo = -block_max(-lo);
   return RowStats{ms.m, ms.s, mlo};
 }
 
-// Top-k then top-p (either may be off: k == 0, top_p >= 1).
+// Block sum of 64-bit values in a fixed order (deterministic).
+__device__ u64 block_sum_u64(u64 v, FiltSmem& sm) {
+  uint32_t unused;
+  u64 excl;
+  scan2(0u, v, unused, excl, sm);
+  return sm.ctot_w;
+}
+
+// Exact kept mass of the tokens with key >= K.
+__device__ u64 kept_mass(const uint16_t* row, int V, float inv_temp, float m, u64 K, FiltSmem& sm) {
+  u64 acc = 0;
+  row_each(row, V, [&](int i, uint32_t h) {
+    if (make_key(ord16(h), i) >= K) acc += wfix(__fsub_rn(m, scaled(h, inv_temp)));
+  });
+  const u64 tot = block_sum_u64(acc, sm);
+  return tot;
+}
+
+__device__ __forceinline__ float key_dist(u64 K, float m, float inv_temp) {
+  return __fsub_rn(m, scaled(unord16((uint32_t)(K >> 32)), inv_temp));
+}
+
+// Top-k then top-p (either may be off: k == 0, top_p >= 1).  S of the result
+// is 0 when only the count criterion ran.
 __device__ Sel filtered_select(const uint16_t* row, int V, float inv_temp, int k, float top_p, const RowStats& st,
                                FiltSmem& sm) {
   const float dfull = st.m - st.lo;
   if (k > 0) {
     Sel s = select_tokens(row, V, inv_temp, st.m, dfull, k, 0ull, sm);
+    s.S = 0;  // the count criterion forms no mass above its boundary bin
     if (top_p < 1.f) {
-      const u64 P = (u64)((double)top_p * (double)s.S);
-      s = select_tokens(row, V, inv_temp, st.m, dfull, 0, P, sm);
+      const u64 Sk = kept_mass(row, V, inv_temp, st.m, s.K, sm);
+      const u64 P = (u64)((double)top_p * (double)Sk);
+      // the nucleus lies inside the top-k set, whose last token is at distance key_dist(K)
+      s = select_tokens(row, V, inv_temp, st.m, fminf(dfull, key_dist(s.K, st.m, inv_temp)), 0, P, sm);
     }
     return s;
   }
   const u64 P = (u64)((double)top_p * (double)st.Z * (double)FIX);
-  const float bound = __logf((float)V / (1.f - top_p)) + 1.f;
+  const float bound = __logf((float)V / ((1.f - top_p) * fmaxf(st.Z, 1.f))) + 1.f;
   return select_tokens(row, V, inv_temp, st.m, fminf(dfull, bound), 0, P, sm);
 }
 
@@ -467,15 +519,20 @@ __global__ void __launch_bounds__(FT, 1)
   const RowStats st = row_stats(row, V, inv_temp);
   const Sel s = filtered_select(row, V, inv_temp, k, top_p, st, sm);
   ArgBest best{-INFINITY, 0x7fffffff};
+  u64 acc = 0;
   row_each(row, V, [&](int i, uint32_t h) {
-    if (make_key(ord16(h), i) >= s.K)
-      best = better(best, ArgBest{scaled(h, inv_temp) + gumbel1(seed, offset, r, 4u, i), i});
+    if (make_key(ord16(h), i) >= s.K) {
+      const float y = scaled(h, inv_temp);
+      acc += wfix(__fsub_rn(st.m, y));
+      best = better(best, ArgBest{y + gumbel1(seed, offset, r, 4u, i), i});
+    }
   });
   best = block_best(best);
+  const u64 S_fix = block_sum_u64(acc, sm);
   if (threadIdx.x == 0) {
     tokens[r] = best.i;
     params[2 * r] = (int64_t)s.K;
-    const float S = sel_mass(s);
+    const float S = sel_mass(Sel{s.K, S_fix});
     params[2 * r + 1] = (int64_t)(((u64)__float_as_uint(S) << 32) | (u64)__float_as_uint(st.m));
   }
 }
@@ -491,7 +548,8 @@ __global__ void __launch_bounds__(FT, 1)
   const uint16_t* c = clean + cm_.off(r);
   const uint16_t* d = draft + dm_.off(r);
   const RowStats st = row_stats(c, V, inv_temp);
-  const Sel sc = filtered_select(c, V, inv_temp, k, top_p, st, sm);
+  Sel sc = filtered_select(c, V, inv_temp, k, top_p, st, sm);
+  if (sc.S == 0) sc.S = kept_mass(c, V, inv_temp, st.m, sc.K, sm);
   const u64 Kc = sc.K, Kd = (u64)dparams[2 * r];
   const u64 packed = (u64)dparams[2 * r + 1];
   const float md = __uint_as_float((uint32_t)packed), Sd = __uint_as_float((uint32_t)(packed >> 32));
