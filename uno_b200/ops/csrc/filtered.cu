@@ -79,13 +79,24 @@ __device__ __forceinline__ u64 make_key(uint32_t o, int i) {
 // Scaled logit and its distance below the row max.  The _rn intrinsics are
 // never contracted into FMAs, so every pass computes bit-identical values.
 __device__ __forceinline__ float scaled(uint32_t h, float inv_temp) { return __fmul_rn(bits2f(h), inv_temp); }
+// Histogram bin of a distance d in [0, dr]: floor(d * NB / dr), clamped.
+__device__ __forceinline__ int bin_of(float d, float scale) { return min((int)__fmul_rn(d, scale), NB - 1); }
+// floor(exp(-d) * 2^40): the token's mass in fixed point.
 __device__ __forceinline__ u64 wfix(float d) { return __float2ull_rz(__fmul_rn(__expf(-d), FIX)); }
-__device__ __forceinline__ void add_mass(FiltSmem& sm, int b, u64 w) {
+// Adds a token's mass to a bin as three 14-bit limbs (bits 0-13, 14-27, 28-40).
+__device__ __forceinline__ void add_mass(FiltSmem& sm, int b, float d) {
+  const u64 w = wfix(d);
   if (!w) return;
   atomicAdd(&sm.hm[0][b], (uint32_t)(w & 0x3FFFu));
   atomicAdd(&sm.hm[1][b], (uint32_t)((w >> 14) & 0x3FFFu));
   atomicAdd(&sm.hm[2][b], (uint32_t)(w >> 28));
 }
+// key(i) >= K with 32-bit operations: value above K's, or equal and id <= K's.
+struct KeyCut {
+  uint32_t o, idx;
+  __device__ __forceinline__ explicit KeyCut(u64 K) : o((uint32_t)(K >> 32)), idx(0xFFFFFFFFu - (uint32_t)K) {}
+  __device__ __forceinline__ bool keeps(uint32_t oi, int i) const { return oi > o || (oi == o && (uint32_t)i <= idx); }
+};
 __device__ __forceinline__ u64 bin_mass(const FiltSmem& sm, int b) {
   return (u64)sm.hm[0][b] + ((u64)sm.hm[1][b] << 14) + ((u64)sm.hm[2][b] << 28);
 }
@@ -353,9 +364,9 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
   row_each(row, V, [&](int, uint32_t h) {
     const float d = __fsub_rn(m, scaled(h, inv_temp));
     if (d <= dr) {
-      const int b = min((int)__fmul_rn(d, scale), NB - 1);
+      const int b = bin_of(d, scale);
       atomicAdd(&sm.hcnt[b], 1u);
-      if (k == 0) add_mass(sm, b, wfix(d));
+      if (k == 0) add_mass(sm, b, d);
     }
   });
   __syncthreads();
@@ -368,7 +379,7 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
     const int bb = b;
     collect(row, V, [&](int, uint32_t h, uint32_t) {
       const float d = __fsub_rn(m, scaled(h, inv_temp));
-      return d <= dr && min((int)__fmul_rn(d, scale), NB - 1) == bb;
+      return d <= dr && bin_of(d, scale) == bb;
     }, sm);
     return sort_and_walk((int)n, k, P, c_above, w_above, m, inv_temp, sm);
   }
@@ -383,7 +394,7 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
     const int bb = b;
     row_each(row, V, [&](int, uint32_t h) {
       const float d = __fsub_rn(m, scaled(h, inv_temp));
-      if (d <= dr && min((int)__fmul_rn(d, scale), NB - 1) == bb) {
+      if (d <= dr && bin_of(d, scale) == bb) {
         const uint32_t o = ord16(h);
         lo = min(lo, o);
         hi = max(hi, o);
@@ -406,7 +417,7 @@ __device__ Sel select_tokens(const uint16_t* row, int V, float inv_temp, float m
       if (o >= lo0 && o <= hi0) {
         const int sb = (int)((hi0 - o) >> shift);
         atomicAdd(&sm.hcnt[sb], 1u);
-        if (k == 0) add_mass(sm, sb, wfix(__fsub_rn(m, scaled(h, inv_temp))));
+        if (k == 0) add_mass(sm, sb, __fsub_rn(m, scaled(h, inv_temp)));
       }
     });
     __syncthreads();
@@ -434,7 +445,8 @@ struct RowStats {
   float m, Z, lo;
 };
 
-__device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp) {
+// need_z: top-p alone needs Z; top-k only needs m and the smallest value.
+__device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp, bool need_z) {
   MaxSum ms{-INFINITY, 0.f};
   float lo = INFINITY;
   row_vecs(row, V, [&](int, const uint4& w) {
@@ -449,13 +461,17 @@ __device__ RowStats row_stats(const uint16_t* row, int V, float inv_temp) {
 #pragma unroll
     for (int j = 1; j < 8; ++j) mx = fmaxf(mx, y[j]);
     if (mx == -INFINITY) return;
-    float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      s += __expf(y[j] - mx);
+    for (int j = 0; j < 8; ++j)
       if (y[j] != -INFINITY) lo = fminf(lo, y[j]);
+    if (need_z) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += __expf(y[j] - mx);
+      ms = ms_merge(ms, MaxSum{mx, s});
+    } else {
+      ms.m = fmaxf(ms.m, mx);
     }
-    ms = ms_merge(ms, MaxSum{mx, s});
   });
   ms = block_maxsum(ms);
   const float mlo = -block_max(-lo);
@@ -473,8 +489,9 @@ __device__ u64 block_sum_u64(u64 v, FiltSmem& sm) {
 // Exact kept mass of the tokens with key >= K.
 __device__ u64 kept_mass(const uint16_t* row, int V, float inv_temp, float m, u64 K, FiltSmem& sm) {
   u64 acc = 0;
+  const KeyCut cut(K);
   row_each(row, V, [&](int i, uint32_t h) {
-    if (make_key(ord16(h), i) >= K) acc += wfix(__fsub_rn(m, scaled(h, inv_temp)));
+    if (cut.keeps(ord16(h), i)) acc += wfix(__fsub_rn(m, scaled(h, inv_temp)));
   });
   const u64 tot = block_sum_u64(acc, sm);
   return tot;
@@ -516,12 +533,13 @@ __global__ void __launch_bounds__(FT, 1)
   FiltSmem& sm = *reinterpret_cast<FiltSmem*>(smem_raw);
   const int r = blockIdx.x;
   const uint16_t* row = x + rm.off(r);
-  const RowStats st = row_stats(row, V, inv_temp);
+  const RowStats st = row_stats(row, V, inv_temp, k == 0);
   const Sel s = filtered_select(row, V, inv_temp, k, top_p, st, sm);
+  const KeyCut cut(s.K);
   ArgBest best{-INFINITY, 0x7fffffff};
   u64 acc = 0;
   row_each(row, V, [&](int i, uint32_t h) {
-    if (make_key(ord16(h), i) >= s.K) {
+    if (cut.keeps(ord16(h), i)) {
       const float y = scaled(h, inv_temp);
       acc += wfix(__fsub_rn(st.m, y));
       best = better(best, ArgBest{y + gumbel1(seed, offset, r, 4u, i), i});
@@ -547,7 +565,7 @@ __global__ void __launch_bounds__(FT, 1)
   const int r = blockIdx.x;
   const uint16_t* c = clean + cm_.off(r);
   const uint16_t* d = draft + dm_.off(r);
-  const RowStats st = row_stats(c, V, inv_temp);
+  const RowStats st = row_stats(c, V, inv_temp, k == 0);
   Sel sc = filtered_select(c, V, inv_temp, k, top_p, st, sm);
   if (sc.S == 0) sc.S = kept_mass(c, V, inv_temp, st.m, sc.K, sm);
   const u64 Kc = sc.K, Kd = (u64)dparams[2 * r];
@@ -557,8 +575,9 @@ __global__ void __launch_bounds__(FT, 1)
   const float ic = 1.f / Sc, id = 1.f / Sd;
   const int64_t s = spec[r];
   const uint32_t hs = c[s], hd = d[s];
-  const float ps = make_key(ord16(hs), (int)s) >= Kc ? __expf(scaled(hs, inv_temp) - mc) * ic : 0.f;
-  const float qs = make_key(ord16(hd), (int)s) >= Kd ? __expf(scaled(hd, inv_temp) - md) * id : 0.f;
+  const KeyCut cc(Kc), cd(Kd);
+  const float ps = cc.keeps(ord16(hs), (int)s) ? __expf(scaled(hs, inv_temp) - mc) * ic : 0.f;
+  const float qs = cd.keeps(ord16(hd), (int)s) ? __expf(scaled(hd, inv_temp) - md) * id : 0.f;
   const float ratio = qs > 0.f ? ps / qs : 0.f;
   const Philox4 ur = philox4x32_10(0u, (uint32_t)r, 5u, 0u, seed, offset);
   if (u01(ur.x) < fminf(ratio, 1.f)) {
@@ -579,10 +598,10 @@ __global__ void __launch_bounds__(FT, 1)
     for (int j = 0; j < 8; ++j) {
       const int i = kk * 8 + j;
       const uint32_t h1 = (j & 1) ? pc[j >> 1] >> 16 : pc[j >> 1] & 0xFFFFu;
-      if (make_key(ord16(h1), i) < Kc) continue;
+      if (!cc.keeps(ord16(h1), i)) continue;
       const uint32_t h2 = (j & 1) ? pd[j >> 1] >> 16 : pd[j >> 1] & 0xFFFFu;
       const float p = __expf(scaled(h1, inv_temp) - mc) * ic;
-      const float q = make_key(ord16(h2), i) >= Kd ? __expf(scaled(h2, inv_temp) - md) * id : 0.f;
+      const float q = cd.keeps(ord16(h2), i) ? __expf(scaled(h2, inv_temp) - md) * id : 0.f;
       const float res = p - q;
       if (res > 0.f) best = better(best, ArgBest{__logf(res) + gumbel1(seed, offset, r, 6u, i), i});
     }
@@ -591,7 +610,7 @@ __global__ void __launch_bounds__(FT, 1)
   if (best.i == 0x7fffffff) {  // p == q on the support: sample p itself
     best = ArgBest{-INFINITY, 0x7fffffff};
     row_each(c, V, [&](int i, uint32_t h) {
-      if (make_key(ord16(h), i) >= Kc)
+      if (cc.keeps(ord16(h), i))
         best = better(best, ArgBest{scaled(h, inv_temp) + gumbel1(seed, offset, r, 6u, i), i});
     });
     best = block_best(best);
