@@ -12,7 +12,10 @@ alone, and the sampling case alternates two 156 MB logit blocks.
 
 Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden),
 ``lm-head``, ``decode-attention``, ``sampling`` (full-vocab verify and one
-vocab-parallel shard), ``train-attention`` (block-diffusion forward / backward).
+vocab-parallel shard), ``filtered`` (top-k / top-p sampling and verify, with
+the eager torch nucleus for comparison), ``train-attention`` (block-diffusion
+forward / backward).  A case entry marked ``eager`` (a path with host syncs,
+which a graph cannot hold) is timed as ``--repeat`` eager calls instead.
 """
 
 from __future__ import annotations
@@ -104,6 +107,47 @@ def _sampling():
     }
 
 
+def _filtered():
+    """Top-p / top-k sampling of the 64 x 7 draft rows of a decode step and the filtered verify.
+
+    Logit rows are a trained-model-like mix: a peaked head of 50 tokens over a
+    N(0, 2.5^2) bulk, so the 0.95 nucleus holds thousands of tokens."""
+    from uno_b200.engine import sampling as S
+    from uno_b200.ops import cuda as C
+
+    B, L, V = 64, 8, 151936
+    head = torch.linspace(12, 4, 50, device="cuda")
+
+    def block():
+        x = torch.randn(B, L, V, device="cuda") * 2.5
+        x[:, :, :50] += head
+        return x.bfloat16()
+
+    blocks = [block(), block()]  # 2 x 156 MB
+    rows = B * (L - 1)
+    drafted = [C.filtered_sample(b[:, 1:], 1.0, 0, 0.95, 1, 0) for b in blocks]
+    nbytes = rows * V * 2
+
+    def sample(k, p):
+        return lambda i: C.filtered_sample(blocks[i % 2][:, 1:], 1.0, k, p, 1, i)
+
+    def verify(i):
+        j = i % 2
+        spec, params = drafted[1 - j]
+        C.filtered_verify(blocks[j][:, : L - 1], blocks[1 - j][:, 1:], params, spec, 1.0, 0, 0.95, 1, i)
+
+    return {
+        f"filtered_sample top-p 0.95, {rows} rows": (sample(0, 0.95), 0, nbytes),
+        f"filtered_sample top-k 50, {rows} rows": (sample(50, 1.0), 0, nbytes),
+        f"filtered_sample top-k 50 + top-p 0.9, {rows} rows": (sample(50, 0.9), 0, nbytes),
+        f"filtered_verify top-p 0.95, {rows} rows": (verify, 0, 2 * nbytes),
+        f"torch sparse_top_p 0.95 (eager), {rows} rows": (
+            lambda i: S.sparse_top_p(blocks[i % 2][:, 1:].reshape(-1, V), 1.0, 0.95), 0, nbytes, "eager"),
+        f"torch topk 50 (eager), {rows} rows": (
+            lambda i: torch.topk(blocks[i % 2][:, 1:].reshape(-1, V), 50, dim=-1), 0, nbytes, "eager"),
+    }
+
+
 def _decode_attention():
     from uno_b200.layers.meta import ForwardMeta, Mode, causal_suffix_masks
     from uno_b200.ops import cuda as C
@@ -169,7 +213,7 @@ def _train_attention():
 
 
 CASES = {"layer-gemms": _layer_gemms, "lm-head": _lm_head, "decode-attention": _decode_attention,
-         "sampling": _sampling, "train-attention": _train_attention}
+         "sampling": _sampling, "filtered": _filtered, "train-attention": _train_attention}
 
 
 def main(argv=None):
@@ -182,16 +226,29 @@ def main(argv=None):
     torch.manual_seed(0)
     cases = CASES[args.case]()
     for i in range(2):
-        for fn, _, _ in cases.values():
+        for fn, *_ in cases.values():
             fn(i)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("capture")
-    for fn, _, _ in cases.values():
+    for fn, *_ in cases.values():
         fn(2)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     out = []
-    for name, (fn, flops, nbytes) in cases.items():
+    for name, (fn, flops, nbytes, *mode) in cases.items():
+        if mode == ["eager"]:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(args.repeat):
+                fn(i)
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / args.repeat
+            rec = {"kernel": name, "us": round(ms * 1e3, 2), "tflops": None, "gbs": round(nbytes / ms / 1e6, 1),
+                   "timing": "eager calls (host syncs included)"}
+            out.append(rec)
+            print(json.dumps(rec))
+            continue
         # replay a CUDA graph of back-to-back launches: host launch cost stays off the clock
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
