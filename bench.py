@@ -167,6 +167,12 @@ def engine_kwargs(args, tp: int) -> dict:
     ) | ({"tree_verify_size": 64, "tree_candidate_top_k": 4} if getattr(args, "sampler", "linear") == "tree" else {})
 
 
+def emit(obj) -> None:
+    """One JSON line in a single write, so that another rank's output cannot split it."""
+    sys.stdout.write(json.dumps(obj) + "\n")
+    sys.stdout.flush()
+
+
 def _filter_note(args) -> str:
     parts = ([f"top-k {args.top_k}"] if args.top_k else []) + ([f"top-p {args.top_p}"] if args.top_p else [])
     return (", " + ", ".join(parts)) if parts else ""
@@ -266,7 +272,7 @@ def run_dp_replicas(args):
             "clocks": clock_info, "e2e": e2e,
             "gpu_launches": launches * args.steps if launches is not None else None, "impl": "native",
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     llm.exit()
     if world > 1:
         dist.destroy_process_group()
@@ -376,9 +382,9 @@ def run_native(args):
         "gpu_launches": launches * args.steps if launches is not None else None,
         "impl": "native",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     if breakdown is not None:
-        print(json.dumps({"breakdown": breakdown, "n_gpus": args.gpus}), flush=True)
+        emit({"breakdown": breakdown, "n_gpus": args.gpus})
     llm.exit()
 
 

@@ -89,3 +89,37 @@ def test_fsdp_sharded_projection_gemms_match_replicated(world):
            "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(HERE, "fsdp_worker.py")]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "FSDP_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_data_parallel_replicas_match_one_engine_gpu():
+    """``LLM(..., data_parallel_size=2)``: one engine process per GPU, prompts dealt round-robin.
+
+    Greedy Psi-Spec output is the AR greedy output whatever the drafts, so each
+    request's leading tokens equal those of a single in-process engine (later
+    tokens may differ where a near-tie sees another batch composition)."""
+    from uno_b200 import LLM, SamplingParams
+    from uno_b200.utils.hf_compat import ModelConfig
+
+    cfg = ModelConfig(model_type="qwen3", vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                      max_position_embeddings=2048, eos_token_id=None, mask_token_id=2000)
+    kw = dict(max_num_seqs=4, max_model_len=256, kvcache_block_size=64, dummy_lora_rank=16, max_diffusion_block_size=4,
+              enforce_eager=True, gpu_memory_utilization=0.2, num_kvcache_blocks=64)
+    prompts = [list(range(1 + 7 * i, 30 + 7 * i)) for i in range(5)]
+    sp = SamplingParams(temperature=0.0, max_tokens=16, diffusion_block_size=4, mask_token_id=2000, ignore_eos=True)
+    dp = LLM(cfg, data_parallel_size=2, **kw)
+    try:
+        got = [o["token_ids"] for o in dp.generate(prompts, sp, use_tqdm=False, detokenize=False)]
+        stats = dp.last_generate_stats
+    finally:
+        dp.exit()
+    one = LLM(cfg, **kw)
+    try:
+        want = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False, detokenize=False)]
+    finally:
+        one.exit()
+    assert len(got) == len(prompts) and all(len(t) >= 16 for t in got)
+    assert stats["forwards"] > 0
+    for a, b in zip(got, want):
+        assert a[:6] == b[:6], (a, b)

@@ -14,6 +14,7 @@ import atexit
 import logging
 import os
 import socket
+import sys
 from time import perf_counter, perf_counter_ns
 from typing import Callable
 
@@ -144,7 +145,8 @@ class LLMEngine:
         if getattr(self, "_exited", True):
             return
         self._exited = True
-        print(f"Engine stats: preemptions={self.scheduler.num_preemptions}", flush=True)
+        sys.stdout.write(f"Engine stats: preemptions={self.scheduler.num_preemptions}\n")  # one write: ranks share stdout
+        sys.stdout.flush()
         try:
             self.call("exit")
         except Exception:  # pragma: no cover - best-effort teardown

@@ -286,7 +286,7 @@ __device__ Sel sort_and_walk(int n, int k, u64 P, uint32_t c_above, u64 w_above,
   }
   if (mine >= 0) atomicMax(&sm.jstar, mine);
   __syncthreads();
-  const int js = sm.jstar;
+  const int js = max(sm.jstar, 0);  // >= 0 whenever the histogram and the collection agree
   if (js >= j0 && js < j0 + 4) {
     u64 s = excl;
 #pragma unroll
@@ -574,10 +574,11 @@ __global__ void __launch_bounds__(FT, 1)
   const float mc = st.m, Sc = sel_mass(sc);
   const float ic = 1.f / Sc, id = 1.f / Sd;
   const int64_t s = spec[r];
-  const uint32_t hs = c[s], hd = d[s];
+  const bool s_ok = s >= 0 && s < V;  // an out-of-range draft token has probability 0 and is rejected
+  const uint32_t hs = s_ok ? c[s] : 0u, hd = s_ok ? d[s] : 0u;
   const KeyCut cc(Kc), cd(Kd);
-  const float ps = cc.keeps(ord16(hs), (int)s) ? __expf(scaled(hs, inv_temp) - mc) * ic : 0.f;
-  const float qs = cd.keeps(ord16(hd), (int)s) ? __expf(scaled(hd, inv_temp) - md) * id : 0.f;
+  const float ps = s_ok && cc.keeps(ord16(hs), (int)s) ? __expf(scaled(hs, inv_temp) - mc) * ic : 0.f;
+  const float qs = s_ok && cd.keeps(ord16(hd), (int)s) ? __expf(scaled(hd, inv_temp) - md) * id : 0.f;
   const float ratio = qs > 0.f ? ps / qs : 0.f;
   const Philox4 ur = philox4x32_10(0u, (uint32_t)r, 5u, 0u, seed, offset);
   if (u01(ur.x) < fminf(ratio, 1.f)) {
