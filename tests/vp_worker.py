@@ -4,11 +4,13 @@ Every rank builds the same full logits from a common seed, keeps its vocabulary
 shard, and runs the vocab-parallel sample / arg-max / verify kernels over the
 fused-collective workspace; the results must equal the single-GPU kernels on
 the full rows (samples and arg-max exactly, verify decisions up to summation
-order, which these inputs do not reach).
+order, which these inputs do not reach).  The draft-tree candidates merged from
+the shards must equal the top-K of the full rows, and build the same trees.
 """
 
 import os
 import sys
+from types import SimpleNamespace
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -55,6 +57,34 @@ def main():
             failures.append(f"resample rows={rows}: {(corr_w[rej] != corr_g[rej]).sum().item()} differ")
         if not (0 < int(acc_w.sum()) < rows or rows < 16):
             failures.append(f"rows={rows}: accept mix not exercised ({int(acc_w.sum())})")
+    # draft-tree candidates: per-shard top-K merged over the group == top-K of the full rows
+    from uno_b200.engine.draft_tree import build_draft_tree_batch, shard_candidate_log_probs
+
+    def gather(x):
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous())
+        return torch.cat(parts, dim=-1)
+
+    for B, D, K in ((1, 7, 4), (8, 7, 16)):
+        full = (torch.randn(B, D + 1, V, device="cuda", generator=g) * 3).bfloat16()
+        draft = full[:, 1:]
+        ids, lp = shard_candidate_log_probs(draft[:, :, rank * Vs:(rank + 1) * Vs], K, 1.0, rank * Vs, gather)
+        want_ids = torch.empty(B * D, K, device="cuda", dtype=torch.int64)
+        want_lp = torch.empty(B * D, K, device="cuda", dtype=torch.float32)
+        cuda.ext().topk_lse(draft.reshape(B * D, V).contiguous(), K, 1.0, want_ids, want_lp)
+        if not torch.equal(ids.reshape(B * D, K), want_ids):
+            failures.append(f"tree candidates B={B} K={K}: ids differ")
+        if float((lp.reshape(B * D, K) - want_lp).abs().max()) > 1e-4:
+            failures.append(f"tree candidates B={B} K={K}: log-probs differ")
+        roots = torch.arange(B, device="cuda", dtype=torch.int64) + 3
+        t_full = build_draft_tree_batch(roots, draft, max_nodes=16, candidate_top_k=K, temperature=1.0)
+
+        t_vp = build_draft_tree_batch(roots, draft[:, :, rank * Vs:(rank + 1) * Vs], max_nodes=16,
+                                      candidate_top_k=K, temperature=1.0,
+                                      shard=SimpleNamespace(start=rank * Vs, gather=gather))
+        if not (torch.equal(t_full.token_ids, t_vp.token_ids) and torch.equal(t_full.parent_indices,
+                                                                               t_vp.parent_indices)):
+            failures.append(f"tree B={B} K={K}: trees differ")
     err = cuda.error_flag()
     if err:
         failures.append(f"device error flag {err}")

@@ -128,7 +128,8 @@ class TwoPassDecoder:
                 spec, q_sparse = self.sampler.sample(spec_rows, sp)
                 proposal[:, 1:] = spec.view(B, L - 1)
         else:
-            logits = self.sampler.full(logits)  # the tree builder ranks candidates over the whole vocabulary
+            # Under vocab parallelism the logits stay sharded: the root is sampled by the
+            # vocab-parallel sampler and the tree builder merges per-shard candidates.
             proposal = torch.zeros((B, L), dtype=torch.int64, device=logits.device)
             root, _ = self.sampler.sample(logits[:, 0, :], sp)
             proposal[:, 0] = root
@@ -225,9 +226,11 @@ class TwoPassDecoder:
     def tree_verify_stage(self, seqs, root_tokens, draft_logits, L: int, sp: SamplingParams):
         B = len(seqs)
         Q = int(self.tree_verify_size)
+        sharded = self.sampler.vocab_size(draft_logits) != draft_logits.shape[-1]
+        shard = self.sampler.shard if sharded else None
         tree = build_draft_tree_batch(root_tokens, draft_logits, max_nodes=Q,
                                       candidate_top_k=self.tree_candidate_top_k,
-                                      temperature=sp.temperature)
+                                      temperature=sp.temperature, shard=shard)
         logits = self.run_tree(seqs, tree.token_ids, tree.depths, tree.parent_indices)  # [B, Q, V]
         targets, _ = self.sampler.sample(logits.reshape(-1, logits.shape[-1]), sp)
         targets = targets.view(B, Q)

@@ -98,19 +98,69 @@ def candidate_log_probs(draft_logits: torch.Tensor, k: int, temperature: float):
     return ids, values - torch.logsumexp(scaled, dim=-1, keepdim=True)
 
 
+def shard_candidate_log_probs(shard_logits: torch.Tensor, k: int, temperature: float, vocab_start: int,
+                              gather) -> tuple[torch.Tensor, torch.Tensor]:
+    """:func:`candidate_log_probs` of the full vocabulary from this rank's shard ``[B, D, V/tp]``.
+
+    Each rank takes the top-K of its shard with log-softmax values over the
+    shard, recovers the shard's log-normaliser from its best candidate, and
+    ``gather`` (an all-gather over the last dimension of the tensor-parallel
+    group) exchanges those K ids, K values and one normaliser per row -- not the
+    logits.  Every rank then merges the same ``tp * K`` candidates: global
+    log-probability = shard log-probability + shard normaliser - logsumexp of
+    the normalisers, and the best K of them.  The reference gathers the full
+    logits to rank 0 for this (``nano_vllm_uno/layers/embed_head.py:62-65``).
+    """
+    B, D, Vs = shard_logits.shape
+    K = min(int(k), Vs)
+    rows = shard_logits.reshape(B * D, Vs)
+    inv_t = 1.0 / float(temperature) if temperature > 0 else 1.0
+    if rows.is_cuda and rows.dtype == torch.bfloat16 and K <= 32:
+        from uno_b200.ops.cuda import ext
+
+        rows = rows.contiguous()
+        ids = torch.empty(B * D, K, device=rows.device, dtype=torch.int64)
+        lp = torch.empty(B * D, K, device=rows.device, dtype=torch.float32)
+        ext().topk_lse(rows, K, inv_t, ids, lp)
+    else:
+        ids, lp = candidate_log_probs(rows[:, None, :], K, temperature)
+        ids, lp = ids[:, 0], lp[:, 0].float()
+    # x_best / T - log_softmax(x_best) = the shard's log-normaliser
+    lse = rows.gather(1, ids[:, :1]).float() * inv_t - lp[:, :1]
+    packed = torch.cat([(ids + int(vocab_start)).double(), lp.double(), lse.double()], dim=1)
+    everyone = gather(packed)
+    tp = everyone.shape[1] // (2 * K + 1)
+    everyone = everyone.view(B * D, tp, 2 * K + 1)
+    g_ids = everyone[..., :K].round().long()
+    g_lse = everyone[..., 2 * K]
+    shift = (g_lse - torch.logsumexp(g_lse, dim=1, keepdim=True))[..., None]
+    cand = (everyone[..., K:2 * K] + shift).reshape(B * D, tp * K)
+    vals, pos = torch.topk(cand, K, dim=1, sorted=True)
+    out_ids = g_ids.reshape(B * D, tp * K).gather(1, pos)
+    return out_ids.view(B, D, K), vals.float().view(B, D, K)
+
+
 def build_draft_tree_batch(root_tokens: torch.Tensor, draft_logits: torch.Tensor, *, max_nodes: int,
-                           candidate_top_k: int, temperature: float) -> DraftTreeBatch:
+                           candidate_top_k: int, temperature: float, shard=None) -> DraftTreeBatch:
+    """Best-first draft trees from ``[B, depth, V]`` draft logits.  With ``shard``
+    (a vocab-parallel ``VocabShard``) the logits are this rank's vocabulary
+    slice and the candidates come from :func:`shard_candidate_log_probs`."""
     if root_tokens.dim() != 1:
         raise ValueError("root_tokens must have shape [B]")
     if draft_logits.dim() != 3 or draft_logits.shape[0] != root_tokens.shape[0]:
         raise ValueError("draft_logits must have shape [B, depth, vocab]")
     if candidate_top_k < 1:
         raise ValueError("candidate_top_k must be >= 1")
+    candidates = None
+    if shard is not None:
+        candidates = shard_candidate_log_probs(draft_logits, candidate_top_k, temperature, shard.start, shard.gather)
     if draft_logits.is_cuda:
         from uno_b200.ops import cuda
 
-        return cuda.build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature)
-    ids, lps = candidate_log_probs(draft_logits, candidate_top_k, temperature)
+        return cuda.build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature,
+                                     candidates=candidates)
+    ids, lps = candidates if candidates is not None else candidate_log_probs(draft_logits, candidate_top_k,
+                                                                             temperature)
     trees = [build_tree_from_candidates(r, t, lp, max_nodes)
              for r, t, lp in zip(root_tokens.tolist(), ids.tolist(), lps.tolist())]
     for tree in trees:

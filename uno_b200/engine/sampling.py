@@ -33,8 +33,9 @@ the lm_head leaves each rank a ``[rows, V/tp]`` logits shard and
 sampling and the unfiltered verify then run the vocab-parallel kernels, which
 exchange a few numbers per row between ranks instead of the logits; the
 Philox noise is keyed by global token id, so the tokens equal those of the
-same logits on one GPU.  Top-k / top-p and the draft tree gather the full
-logits first (``Sampler.full``).
+same logits on one GPU.  Top-k / top-p gather the full logits first
+(``Sampler.full``); the draft tree merges per-shard top-K candidates
+(``draft_tree.shard_candidate_log_probs``).
 """
 
 from __future__ import annotations

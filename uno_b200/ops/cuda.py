@@ -451,21 +451,28 @@ def vp_verify(clean, draft, spec, inv_temp, seed, offset, vocab_start):
     return acc, corr
 
 
-def build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature):
+def build_draft_tree(root_tokens, draft_logits, max_nodes, candidate_top_k, temperature, candidates=None):
+    """Draft trees on the device; ``candidates`` = precomputed ``(ids, log-probs)`` ``[B, D, K]``."""
     from uno_b200.engine.draft_tree import DraftTreeBatch
 
     B, D, V = draft_logits.shape
-    K = min(int(candidate_top_k), V)
-    rows = draft_logits.reshape(B * D, V)
-    ids = torch.empty(B * D, K, device=rows.device, dtype=torch.int64)
-    lp = torch.empty(B * D, K, device=rows.device, dtype=torch.float32)
-    inv_t = 1.0 / temperature if temperature > 0 else 1.0
-    ext().topk_lse(rows, K, inv_t, ids, lp)
-    tok = torch.empty(B, max_nodes, device=rows.device, dtype=torch.int64)
+    if candidates is not None:
+        ids, lp = (c.reshape(B * D, -1).contiguous() for c in candidates)
+        lp = lp.float()
+        K = ids.shape[1]
+    else:
+        K = min(int(candidate_top_k), V)
+        rows = draft_logits.reshape(B * D, V)
+        ids = torch.empty(B * D, K, device=rows.device, dtype=torch.int64)
+        lp = torch.empty(B * D, K, device=rows.device, dtype=torch.float32)
+        inv_t = 1.0 / temperature if temperature > 0 else 1.0
+        ext().topk_lse(rows, K, inv_t, ids, lp)
+    dev = draft_logits.device
+    tok = torch.empty(B, max_nodes, device=dev, dtype=torch.int64)
     par = torch.empty_like(tok)
     dep = torch.empty_like(tok)
-    mass = torch.empty(B, max_nodes, device=rows.device, dtype=torch.float32)
-    count = torch.empty(B, device=rows.device, dtype=torch.int32)
+    mass = torch.empty(B, max_nodes, device=dev, dtype=torch.float32)
+    count = torch.empty(B, device=dev, dtype=torch.int32)
     ext().build_tree(root_tokens.contiguous(), ids.view(B, D, K), lp.view(B, D, K), int(max_nodes), tok, par, dep,
                      mass, count)
     return DraftTreeBatch(tok, par, dep, mass)
