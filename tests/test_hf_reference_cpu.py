@@ -2,9 +2,9 @@
 
 A random-init ``Qwen3ForCausalLM`` written with ``save_pretrained`` is loaded
 by this framework from the same directory (HF safetensors layout and config).
-Greedy decoding through ``LLM.generate`` -- plain autoregressive (block 1) and
-Psi-Spec with diffusion blocks of 4, whose output is the AR greedy output
-whatever the drafts -- must reproduce ``transformers``' own greedy
+Greedy decoding through ``LLM.generate`` -- plain autoregressive (block 1),
+linear Psi-Spec with diffusion blocks of 4 and the tree sampler, whose output
+is the AR greedy output whatever the drafts -- must reproduce ``transformers``' own greedy
 ``generate`` token for token.  The checkpoint carries no diffusion adapter, so
 the engine adds a random gated LoRA for the drafts (``dummy_lora_rank``).
 """
@@ -34,8 +34,8 @@ def hf_dir(tmp_path_factory):
 PROMPTS = [[5, 17, 300, 42, 9, 1000, 7, 88], [1203, 4, 4, 77, 3050, 12, 600, 2, 31, 999, 18, 250]]
 
 
-@pytest.mark.parametrize("block", [1, 4])
-def test_greedy_generation_matches_transformers(hf_dir, block):
+@pytest.mark.parametrize("block,tree", [(1, False), (4, False), (4, True)])
+def test_greedy_generation_matches_transformers(hf_dir, block, tree):
     from uno_b200 import LLM, SamplingParams
 
     path, model = hf_dir
@@ -45,8 +45,9 @@ def test_greedy_generation_matches_transformers(hf_dir, block):
             ids = model.generate(torch.tensor([p]), max_new_tokens=NEW, do_sample=False, eos_token_id=None,
                                  pad_token_id=0)
             want.append(ids[0, len(p):].tolist())
+    extra = {"tree_verify_size": 8, "tree_candidate_top_k": 3} if tree else {}
     llm = LLM(str(path), device="cpu", max_num_seqs=2, max_model_len=128, kvcache_block_size=64,
-              dummy_lora_rank=8, max_diffusion_block_size=4)
+              dummy_lora_rank=8, max_diffusion_block_size=4, **extra)
     try:
         sp = SamplingParams(temperature=0.0, max_tokens=NEW, diffusion_block_size=block, mask_token_id=4000,
                             ignore_eos=True)
