@@ -5,7 +5,7 @@
 set -euo pipefail
 cd "$(dirname "${BASH_SOURCE[0]}")/../.."
 MODEL="${MODEL:?set MODEL to the Uno Qwen3-8B checkpoint directory or hub id}"
-OUT="${OUT:-eval_runs/$(date -u +%Y%m%dT%H%M%SZ)}"
+OUT="${OUT:-${RESULTS_ROOT:-eval_runs}/${RUN_NAME:-$(date -u +%Y%m%dT%H%M%SZ)}}"
 BENCHMARKS=(${BENCHMARKS:-gsm8k math500 aime25 gpqa_diamond humaneval mbpp ifeval})
 mkdir -p "${OUT}"
 python -m uno_b200.eval.prepare "${BENCHMARKS[@]}" ${SOURCE_DIR:+--source-dir "${SOURCE_DIR}"}

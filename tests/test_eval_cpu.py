@@ -353,3 +353,62 @@ def test_prepare_builders_render_protocol_prompts():
                       "private_test_cases": packed, "metadata": json.dumps({"func_name": "f"}), "starter_code": "x"}])[0]
     assert len(json.loads(lcb["ground_truth"])) == 2 and json.loads(lcb["ground_truth"])[0]["method_name"] == "f"
     assert lcb["chat_input"][0]["role"] == "system" and "```python\nx\n```" in lcb["chat_input"][1]["content"]
+
+
+def test_pull_suite_jobs_manifest_and_scoring(tmp_path):
+    """``jobs`` expands a registered benchmark with the canonical prompt rendering and budgets;
+    ``score`` splits the results per benchmark and grades them."""
+    from uno_b200.eval.benchmarks import get_benchmark
+    from uno_b200.eval.pull_suite import build_jobs, score_results, suite_sampling
+    from uno_b200.utils.hf_compat import load_model_config, load_tokenizer
+
+    model = _chat_model_dir(tmp_path)
+    tok = load_tokenizer(str(model), load_model_config(str(model)))
+    root = tmp_path / "data"
+    root.mkdir()
+    bench = get_benchmark("gsm8k")
+    (root / bench.data_path.name).write_text(_dataset(tmp_path).read_text())
+    jobs, entries = build_jobs(["gsm8k"], tok, data_root=root, context_length=64, reserve=8)
+    assert len(jobs) == 2 * bench.num_samples
+    assert {(j["id"], j["sample"]) for j in jobs} == {("q1", 0), ("q1", 1), ("q2", 0), ("q2", 1)}
+    assert all(j["max_tokens"] == 64 - len(j["prompt_ids"]) - 8 for j in jobs)
+    assert entries[0]["rows"] == 2 and entries[0]["num_samples"] == bench.num_samples
+    assert suite_sampling(entries) == {"temperature": 1.0, "top_p": 0.95, "top_k": None}
+    assert suite_sampling(entries, {"top_p": 0.5})["top_p"] == 0.5
+    # a prompt longer than the context gets no job
+    short, e2 = build_jobs(["gsm8k"], tok, data_root=root, context_length=12, reserve=8)
+    assert short == [] and e2[0]["skipped_no_budget"] == 2
+    results = tmp_path / "results.jsonl"
+    results.write_text("".join(json.dumps({"benchmark": "gsm8k", "id": j["id"], "sample": j["sample"],
+                                           "generation": "so \\boxed{5}", "ground_truth": j["ground_truth"]}) + "\n"
+                               for j in jobs))
+    summary = score_results(results, {"benchmarks": entries}, tmp_path / "run")
+    assert summary["gsm8k"]["rows"] == 4 and summary["gsm8k"]["accuracy"] == 0.5  # q1 (5) right, q2 (2) wrong
+    assert (tmp_path / "run" / "gsm8k" / "scores.json").is_file()
+
+
+def test_suite_launchers_dry_run(tmp_path):
+    """The suite and Slurm launchers print their commands under DRY_RUN=1 and run nothing."""
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    base = dict(os.environ, DRY_RUN="1", MODEL="preset:tiny-qwen3", RESULTS_ROOT=str(tmp_path / "results"))
+
+    def run(script, **env):
+        out = subprocess.run(["bash", os.path.join(root, "uno_b200", "eval", script)], env={**base, **env},
+                             capture_output=True, text=True, timeout=120)
+        assert out.returncode == 0, out.stderr
+        return out.stdout.splitlines()
+
+    lines = run("run_suite.sh", BENCHMARKS="gsm8k math500")
+    assert len(lines) == 2 and lines[0].startswith("run:") and "BENCHMARKS=gsm8k" in lines[0]
+    lines = run("submit_suite.sh", BENCHMARKS="gsm8k aime25", SBATCH_ARGS="--partition=p1")
+    assert len(lines) == 2 and all("sbatch" in ln and "--partition=p1" in ln for ln in lines)
+    lines = run("submit_pull_suite.sh", BENCHMARKS="ifeval")
+    assert len(lines) == 1 and "run_pull_suite_slurm.sh" in lines[0] and "BENCHMARKS=ifeval" in lines[0]
+    lines = run("run_pull_suite_slurm.sh", BENCHMARKS="gsm8k", SLURM_JOB_ID="77", SLURM_NNODES="2",
+                SLURM_NTASKS="16", TOP_P="0.9")
+    roles = [ln.split(":", 1)[0] for ln in lines]
+    assert roles == ["jobs", "coord", "worker", "score"]
+    assert "--top-p 0.9" in lines[0] and "--num-workers 16" in lines[1] and "--ntasks=16" in lines[2]
+    assert not (tmp_path / "results").exists()  # a dry run writes nothing
