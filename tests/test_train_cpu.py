@@ -414,3 +414,31 @@ def test_openthoughts_encoding_budget_alignment_and_hash(tmp_path):
     man = prepare(str(src), tmp_path / "out", Tok())
     assert man["hash"]["row_count"] == 3
     prepare(str(src), tmp_path / "again", Tok(), verify_against=tmp_path / "out")   # same corpus verifies
+
+
+def test_fixed_curriculum_builder(tmp_path):
+    import pytest
+
+    from uno_b200.train.curriculum import BlockCurriculumPlan, fixed_curriculum, write_curriculum
+    from uno_b200.train.make_curriculum import main as make_curriculum
+
+    m = fixed_curriculum("0.5")  # 0.5 x 9375 = 4687.5 steps, rounded half up
+    plan = BlockCurriculumPlan.from_mapping(m)
+    assert plan.max_steps == 4688 and [s.block_size for s in plan.stages] == [8]
+    assert m["tokens_per_step"] == 4096 * 128 and m["total_tokens"] == 4688 * 4096 * 128
+    assert m["requested_epochs"] == "0.5" and m["resolved_epochs"].startswith("0.50005")
+    with pytest.raises(ValueError):
+        fixed_curriculum("0")
+    with pytest.raises(ValueError):
+        fixed_curriculum("nan")
+    out = tmp_path / "c" / "b16.yaml"
+    got = make_curriculum(["fixed", "--output", str(out), "--epochs", "2", "--block-size", "16",
+                           "--steps-per-epoch", "10", "--global-batch-size", "4", "--sequence-length", "64"])
+    loaded = BlockCurriculumPlan.from_yaml(out)
+    assert got["max_steps"] == loaded.max_steps == 20 and loaded.stages[0].block_size == 16
+    assert got["sha256"] == loaded.sha256()
+    write_curriculum(out, fixed_curriculum("2", block_size=16, steps_per_epoch=10, global_batch_size=4,
+                                           sequence_length=64))  # the same plan: kept
+    with pytest.raises(FileExistsError):
+        write_curriculum(out, fixed_curriculum("3", block_size=16, steps_per_epoch=10, global_batch_size=4,
+                                               sequence_length=64))

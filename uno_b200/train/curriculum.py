@@ -128,3 +128,56 @@ class BlockCurriculumPlan:
 
     def sha256(self) -> str:
         return hashlib.sha256(json.dumps(self.manifest(), sort_keys=True, separators=(",", ":")).encode()).hexdigest()
+
+
+# The released recipe's data definition: 4,096-token rows, 128 rows per optimizer
+# step and 9,375 steps per pass over the corpus (``training/constants.py:14-18``).
+RECIPE_SEQUENCE_LENGTH = 4096
+RECIPE_GLOBAL_BATCH = 128
+RECIPE_STEPS_PER_EPOCH = 9375
+RECIPE_SEED = 20260813
+
+
+def fixed_curriculum(epochs, *, block_size: int = 8, sequence_length: int = RECIPE_SEQUENCE_LENGTH,
+                     global_batch_size: int = RECIPE_GLOBAL_BATCH, steps_per_epoch: int = RECIPE_STEPS_PER_EPOCH,
+                     seed: int = RECIPE_SEED) -> dict[str, Any]:
+    """A one-stage curriculum mapping: ``epochs`` passes at one block size.
+
+    The step count is ``epochs * steps_per_epoch`` rounded half up (at least
+    one step), so a fractional epoch count names a whole number of optimizer
+    steps; the mapping records both the requested and the resolved epochs.
+    Behaviour of ``training/create_fixed_curriculum.py``.
+    """
+    from decimal import ROUND_HALF_UP, Decimal, InvalidOperation
+
+    try:
+        e = Decimal(str(epochs))
+    except InvalidOperation as exc:
+        raise ValueError(f"epochs must be a number, got {epochs!r}") from exc
+    if not e.is_finite() or e <= 0:
+        raise ValueError("epochs must be a finite positive number")
+    if min(block_size, sequence_length, global_batch_size, steps_per_epoch) <= 0:
+        raise ValueError("block size, sequence length, global batch and steps per epoch must be positive")
+    steps = max(1, int((e * steps_per_epoch).to_integral_value(rounding=ROUND_HALF_UP)))
+    tps = sequence_length * global_batch_size
+    return {"version": 1, "requested_epochs": str(e), "resolved_epochs": str(Decimal(steps) / Decimal(steps_per_epoch)),
+            "steps_per_epoch": steps_per_epoch, "tokens_per_step": tps, "sequence_length": sequence_length,
+            "global_batch_size": global_batch_size, "total_tokens": steps * tps, "seed": seed,
+            "stages": [{"block_size": block_size, "tokens": steps * tps}]}
+
+
+def write_curriculum(path: str | Path, mapping: dict[str, Any]) -> Path:
+    """Writes the YAML atomically; an existing file must already hold the same plan."""
+    import yaml
+
+    path = Path(path)
+    text = yaml.safe_dump(mapping, sort_keys=False)
+    if path.exists():
+        if path.read_text() != text:
+            raise FileExistsError(f"{path} holds a different curriculum; refusing to replace it")
+        return path
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.with_name(path.name + ".tmp")
+    tmp.write_text(text)
+    tmp.replace(path)
+    return path

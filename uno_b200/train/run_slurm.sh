@@ -6,6 +6,9 @@
 # framework's trainer (`python -m uno_b200.train`, FSDP base weights + ZeRO-2
 # LoRA optimizer state).
 #
+# FIXED_BLOCK_SIZE=B (with EPOCHS, default 1) trains at one block size through a
+# generated one-stage curriculum instead of CURRICULUM.
+#
 # Required: MODEL (checkpoint dir or preset:NAME), DATA (prepared rows.jsonl
 # directory or "synthetic"), OUTPUT_ROOT (shared storage).  Optional knobs
 # below; GLOBAL_BATCH must divide by NODES * GPUS_PER_NODE * MICRO_BATCH
@@ -42,6 +45,13 @@ if (( GLOBAL_BATCH % per_step != 0 )); then
 fi
 OUTPUT_DIR="${OUTPUT_DIR:-${OUTPUT_ROOT}/runs/${RUN_NAME}}"
 LOG_DIR="${LOG_DIR:-${OUTPUT_ROOT}/logs/${RUN_NAME}}"
+if [[ -z "${CURRICULUM}" && -n "${FIXED_BLOCK_SIZE:-}" && "${UNO_NODE_WORKER:-0}" != "1" ]]; then
+  # one block size for EPOCHS passes (python -m uno_b200.train.make_curriculum)
+  CURRICULUM="${OUTPUT_DIR}/curriculum-b${FIXED_BLOCK_SIZE}.yaml"
+  (cd "${REPO_ROOT}" && "${PYTHON_BIN}" -m uno_b200.train.make_curriculum fixed --output "${CURRICULUM}" \
+    --epochs "${EPOCHS:-1}" --block-size "${FIXED_BLOCK_SIZE}" --sequence-length "${SEQ_LEN}" \
+    --global-batch-size "${GLOBAL_BATCH}")
+fi
 export REPO_ROOT PYTHON_BIN NODES GPUS_PER_NODE MICRO_BATCH GLOBAL_BATCH SEQ_LEN LORA_RANK LORA_TARGET LR \
   WARMUP_STEPS TV_WEIGHT KL_WEIGHT CE_WEIGHT CE_TARGET CURRICULUM RUN_NAME MODEL DATA OUTPUT_DIR LOG_DIR
 
