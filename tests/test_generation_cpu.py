@@ -125,3 +125,18 @@ def test_model_token_ids_rules(tmp_path):
     assert resolve_model_token_ids(str(k2), tok, noise_mode="random_uniform")[0] == 4096
     with pytest.raises(ValueError, match="mask token"):
         resolve_model_token_ids(str(k2), tok, noise_mode="mask")
+
+
+def test_hub_prefetch_reuses_the_cache(tmp_path):
+    from uno_b200.utils.hub import PINNED_MODEL_ID, PINNED_MODEL_REVISION, main
+
+    repo = tmp_path / ("models--" + PINNED_MODEL_ID.replace("/", "--"))
+    snap = repo / "snapshots" / PINNED_MODEL_REVISION
+    snap.mkdir(parents=True)
+    (snap / "config.json").write_text("{}")
+    out = main(["prefetch", "--cache-dir", str(tmp_path), "--local-files-only"])
+    assert out["snapshot_path"] == str(snap) and out["revision"] == PINNED_MODEL_REVISION
+    (repo / "refs").mkdir()
+    (repo / "refs" / "v1").write_text(PINNED_MODEL_REVISION)
+    assert main(["prefetch", "--cache-dir", str(tmp_path), "--revision", "v1", "--local-files-only"])[
+        "snapshot_path"] == str(snap)

@@ -36,14 +36,15 @@ from typing import Any, Iterable, Sequence
 
 import numpy as np
 
+from uno_b200.utils.hub import PINNED_MODEL_ID, PINNED_MODEL_REVISION
+
 IGNORE = -100
 CUTOFF = 4096
 ALIGN = 3
 THINK_OPEN, THINK_CLOSE = "<think>\n", "\n</think>\n\n"
 DATASET_ID = "open-thoughts/OpenThoughts3-1.2M"
 DATASET_REVISION = "61bcf9d4eb38b30295efc2021227a63cc5bb34c8"
-MODEL_ID = "s-sahoo/uno-qwen3-8B"
-MODEL_REVISION = "b8a7577b3223bdcf2b3af0f2fc6e95258b3bbc29"
+MODEL_ID, MODEL_REVISION = PINNED_MODEL_ID, PINNED_MODEL_REVISION
 HASH_ALGORITHM = "sha256-rowlen-u64le-input-i32le-label-i32le-v1"
 
 

@@ -65,3 +65,36 @@ def resolve_hf_snapshot(source: str | os.PathLike[str], *, revision: str | None 
                              "directory, the Hugging Face cache or the Hub.") from exc
     raise ValueError(f"Could not resolve {artifact_name} {source!r}{rev_text} from a local directory "
                      "or the local Hugging Face cache.")
+
+
+# The released Uno Qwen3-8B checkpoint that the training recipe starts from
+# (``training/constants.py``, ``training/prefetch_model.py``).
+PINNED_MODEL_ID = "s-sahoo/uno-qwen3-8B"
+PINNED_MODEL_REVISION = "b8a7577b3223bdcf2b3af0f2fc6e95258b3bbc29"
+
+
+def main(argv: list[str] | None = None) -> dict:
+    """``python -m uno_b200.utils.hub prefetch --cache-dir DIR [--model ID] [--revision REV]``:
+    fetch a checkpoint once into a shared cache (a cached copy is reused) and
+    print its snapshot directory, so that later jobs can run offline."""
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("command", choices=("prefetch",))
+    ap.add_argument("--cache-dir", required=True, type=Path)
+    ap.add_argument("--model", default=PINNED_MODEL_ID)
+    ap.add_argument("--revision")
+    ap.add_argument("--local-files-only", action="store_true")
+    args = ap.parse_args(argv)
+    revision = args.revision or (PINNED_MODEL_REVISION if args.model == PINNED_MODEL_ID else None)
+    args.cache_dir.mkdir(parents=True, exist_ok=True)
+    path = resolve_hf_snapshot(args.model, revision=revision, cache_dir=args.cache_dir,
+                               local_files_only=args.local_files_only, artifact_name="model")
+    out = {"model_id": args.model, "revision": revision, "snapshot_path": path}
+    print(json.dumps(out, sort_keys=True))
+    return out
+
+
+if __name__ == "__main__":
+    main()
