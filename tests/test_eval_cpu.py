@@ -412,3 +412,44 @@ def test_suite_launchers_dry_run(tmp_path):
     assert roles == ["jobs", "coord", "worker", "score"]
     assert "--top-p 0.9" in lines[0] and "--num-workers 16" in lines[1] and "--ntasks=16" in lines[2]
     assert not (tmp_path / "results").exists()  # a dry run writes nothing
+
+
+def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
+    """``--judge-base-url`` / ``--judge-model`` reach the grader: an OpenAI-compatible stub judge
+    on 127.0.0.1 sees the benchmark's judge request and its verdict lands in the scores."""
+    from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+
+    from uno_b200.eval.run import main
+
+    seen = []
+
+    class Judge(BaseHTTPRequestHandler):
+        def do_POST(self):  # noqa: N802 - http.server API
+            body = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
+            seen.append((self.path, body["model"], self.headers.get("Authorization")))
+            reply = json.dumps({"choices": [{"message": {"content": "CORRECT"}}]}).encode()
+            self.send_response(200)
+            self.send_header("Content-Type", "application/json")
+            self.send_header("Content-Length", str(len(reply)))
+            self.end_headers()
+            self.wfile.write(reply)
+
+        def log_message(self, *args):
+            pass
+
+    server = ThreadingHTTPServer(("127.0.0.1", 0), Judge)
+    threading.Thread(target=server.serve_forever, daemon=True).start()
+    try:
+        model = _chat_model_dir(tmp_path)
+        data = _dataset(tmp_path)
+        s = main(["--benchmark", "hle", "--model", str(model), "--data", str(data), "--device", "cpu",
+                  "--load-format", "dummy", "--output", str(tmp_path / "hle.jsonl"), "--protocol-arm", "toy",
+                  "--skip-row-count-check", "--num-samples", "1", "--max-tokens", "4", "--max-model-len", "128",
+                  "--diffusion-block-size", "4", "--seed", "0",
+                  "--judge-base-url", f"http://127.0.0.1:{server.server_port}", "--judge-model", "stub-judge",
+                  "--judge-api-key", "k1"])
+    finally:
+        server.shutdown()
+    assert s["scores"]["graded"] == 2 and s["scores"]["accuracy"] == 1.0
+    assert seen and all(p == "/v1/chat/completions" and m == "stub-judge" and a == "Bearer k1"
+                        for p, m, a in seen)

@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import time
 from pathlib import Path
 from typing import Any
@@ -42,8 +43,12 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--data", type=Path)
     p.add_argument("--model", required=True)
     p.add_argument("--tokenizer-path")
+    p.add_argument("--model-revision")
     p.add_argument("--gated-lora-path")
+    p.add_argument("--gated-lora-revision")
     p.add_argument("--gated-lora-subfolder")
+    p.add_argument("--hf-cache-dir")
+    p.add_argument("--hf-local-files-only", action="store_true")
     p.add_argument("--output", type=Path)
     p.add_argument("--summary-output", type=Path)
     p.add_argument("--limit", type=int)
@@ -70,7 +75,11 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--stop-token-ids")
     p.add_argument("--noise-mode", default="random_uniform")
     p.add_argument("--skip-row-count-check", action="store_true")
-    p.add_argument("--no-grade", action="store_true")
+    p.add_argument("--no-grade", "--skip-grading", dest="no_grade", action="store_true")
+    p.add_argument("--judge-model", help="judge model for LLM-graded benchmarks (default: the benchmark's)")
+    p.add_argument("--judge-base-url", default=os.environ.get("UNO_JUDGE_BASE_URL"),
+                   help="OpenAI-compatible endpoint of the judge (env UNO_JUDGE_BASE_URL)")
+    p.add_argument("--judge-api-key", default=os.environ.get("UNO_JUDGE_API_KEY"))
     p.add_argument("--seed", type=int)
     return p
 
@@ -105,8 +114,10 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
     from uno_b200.utils.hub import resolve_hf_snapshot
     from uno_b200.utils.model_tokens import resolve_model_token_ids
 
-    model, adapter = resolve_model_sources(args.model, args.gated_lora_path,
-                                           gated_lora_subfolder=args.gated_lora_subfolder)
+    model, adapter = resolve_model_sources(args.model, args.gated_lora_path, model_revision=args.model_revision,
+                                           gated_lora_subfolder=args.gated_lora_subfolder,
+                                           hf_cache_dir=args.hf_cache_dir,
+                                           hf_local_files_only=args.hf_local_files_only)
     bench = get_benchmark(args.benchmark) if args.benchmark else None
     overrides = resolve_protocol(args, bench)
     chat_kwargs = dict(bench.chat_template_kwargs) if bench else {}
@@ -147,7 +158,8 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
 
         cfg, model_dir = resolve_preset(str(model)[len("preset:"):]), None
     else:
-        model_dir = resolve_hf_snapshot(model, artifact_name="model")
+        model_dir = resolve_hf_snapshot(model, revision=args.model_revision, cache_dir=args.hf_cache_dir,
+                                        local_files_only=args.hf_local_files_only, artifact_name="model")
         cfg = load_model_config(model_dir)
     tokenizer = load_tokenizer(args.tokenizer_path or model_dir, cfg)
     stops = [int(x) for x in args.stop_token_ids.split(",")] if args.stop_token_ids else None
@@ -191,6 +203,8 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
                   max_diffusion_block_size=args.diffusion_block_size,
                   cuda_graph_block_sizes=sorted({1, args.diffusion_block_size}),
                   tree_verify_size=args.tree_verify_size, tree_candidate_top_k=args.tree_candidate_top_k,
+                  gated_lora_revision=args.gated_lora_revision, hf_cache_dir=args.hf_cache_dir,
+                  hf_local_files_only=args.hf_local_files_only,
                   **({"seed": args.seed} if args.seed is not None else {}))
         sp = SamplingParams(temperature=args.temperature, top_p=args.top_p, top_k=args.top_k,
                             max_tokens=max(b for _, b in pending), stop_token_ids=stop_ids, mask_token_id=mask_id,
@@ -223,9 +237,16 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
     if not args.no_grade:
         from uno_b200.eval.score import score_file
 
+        judge = None
+        if args.judge_base_url:
+            from uno_b200.eval.graders import http_chat_transport
+
+            url = args.judge_base_url.rstrip("/")
+            judge = http_chat_transport(url if url.endswith("/v1") else url + "/v1", args.judge_api_key)
         summary["scores"] = score_file(out, benchmark=args.benchmark, data=args.data, parser=args.parser,
                                        grades_out=out.with_name("grades.jsonl"),
-                                       scores_out=out.with_name("scores.json"), summary=summary_path)
+                                       scores_out=out.with_name("scores.json"), summary=summary_path,
+                                       judge=judge, judge_model=args.judge_model)
     return summary
 
 

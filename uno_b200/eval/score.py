@@ -61,7 +61,8 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
 def score_file(generations: str | Path, *, benchmark: str | None = None, data: str | Path | None = None,
                parser: str | None = None, grades_out: str | Path | None = None,
                scores_out: str | Path | None = None, summary: str | Path | None = None,
-               judge: Callable | None = None, task: str | None = None) -> dict[str, Any]:
+               judge: Callable | None = None, task: str | None = None,
+               judge_model: str | None = None) -> dict[str, Any]:
     rows = read_jsonl(generations)
     bench = get_benchmark(benchmark) if benchmark else None
     task = task or (bench.task if bench else "math")
@@ -74,7 +75,8 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
     grades = []
     for row in rows:
         g = grade_row(row, records.get(str(row.get("id"))), task=task, parser=parser, judge=judge,
-                      judge_model=bench.judge if bench else None, timeout=bench.grader_timeout if bench else 10.0)
+                      judge_model=judge_model or (bench.judge if bench else None),
+                      timeout=bench.grader_timeout if bench else 10.0)
         grades.append({"id": row.get("id"), "sample": row.get("sample"), **g})
     graded = [g for g in grades if g["correct"] is not None]
     per_q: dict[str, list[bool]] = {}
