@@ -426,7 +426,7 @@ def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
     class Judge(BaseHTTPRequestHandler):
         def do_POST(self):  # noqa: N802 - http.server API
             body = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
-            seen.append((self.path, body["model"], self.headers.get("Authorization")))
+            seen.append((self.path, body["model"], self.headers.get("Authorization"), body))
             reply = json.dumps({"choices": [{"message": {"content": "CORRECT"}}]}).encode()
             self.send_response(200)
             self.send_header("Content-Type", "application/json")
@@ -447,9 +447,16 @@ def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
                   "--skip-row-count-check", "--num-samples", "1", "--max-tokens", "4", "--max-model-len", "128",
                   "--diffusion-block-size", "4", "--seed", "0",
                   "--judge-base-url", f"http://127.0.0.1:{server.server_port}", "--judge-model", "stub-judge",
-                  "--judge-api-key", "k1"])
+                  "--judge-api-key", "k1", "--judge-temperature", "0.3", "--judge-max-tokens", "77",
+                  "--judge-reasoning-effort", "low", "--judge-max-concurrency", "2", "--save-token-ids",
+                  "--no-progress", "--grades", str(tmp_path / "g.jsonl"), "--scores", str(tmp_path / "s.json")])
     finally:
         server.shutdown()
     assert s["scores"]["graded"] == 2 and s["scores"]["accuracy"] == 1.0
     assert seen and all(p == "/v1/chat/completions" and m == "stub-judge" and a == "Bearer k1"
-                        for p, m, a in seen)
+                        for p, m, a, _ in seen)
+    assert all(b["temperature"] == 0.3 and b["max_tokens"] == 77 and b["reasoning_effort"] == "low"
+               for *_, b in seen)
+    rows = [json.loads(x) for x in (tmp_path / "hle.jsonl").read_text().splitlines()]
+    assert all(len(r["token_ids"]) == r["token_count"] for r in rows)
+    assert (tmp_path / "g.jsonl").is_file() and json.loads((tmp_path / "s.json").read_text())["graded"] == 2

@@ -164,11 +164,22 @@ def http_chat_transport(base_url: str, api_key: str | None = None, timeout: floa
     return send
 
 
+def _judge_payload(model: str, content: str, temperature: float | None, max_tokens: int | None,
+                   reasoning_effort: str | None, default_max_tokens: int) -> dict:
+    payload = {"model": model, "temperature": 0.0 if temperature is None else float(temperature),
+               "max_tokens": default_max_tokens if max_tokens is None else int(max_tokens),
+               "messages": [{"role": "user", "content": content}]}
+    if reasoning_effort:
+        payload["reasoning_effort"] = reasoning_effort
+    return payload
+
+
 def grade_with_judge(question: str, answer: Any, response: str, *, model: str, transport: Callable,
-                     temperature: float = 0.0, max_tokens: int = 4096) -> dict:
-    payload = {"model": model, "temperature": temperature, "max_tokens": max_tokens,
-               "messages": [{"role": "user", "content": JUDGE_TEMPLATE.format(
-                   question=question, answer=answer, response=strip_reasoning(response))}]}
+                     temperature: float | None = None, max_tokens: int | None = None,
+                     reasoning_effort: str | None = None) -> dict:
+    payload = _judge_payload(model, JUDGE_TEMPLATE.format(question=question, answer=answer,
+                                                          response=strip_reasoning(response)),
+                             temperature, max_tokens, reasoning_effort, 4096)
     verdict = transport(payload).strip().upper()
     return {"judge": verdict[:64], "correct": verdict.startswith("CORRECT")}
 
@@ -197,12 +208,13 @@ def lcr_transport_from_env() -> Callable:
 
 
 def grade_lcr(question: str, answer: str, reference: Any, *, transport: Callable | None = None,
-              model: str | None = None) -> dict:
+              model: str | None = None, temperature: float | None = None, max_tokens: int | None = None,
+              reasoning_effort: str | None = None) -> dict:
     transport = transport or lcr_transport_from_env()
     model = model or os.environ.get("UNO_LCR_JUDGE_MODEL", "judge")
-    payload = {"model": model, "temperature": 0, "max_tokens": 32,
-               "messages": [{"role": "user", "content": LCR_TEMPLATE.format(
-                   question=question, answer=strip_reasoning(answer), reference=reference)}]}
+    payload = _judge_payload(model, LCR_TEMPLATE.format(question=question, answer=strip_reasoning(answer),
+                                                        reference=reference),
+                             temperature, max_tokens, reasoning_effort, 32)
     reply = transport(payload)
     m = _LCR_GRADE.search(reply or "")
     return {"judge": (reply or "")[:256], "correct": bool(m) and m.group(1).upper() == "CORRECT"}

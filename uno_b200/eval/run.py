@@ -37,6 +37,10 @@ def completion_budget(prompt_tokens: int, context_length: int, reserve: int, glo
     return max(0, room if global_max is None else min(global_max, room))
 
 
+def _int_list(value: str) -> list[int]:
+    return [int(x) for x in str(value).split(",") if x.strip()]
+
+
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--benchmark")
@@ -50,6 +54,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--hf-cache-dir")
     p.add_argument("--hf-local-files-only", action="store_true")
     p.add_argument("--output", type=Path)
+    p.add_argument("--grades", type=Path, help="grades JSONL (default: grades.jsonl beside --output)")
+    p.add_argument("--scores", type=Path, help="scores JSON (default: scores.json beside --output)")
     p.add_argument("--summary-output", type=Path)
     p.add_argument("--limit", type=int)
     p.add_argument("--num-samples", type=int)
@@ -74,12 +80,30 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--mask-token-id", type=int)
     p.add_argument("--stop-token-ids")
     p.add_argument("--noise-mode", default="random_uniform")
+    p.add_argument("--noise-salt", type=int)
+    p.add_argument("--ignore-eos", action="store_true")
+    p.add_argument("--save-token-ids", action="store_true", help="keep each generation's token ids in its row")
+    p.add_argument("--no-progress", action="store_true")
+    p.add_argument("--gpu-memory-utilization", type=float)
+    p.add_argument("--attention-backend", choices=("fa2", "fa3", "fa4", "native"), default="native",
+                   help="accepted for script compatibility; every value runs this framework's attention kernels")
+    p.add_argument("--cuda-graph-block-sizes", type=_int_list, help="comma-separated forward lengths to capture")
+    p.add_argument("--cuda-graph-batch-sizes", type=_int_list, help="comma-separated batch sizes to capture")
+    p.add_argument("--torch-compile", action="store_true",
+                   help="accepted for script compatibility; this framework runs hand-written kernels and "
+                        "CUDA graphs, so the flag changes nothing")
+    p.add_argument("--grader-timeout", type=float, help="per-test grader time limit (default: the benchmark's)")
+    p.add_argument("--grader-num-processes", type=int, default=1, help="grading threads")
     p.add_argument("--skip-row-count-check", action="store_true")
     p.add_argument("--no-grade", "--skip-grading", dest="no_grade", action="store_true")
     p.add_argument("--judge-model", help="judge model for LLM-graded benchmarks (default: the benchmark's)")
     p.add_argument("--judge-base-url", default=os.environ.get("UNO_JUDGE_BASE_URL"),
                    help="OpenAI-compatible endpoint of the judge (env UNO_JUDGE_BASE_URL)")
     p.add_argument("--judge-api-key", default=os.environ.get("UNO_JUDGE_API_KEY"))
+    p.add_argument("--judge-max-concurrency", type=int, help="concurrent judge requests")
+    p.add_argument("--judge-temperature", type=float)
+    p.add_argument("--judge-max-tokens", type=int)
+    p.add_argument("--judge-reasoning-effort")
     p.add_argument("--seed", type=int)
     return p
 
@@ -201,18 +225,23 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
                   data_parallel_size=args.data_parallel_size, max_num_seqs=args.max_num_seqs,
                   max_model_len=args.max_model_len, max_num_batched_tokens=args.max_num_batched_tokens,
                   max_diffusion_block_size=args.diffusion_block_size,
-                  cuda_graph_block_sizes=sorted({1, args.diffusion_block_size}),
+                  cuda_graph_block_sizes=args.cuda_graph_block_sizes or sorted({1, args.diffusion_block_size}),
+                  attention_backend=args.attention_backend,
+                  **({"cuda_graph_batch_sizes": args.cuda_graph_batch_sizes} if args.cuda_graph_batch_sizes else {}),
                   tree_verify_size=args.tree_verify_size, tree_candidate_top_k=args.tree_candidate_top_k,
                   gated_lora_revision=args.gated_lora_revision, hf_cache_dir=args.hf_cache_dir,
                   hf_local_files_only=args.hf_local_files_only,
+                  **({"gpu_memory_utilization": args.gpu_memory_utilization}
+                     if args.gpu_memory_utilization is not None else {}),
                   **({"seed": args.seed} if args.seed is not None else {}))
         sp = SamplingParams(temperature=args.temperature, top_p=args.top_p, top_k=args.top_k,
                             max_tokens=max(b for _, b in pending), stop_token_ids=stop_ids, mask_token_id=mask_id,
-                            noise_mode=args.noise_mode, diffusion_block_size=args.diffusion_block_size)
+                            noise_mode=args.noise_mode, noise_salt=args.noise_salt, ignore_eos=args.ignore_eos,
+                            diffusion_block_size=args.diffusion_block_size)
         t0 = time.perf_counter()
         try:
             outs = llm.generate([it["prompt_ids"] for it, _ in pending], sp,
-                                request_max_tokens=[b for _, b in pending], use_tqdm=False)
+                                request_max_tokens=[b for _, b in pending], use_tqdm=not args.no_progress)
             elapsed = time.perf_counter() - t0
             stats = dict(getattr(llm, "last_generate_stats", {}))
         finally:
@@ -220,9 +249,12 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
         rows = []
         for (it, budget), o in zip(pending, outs):
             total_tokens += len(o["token_ids"])
-            rows.append({"id": it["id"], "sample": it["sample"], "question": it["prompt"],
-                         "generation": o["text"], "token_count": len(o["token_ids"]), "budget": budget,
-                         "ground_truth": it["ground_truth"], "stats": o.get("stats", {})})
+            row = {"id": it["id"], "sample": it["sample"], "question": it["prompt"],
+                   "generation": o["text"], "token_count": len(o["token_ids"]), "budget": budget,
+                   "ground_truth": it["ground_truth"], "stats": o.get("stats", {})}
+            if args.save_token_ids:
+                row["token_ids"] = list(o["token_ids"])
+            rows.append(row)
         append_jsonl(out, rows)
     forwards = int(stats.get("forwards", 0))
     summary = {"protocol": PROTOCOL_NAME, "protocol_date": PROTOCOL_DATE, "benchmark": bench.name if bench else None,
@@ -243,10 +275,15 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
 
             url = args.judge_base_url.rstrip("/")
             judge = http_chat_transport(url if url.endswith("/v1") else url + "/v1", args.judge_api_key)
+        workers = max(int(args.grader_num_processes or 1), int(args.judge_max_concurrency or 1))
         summary["scores"] = score_file(out, benchmark=args.benchmark, data=args.data, parser=args.parser,
-                                       grades_out=out.with_name("grades.jsonl"),
-                                       scores_out=out.with_name("scores.json"), summary=summary_path,
-                                       judge=judge, judge_model=args.judge_model)
+                                       grades_out=args.grades or out.with_name("grades.jsonl"),
+                                       scores_out=args.scores or out.with_name("scores.json"), summary=summary_path,
+                                       judge=judge, judge_model=args.judge_model, timeout=args.grader_timeout,
+                                       workers=workers,
+                                       judge_options={"temperature": args.judge_temperature,
+                                                      "max_tokens": args.judge_max_tokens,
+                                                      "reasoning_effort": args.judge_reasoning_effort})
     return summary
 
 

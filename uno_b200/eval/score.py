@@ -24,7 +24,10 @@ from uno_b200.eval.parsers import parse_generation
 
 
 def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: Callable | None = None,
-              judge_model: str | None = None, timeout: float = 10.0) -> dict[str, Any]:
+              judge_model: str | None = None, timeout: float = 10.0,
+              judge_options: dict | None = None) -> dict[str, Any]:
+    """Grade of one generation row; ``judge_options`` = temperature / max_tokens / reasoning_effort."""
+    jopts = {k: v for k, v in (judge_options or {}).items() if v is not None}
     gen = row.get("generation", "")
     truth = row.get("ground_truth")
     if task == "ifeval":
@@ -43,7 +46,7 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
         if judge is None:
             return {"correct": None, "status": "ungraded: no judge endpoint"}
         question = row.get("question") or row.get("completion_input") or (record or {}).get("question", "")
-        return grade_lcr(question, gen, truth, transport=judge, model=judge_model)
+        return grade_lcr(question, gen, truth, transport=judge, model=judge_model, **jopts)
     if parser == "mc_answer":
         return grade_multiple_choice(parse_generation("mc_answer", gen), truth)
     if parser == "code_completion" or task in ("humaneval", "mbpp"):
@@ -54,7 +57,7 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
         if judge is None:
             return {"correct": None, "status": "ungraded: no judge endpoint"}
         question = row.get("question") or (record or {}).get("question", "")
-        return grade_with_judge(question, truth, gen, model=judge_model, transport=judge)
+        return grade_with_judge(question, truth, gen, model=judge_model, transport=judge, **jopts)
     return grade_math(gen, truth)
 
 
@@ -62,7 +65,13 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
                parser: str | None = None, grades_out: str | Path | None = None,
                scores_out: str | Path | None = None, summary: str | Path | None = None,
                judge: Callable | None = None, task: str | None = None,
-               judge_model: str | None = None) -> dict[str, Any]:
+               judge_model: str | None = None, timeout: float | None = None, workers: int = 1,
+               judge_options: dict | None = None) -> dict[str, Any]:
+    """Grade a generations file and write ``grades_out`` / ``scores_out``.
+
+    ``timeout`` overrides the benchmark's per-test grader timeout; ``workers``
+    grading threads run at once (code runs in its own sandbox subprocess and
+    judge calls are network-bound, so threads overlap them)."""
     rows = read_jsonl(generations)
     bench = get_benchmark(benchmark) if benchmark else None
     task = task or (bench.task if bench else "math")
@@ -72,12 +81,21 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
         for i, rec in enumerate(read_jsonl(data)):
             rid = first_field(rec, ID_FIELDS)
             records[str(rid if rid is not None else i)] = rec
-    grades = []
-    for row in rows:
+    limit = float(timeout) if timeout is not None else (bench.grader_timeout if bench else 10.0)
+    model = judge_model or (bench.judge if bench else None)
+
+    def one(row):
         g = grade_row(row, records.get(str(row.get("id"))), task=task, parser=parser, judge=judge,
-                      judge_model=judge_model or (bench.judge if bench else None),
-                      timeout=bench.grader_timeout if bench else 10.0)
-        grades.append({"id": row.get("id"), "sample": row.get("sample"), **g})
+                      judge_model=model, timeout=limit, judge_options=judge_options)
+        return {"id": row.get("id"), "sample": row.get("sample"), **g}
+
+    if workers > 1 and len(rows) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(max_workers=int(workers)) as pool:
+            grades = list(pool.map(one, rows))  # results keep the rows' order
+    else:
+        grades = [one(row) for row in rows]
     graded = [g for g in grades if g["correct"] is not None]
     per_q: dict[str, list[bool]] = {}
     for g in graded:
