@@ -460,3 +460,18 @@ def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
     rows = [json.loads(x) for x in (tmp_path / "hle.jsonl").read_text().splitlines()]
     assert all(len(r["token_ids"]) == r["token_count"] for r in rows)
     assert (tmp_path / "g.jsonl").is_file() and json.loads((tmp_path / "s.json").read_text())["graded"] == 2
+
+
+def test_score_cli_grades_a_generations_file(tmp_path):
+    from uno_b200.eval.score import main
+
+    gen = tmp_path / "gens.jsonl"
+    gen.write_text("".join(json.dumps(r) + "\n" for r in (
+        {"id": "a", "sample": 0, "generation": "thus \\boxed{12}", "ground_truth": "12"},
+        {"id": "a", "sample": 1, "generation": "thus \\boxed{13}", "ground_truth": "12"},
+        {"id": "b", "sample": 0, "generation": "\\boxed{\\frac{1}{2}}", "ground_truth": "0.5"})))
+    scores = main(["--generations", str(gen), "--task", "math", "--grader-num-processes", "2",
+                   "--scores", str(tmp_path / "sc.json")])
+    assert scores["rows"] == 3 and abs(scores["accuracy"] - 2 / 3) < 1e-9
+    assert scores["question_accuracy"] == 0.75  # a: 1/2, b: 1/1
+    assert (tmp_path / "grades.jsonl").is_file() and json.loads((tmp_path / "sc.json").read_text())["rows"] == 3

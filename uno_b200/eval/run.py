@@ -267,14 +267,9 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
                "decoder_tokens_per_sequence_forward": int(stats.get("accepts", 0)) / forwards if forwards else 0.0}
     Path(summary_path).write_text(json.dumps(summary, indent=2) + "\n")
     if not args.no_grade:
-        from uno_b200.eval.score import score_file
+        from uno_b200.eval.score import judge_transport, score_file
 
-        judge = None
-        if args.judge_base_url:
-            from uno_b200.eval.graders import http_chat_transport
-
-            url = args.judge_base_url.rstrip("/")
-            judge = http_chat_transport(url if url.endswith("/v1") else url + "/v1", args.judge_api_key)
+        judge = judge_transport(args.judge_base_url, args.judge_api_key)
         workers = max(int(args.grader_num_processes or 1), int(args.judge_max_concurrency or 1))
         summary["scores"] = score_file(out, benchmark=args.benchmark, data=args.data, parser=args.parser,
                                        grades_out=args.grades or out.with_name("grades.jsonl"),

@@ -9,6 +9,9 @@ rows are reported as ungraded); ``ifeval`` uses the instruction checkers of ``ev
 everything else is graded as math (boxed answer equivalence).  Scores are
 the mean correctness over all samples, the per-question mean, and the
 generation throughput (TPS, TPF) copied from the generation summary.
+
+CLI: ``python -m uno_b200.eval.score --generations FILE [--benchmark NAME]
+[--data FILE] [--grades OUT] [--scores OUT] [--judge-base-url URL ...]``.
 """
 
 from __future__ import annotations
@@ -119,3 +122,53 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
     if scores_out is not None:
         Path(scores_out).write_text(json.dumps(scores, indent=2) + "\n")
     return scores
+
+
+def judge_transport(base_url: str | None, api_key: str | None = None) -> Callable | None:
+    """OpenAI-compatible chat transport of a judge endpoint (``/v1`` appended when missing)."""
+    if not base_url:
+        return None
+    from uno_b200.eval.graders import http_chat_transport
+
+    url = base_url.rstrip("/")
+    return http_chat_transport(url if url.endswith("/v1") else url + "/v1", api_key)
+
+
+def main(argv: list[str] | None = None) -> dict[str, Any]:
+    import argparse
+    import os
+
+    ap = argparse.ArgumentParser(description="Grade a generations JSONL file and write its scores.")
+    ap.add_argument("--generations", type=Path, required=True)
+    ap.add_argument("--benchmark")
+    ap.add_argument("--data", type=Path, help="the benchmark's records (code graders need them)")
+    ap.add_argument("--task", help="grading task when no benchmark is named (default: math)")
+    ap.add_argument("--parser")
+    ap.add_argument("--grades", type=Path)
+    ap.add_argument("--scores", type=Path)
+    ap.add_argument("--generation-summary", type=Path, help="copies throughput figures into the scores")
+    ap.add_argument("--timeout", type=float, help="per-test grader time limit")
+    ap.add_argument("--grader-num-processes", type=int, default=1)
+    ap.add_argument("--judge-model")
+    ap.add_argument("--judge-base-url", default=os.environ.get("UNO_JUDGE_BASE_URL"))
+    ap.add_argument("--judge-api-key", default=os.environ.get("UNO_JUDGE_API_KEY"))
+    ap.add_argument("--judge-max-concurrency", type=int)
+    ap.add_argument("--judge-temperature", type=float)
+    ap.add_argument("--judge-max-tokens", type=int)
+    ap.add_argument("--judge-reasoning-effort")
+    args = ap.parse_args(argv)
+    gen = args.generations
+    scores = score_file(gen, benchmark=args.benchmark, data=args.data, parser=args.parser, task=args.task,
+                        grades_out=args.grades or gen.with_name("grades.jsonl"),
+                        scores_out=args.scores or gen.with_name("scores.json"), summary=args.generation_summary,
+                        judge=judge_transport(args.judge_base_url, args.judge_api_key), judge_model=args.judge_model,
+                        timeout=args.timeout,
+                        workers=max(int(args.grader_num_processes or 1), int(args.judge_max_concurrency or 1)),
+                        judge_options={"temperature": args.judge_temperature, "max_tokens": args.judge_max_tokens,
+                                       "reasoning_effort": args.judge_reasoning_effort})
+    print(json.dumps(scores, indent=2))
+    return scores
+
+
+if __name__ == "__main__":
+    main()
