@@ -442,3 +442,31 @@ def test_fixed_curriculum_builder(tmp_path):
     with pytest.raises(FileExistsError):
         write_curriculum(out, fixed_curriculum("3", block_size=16, steps_per_epoch=10, global_batch_size=4,
                                                sequence_length=64))
+
+
+def test_training_cli_accepts_the_reference_option_names(tmp_path):
+    """``training/train.py`` spellings and a DeepSpeed config drive the same trainer."""
+    import json
+
+    from uno_b200.train.__main__ import main
+
+    ds = tmp_path / "zero2.json"
+    ds.write_text(json.dumps({"zero_optimization": {"stage": 2}, "gradient_clipping": 0.5,
+                              "train_micro_batch_size_per_gpu": "auto", "gradient_accumulation_steps": "auto"}))
+    out = tmp_path / "run"
+    hist = main(["--model", "preset:tiny-qwen3", "--output-dir", str(out), "--device", "cpu", "--block-sizes", "4",
+                 "--steps-per-stage", "2", "--seq-len", "32", "--lora-rank", "8", "--learning-rate", "2e-4",
+                 "--per-device-batch-size", "1", "--gradient-accumulation-steps", "2", "--dataset-path", "synthetic",
+                 "--tv-gamma", "1.0", "--kl-beta", "0.5", "--ce-alpha", "0.1", "--run-name", "ref-names",
+                 "--logging-steps", "5", "--deepspeed", str(ds), "--wandb-mode", "offline", "--local_rank", "0"])
+    assert [m["step"] for m in hist] == [1, 2]
+    logged = [json.loads(x) for x in (out / "metrics.jsonl").read_text().splitlines()]
+    assert [m["step"] for m in logged] == [1, 2]
+    manifest = json.loads(next(out.glob("*manifest*.json")).read_text())
+    assert manifest["run_name"] == "ref-names"
+    assert manifest["deepspeed_config"]["applied"] == {"max_grad_norm": 0.5, "zero_stage": 2}
+    obj = manifest["compatibility"]["objective"]
+    assert (obj["tv_weight"], obj["kl_weight"], obj["ce_weight"]) == (1.0, 0.5, 0.1)
+    with pytest.raises(SystemExit, match="dropout"):
+        main(["--model", "preset:tiny-qwen3", "--output-dir", str(tmp_path / "r2"), "--device", "cpu",
+              "--lora-dropout", "0.05"])
