@@ -414,6 +414,14 @@ def test_openthoughts_encoding_budget_alignment_and_hash(tmp_path):
     man = prepare(str(src), tmp_path / "out", Tok())
     assert man["hash"]["row_count"] == 3
     prepare(str(src), tmp_path / "again", Tok(), verify_against=tmp_path / "out")   # same corpus verifies
+    many = tmp_path / "many.jsonl"
+    many.write_text("".join(json.dumps({"conversations": [{"from": "human", "value": f"q{i}" * (i + 1)},
+                                                           {"from": "gpt", "value": f"a{i}"}]}) + "\n"
+                            for i in range(7)))
+    one = prepare(str(many), tmp_path / "p1", Tok())
+    two = prepare(str(many), tmp_path / "p2", Tok(), num_proc=2, writer_batch_size=2)
+    assert one["hash"] == two["hash"] and one["hash"]["row_count"] == 7
+    assert (tmp_path / "p1" / "rows.jsonl").read_text() == (tmp_path / "p2" / "rows.jsonl").read_text()
 
 
 def test_fixed_curriculum_builder(tmp_path):

@@ -117,7 +117,7 @@ def corpus_hash(rows: Iterable[dict[str, Sequence[int]]]) -> dict[str, Any]:
             "token_count": n_tok, "supervised_token_count": n_sup}
 
 
-def _source_rows(source: str, max_samples: int | None) -> Iterable[dict]:
+def _source_rows(source: str, max_samples: int | None, cache_dir: str | None = None) -> Iterable[dict]:
     path = Path(source)
     if path.is_file():
         if path.suffix == ".json":
@@ -128,26 +128,56 @@ def _source_rows(source: str, max_samples: int | None) -> Iterable[dict]:
         from datasets import load_dataset  # network / cache path
 
         rows = load_dataset(source, revision=DATASET_REVISION if source == DATASET_ID else None, split="train",
-                            streaming=max_samples is not None)
+                            streaming=max_samples is not None, cache_dir=cache_dir)
     for i, row in enumerate(rows):
         if max_samples is not None and i >= max_samples:
             break
         yield row
 
 
+_WORKER_TOKENIZER = None
+
+
+def _encode_in_worker(conversations):
+    return encode_conversation(conversations, _WORKER_TOKENIZER)
+
+
+def _encoded_rows(rows: Iterable[dict], tokenizer, num_proc: int) -> Iterable[dict]:
+    """Encoded rows in source order; ``num_proc`` > 1 encodes in forked worker processes."""
+    if num_proc <= 1:
+        for row in rows:
+            yield encode_conversation(row["conversations"], tokenizer)
+        return
+    import multiprocessing as mp
+
+    global _WORKER_TOKENIZER
+    _WORKER_TOKENIZER = tokenizer  # inherited by the forked workers
+    with mp.get_context("fork").Pool(num_proc) as pool:
+        yield from pool.imap(_encode_in_worker, (row["conversations"] for row in rows), chunksize=64)
+
+
 def prepare(source: str, output: Path, tokenizer, *, max_samples: int | None = None,
-            verify_against: Path | None = None) -> dict[str, Any]:
+            verify_against: Path | None = None, num_proc: int = 1, writer_batch_size: int = 1000,
+            cache_dir: str | None = None) -> dict[str, Any]:
+    """Encode ``source`` into ``output/rows.jsonl`` plus its manifest.
+
+    ``num_proc`` encoding processes keep the source order (the hash depends on
+    it); rows are written ``writer_batch_size`` at a time."""
     output = Path(output)
     if output.exists() and (not output.is_dir() or any(output.iterdir())):
         raise FileExistsError(f"output must be an empty directory: {output}")
     output.mkdir(parents=True, exist_ok=True)
     rows_path = output / "rows.jsonl"
     encoded = []
+    pending: list[str] = []
     with rows_path.open("w", encoding="utf-8") as fh:
-        for row in _source_rows(source, max_samples):
-            enc = encode_conversation(row["conversations"], tokenizer)
-            fh.write(json.dumps(enc) + "\n")
+        for enc in _encoded_rows(_source_rows(source, max_samples, cache_dir), tokenizer, num_proc):
+            pending.append(json.dumps(enc) + "\n")
             encoded.append(enc)
+            if len(pending) >= max(1, writer_batch_size):
+                fh.write("".join(pending))
+                pending.clear()
+        fh.write("".join(pending))
     digest = corpus_hash(encoded)
     if verify_against is not None:
         ref = Path(verify_against)
@@ -177,15 +207,22 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--tokenizer", default=MODEL_ID, help="tokenizer directory or hub id")
     ap.add_argument("--max-samples", type=int)
     ap.add_argument("--verify-against", type=Path)
+    ap.add_argument("--cache-dir", help="Hugging Face cache for the dataset and tokenizer")
+    ap.add_argument("--num-proc", type=int, default=1, help="encoding processes (source order is kept)")
+    ap.add_argument("--writer-batch-size", type=int, default=1000)
+    ap.add_argument("--tokenizer-local-files-only", action="store_true")
     args = ap.parse_args(argv)
     from transformers import AutoTokenizer
 
     tok = AutoTokenizer.from_pretrained(args.tokenizer, revision=MODEL_REVISION if args.tokenizer == MODEL_ID else None,
-                                        trust_remote_code=True)
+                                        trust_remote_code=True, cache_dir=args.cache_dir,
+                                        local_files_only=args.tokenizer_local_files_only)
     if tok.pad_token_id is None:
         tok.pad_token = tok.eos_token
     print(json.dumps(prepare(args.source, args.output, tok, max_samples=args.max_samples,
-                             verify_against=args.verify_against), indent=2, sort_keys=True))
+                             verify_against=args.verify_against, num_proc=args.num_proc,
+                             writer_batch_size=args.writer_batch_size, cache_dir=args.cache_dir),
+                     indent=2, sort_keys=True))
 
 
 if __name__ == "__main__":
