@@ -127,8 +127,8 @@ def locate_reference() -> tuple[str | None, str]:
 
     Order: the offline install in ``baseline/_ref``; an importable ``nano_vllm_uno``
     installed elsewhere; a run-time offline install (``pip --no-index --no-deps``)
-    from a reference source tree (``UNO_REF_SOURCE``, else the build machine's
-    checkout) into ``baseline/_ref``.  Returns ``(None, reason)`` when none works.
+    from the reference source tree named by ``UNO_REF_SOURCE`` into
+    ``baseline/_ref``.  Returns ``(None, reason)`` when none works.
     """
     if os.path.isdir(os.path.join(REF, "nano_vllm_uno")):
         return REF, "baseline/_ref"
@@ -137,7 +137,7 @@ def locate_reference() -> tuple[str | None, str]:
     spec = importlib.util.find_spec("nano_vllm_uno")
     if spec is not None and spec.origin:
         return os.path.dirname(os.path.dirname(spec.origin)), "importable nano_vllm_uno"
-    sources = [s for s in (os.environ.get("UNO_REF_SOURCE"), "/root/reference") if s]
+    sources = [s for s in (os.environ.get("UNO_REF_SOURCE"),) if s]
     for src in sources:
         if not os.path.isfile(os.path.join(src, "pyproject.toml")):
             continue
