@@ -190,7 +190,7 @@ def run_worker(address: tuple[str, int], authkey: bytes, manifest: dict,
 
 def build_jobs(benchmarks: list[str], tokenizer, *, data_root: str | Path | None = None,
                num_samples: int | None = None, limit: int | None = None, context_length: int | None = None,
-               max_tokens: int | None = None, reserve: int = 16) -> tuple[list[dict], list[dict]]:
+               max_tokens: int | None = None, reserve: int = 8) -> tuple[list[dict], list[dict]]:
     """Jobs of a suite run and the benchmark entries of its manifest.
 
     Per benchmark: its records (the registry's pinned file, or the file of the
@@ -198,8 +198,8 @@ def build_jobs(benchmarks: list[str], tokenizer, *, data_root: str | Path | None
     template, instruction, chat-template kwargs), ``num_samples`` samples of
     each record (the benchmark's own count by default), and each job's
     completion budget -- the context length less the prompt and ``reserve``
-    tokens of decoding slack, capped by the output limit -- as ``eval.run``
-    computes it.  Records whose prompt leaves no budget get no job.
+    slots of the largest decode forward (the diffusion block), capped by the
+    output limit -- as ``eval.run`` computes it.  Records whose prompt leaves no budget get no job.
     """
     from uno_b200.eval.benchmarks import get_benchmark
     from uno_b200.eval.data import ANSWER_FIELDS, ID_FIELDS, first_field, load_records, \
@@ -329,7 +329,7 @@ def main(argv=None):
         tokenizer = load_tokenizer(args.tokenizer_path or model_dir, load_model_config(model_dir))
         jobs, entries = build_jobs(args.benchmark, tokenizer, data_root=args.data_root, num_samples=args.num_samples,
                                    limit=args.limit, context_length=args.context_length, max_tokens=args.max_tokens,
-                                   reserve=max(16, args.diffusion_block_size))
+                                   reserve=args.diffusion_block_size)  # the largest decode forward's slots
         manifest = {"model": args.model, "gated_lora_path": adapter, "diffusion_block_size": args.diffusion_block_size,
                     "benchmarks": entries,
                     "sampling": suite_sampling(entries, {"temperature": args.temperature, "top_p": args.top_p,
