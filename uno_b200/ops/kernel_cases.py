@@ -11,7 +11,8 @@ lm_head weight (1.24 GB) and the decode-attention KV cache (~240 MB) exceed it
 alone, and the sampling case alternates two 156 MB logit blocks.
 
 Cases: ``layer-gemms`` (gate_up + SiLU, qkv, o_proj, down, LoRA hidden),
-``lm-head``, ``decode-attention``, ``sampling`` (full-vocab verify and one
+``lm-head``, ``decode-attention`` (and ``decode-attention-vs-fa2``, the same inputs through the
+reference's FlashAttention-2 call), ``sampling`` (full-vocab verify and one
 vocab-parallel shard), ``filtered`` (top-k / top-p sampling and verify, with
 the eager torch nucleus for comparison), ``train-attention`` (block-diffusion
 forward / backward).  A case entry marked ``eager`` (a path with host syncs,
@@ -148,9 +149,8 @@ def _filtered():
     }
 
 
-def _decode_attention():
+def _decode_attention_inputs():
     from uno_b200.layers.meta import ForwardMeta, Mode, causal_suffix_masks
-    from uno_b200.ops import cuda as C
 
     g = torch.Generator().manual_seed(0)
     B, Q, hq, hkv, page = 64, 8, 32, 8, 256
@@ -169,8 +169,45 @@ def _decode_attention():
                        prefix_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"),
                        suffix_mask=causal_suffix_masks(Q, "cuda").repeat(B, 1), seqlen_q=Q, max_kv=3328)
     kv_bytes = sum(n + Q for n in lens) * hkv * 128 * 2 * 2
+    return B, Q, lens, q, kc, vc, tables, meta, kv_bytes
+
+
+def _decode_attention():
+    from uno_b200.ops import cuda as C
+
+    B, Q, lens, q, kc, vc, _, meta, kv_bytes = _decode_attention_inputs()
     return {f"decode_attention B={B} Q={Q} mean_kv={sum(lens) // B}":
             (lambda i: C.attention(q, kc, vc, meta, 128 ** -0.5), 0, kv_bytes)}
+
+
+def _decode_attention_vs_fa2():
+    """The same decode step through this framework's kernel and through the reference's call,
+    ``flash_attn_with_kvcache`` (FlashAttention 2, ``nano_vllm_uno/layers/attention.py:654-668``),
+    on identical inputs: the paged cache re-laid out as [pages, page, kv heads, dim] for FA2, whose
+    bottom-right causal alignment over ``cache_seqlens = prefix + Q`` is the Q-row causal block mask.
+    The largest output difference is printed before the timings."""
+    import json
+
+    from flash_attn import flash_attn_with_kvcache
+
+    from uno_b200.ops import cuda as C
+
+    B, Q, lens, q, kc, vc, tables, meta, kv_bytes = _decode_attention_inputs()
+    k_fa, v_fa = kc.permute(0, 2, 1, 3).contiguous(), vc.permute(0, 2, 1, 3).contiguous()
+    seqlens = torch.tensor([n + Q for n in lens], dtype=torch.int32, device="cuda")
+    table = tables.cuda()
+    qb = q.view(B, Q, q.shape[1], q.shape[2])
+
+    def fa2(i):
+        return flash_attn_with_kvcache(qb, k_fa, v_fa, cache_seqlens=seqlens, block_table=table,
+                                       softmax_scale=128 ** -0.5, causal=True)
+
+    ours = C.attention(q, kc, vc, meta, 128 ** -0.5).float()
+    ref = fa2(0).reshape(B * Q, q.shape[1], q.shape[2]).float()
+    print(json.dumps({"max_abs_diff_vs_fa2": float((ours - ref).abs().max())}))
+    return {f"decode_attention (this framework) B={B} Q={Q}": (lambda i: C.attention(q, kc, vc, meta, 128 ** -0.5),
+                                                               0, kv_bytes),
+            f"flash_attn_with_kvcache (FA2, the reference's call) B={B} Q={Q}": (fa2, 0, kv_bytes)}
 
 
 def _train_attention():
@@ -213,6 +250,7 @@ def _train_attention():
 
 
 CASES = {"layer-gemms": _layer_gemms, "lm-head": _lm_head, "decode-attention": _decode_attention,
+         "decode-attention-vs-fa2": _decode_attention_vs_fa2,
          "sampling": _sampling, "filtered": _filtered, "train-attention": _train_attention}
 
 
