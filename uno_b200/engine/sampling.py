@@ -70,7 +70,7 @@ def native_filtered(logits: torch.Tensor) -> bool:
     """bf16 logits rows the filtered kernels can read in place."""
     if not logits.is_cuda or logits.dtype != torch.bfloat16 or logits.dim() not in (2, 3):
         return False
-    if logits.stride(-1) != 1 or logits.shape[-1] % 8 or logits.data_ptr() % 16:
+    if logits.stride(-1) != 1 or logits.shape[-1] % 8 or logits.shape[-1] >= 1 << 18 or logits.data_ptr() % 16:
         return False
     return all(st % 8 == 0 for st in logits.stride()[:-1])
 

@@ -55,7 +55,7 @@ typedef unsigned long long u64;
 struct FiltSmem {
   u64 cand[CAND];
   uint32_t hcnt[NB];
-  uint32_t hm[3][NB];  // mass limbs: bits 0-13, 14-27, 28-41 of the 2^-40 fixed-point weights
+  uint32_t hm[3][NB];  // mass limbs: bits 0-13, 14-27, 28-40 of the 2^-40 fixed-point weights
   u64 wsum[32];
   uint32_t wcnt[32];
   u64 ctot_w;
@@ -643,7 +643,8 @@ void filtered_sample_launch(const at::Tensor& x, double inv_temp, int64_t k, dou
   check_dev(params, "params");
   int rows, V;
   RowMap m = row_map(x, rows, V);  // bf16, unit stride, strides % 8, 16-byte aligned
-  TORCH_CHECK(V % 8 == 0, "filtered_sample: the vocabulary must be a multiple of 8");
+  TORCH_CHECK(V % 8 == 0 && V < (1 << 18), "filtered_sample: the vocabulary must be a multiple of 8 below 2^18 "
+              "(the 14-bit mass limbs of a bin sum without carries up to 2^18 tokens)");
   TORCH_CHECK(k >= 0 && k < V, "top_k must be in [0, V)");
   TORCH_CHECK(top_p > 0.0 && top_p <= 1.0, "top_p must be in (0, 1]");
   TORCH_CHECK(k > 0 || top_p < 1.0, "filtered_sample needs top_k or top_p");
@@ -672,7 +673,7 @@ void filtered_verify_launch(const at::Tensor& clean, const at::Tensor& draft, co
   RowMap cm = row_map(clean, rows, V);
   RowMap dm = row_map(draft, rows2, V2);
   TORCH_CHECK(rows == rows2 && V == V2 && spec.numel() == rows, "filtered_verify shapes");
-  TORCH_CHECK(V % 8 == 0, "filtered_verify: the vocabulary must be a multiple of 8");
+  TORCH_CHECK(V % 8 == 0 && V < (1 << 18), "filtered_verify: the vocabulary must be a multiple of 8 below 2^18");
   TORCH_CHECK(k >= 0 && k < V && top_p > 0.0 && top_p <= 1.0 && (k > 0 || top_p < 1.0),
               "filtered_verify needs top_k in (0, V) or top_p in (0, 1)");
   TORCH_CHECK(dparams.scalar_type() == at::kLong && dparams.is_contiguous() && dparams.numel() == 2 * (int64_t)rows,
