@@ -132,3 +132,16 @@ def test_engine_psi_spec_matches_ar_in_law():
         assert stat < chi2_threshold(len(bins)), (stat, len(bins))
     # Psi-Spec must actually accept drafts (TPF > AR's 1 token per forward)
     assert llm.last_generate_stats  # populated
+
+
+def test_cpu_filtered_ranking_keeps_lowest_ids_on_ties():
+    """The sparse CPU path ranks equal logits lowest id first, as the CUDA filtered kernels do."""
+    from uno_b200.engine.sampling import sparse_top_k, sparse_top_p
+
+    logits = torch.zeros(1, 64)
+    logits[0, 40] = 3.0
+    ids, probs = sparse_top_k(logits, 1.0, 5, None)
+    assert ids[0].tolist() == [40, 0, 1, 2, 3]
+    ids, probs = sparse_top_p(logits, 1.0, 0.5)
+    kept = ids[0][probs[0] > 0].tolist()
+    assert kept[0] == 40 and kept[1:] == list(range(len(kept) - 1))

@@ -233,6 +233,15 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     return logits.argmax(dim=-1)
 
 
+def ranked_top(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The ``k`` largest logits per row with their ids, value descending.  On the CPU equal
+    values keep the lowest id first (a stable sort), the ranking of the CUDA filtered kernels."""
+    if logits.is_cuda:
+        return torch.topk(logits, k=int(k), dim=-1, sorted=True)
+    values, ids = torch.sort(logits, dim=-1, descending=True, stable=True)
+    return values[..., : int(k)], ids[..., : int(k)]
+
+
 def sparse_top_k(logits: torch.Tensor, temperature: float, k: int, top_p: float | None):
     if (logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and int(k) <= 32
             and logits.is_contiguous()):
@@ -245,7 +254,7 @@ def sparse_top_k(logits: torch.Tensor, temperature: float, k: int, top_p: float 
         ext().topk_lse(logits, int(k), 1.0 / float(temperature), ids, lp)
         probs = torch.softmax(lp, dim=-1)  # renormalised over the k candidates
     else:
-        values, ids = torch.topk(logits, k=int(k), dim=-1)
+        values, ids = ranked_top(logits, int(k))
         probs = torch.softmax(values.float() / float(temperature), dim=-1)
     if top_p is not None and float(top_p) < 1.0:
         cdf = probs.cumsum(dim=-1)
@@ -260,8 +269,9 @@ def sparse_top_p(logits: torch.Tensor, temperature: float, top_p: float, initial
     V = logits.shape[-1]
     log_z = torch.logsumexp(logits.float() / float(temperature), dim=-1, keepdim=True)
     k = min(int(initial_k), V)
+    ranked = None if logits.is_cuda else ranked_top(logits, V)  # CPU: one stable sort serves every k
     while True:
-        values, ids = torch.topk(logits, k=k, dim=-1, sorted=True)
+        values, ids = ranked_top(logits, k) if ranked is None else (ranked[0][..., :k], ranked[1][..., :k])
         probs = torch.exp(values.float() / float(temperature) - log_z)
         if k == V or bool((probs.sum(dim=-1) >= float(top_p)).all()):
             break
