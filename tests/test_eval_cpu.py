@@ -475,3 +475,33 @@ def test_score_cli_grades_a_generations_file(tmp_path):
     assert scores["rows"] == 3 and abs(scores["accuracy"] - 2 / 3) < 1e-9
     assert scores["question_accuracy"] == 0.75  # a: 1/2, b: 1/1
     assert (tmp_path / "grades.jsonl").is_file() and json.loads((tmp_path / "sc.json").read_text())["rows"] == 3
+
+
+def test_reference_parser_names():
+    from uno_b200.eval.parsers import parse_generation
+
+    assert parse_generation("gpqa_answer", "<think>A or B or C?</think>\nThe answer is **(C)**") == "C"
+    assert parse_generation("gpqa_answer", "ANSWER: b") == "B"
+    assert parse_generation("gpqa_answer", "so \\boxed{D}") == "D"
+    assert parse_generation("gpqa_answer", "I pick **B**") == "B"
+    assert parse_generation("gpqa_answer", "no letter here") == "?" and parse_generation("gpqa_answer", "") == "?"
+    assert parse_generation("mmlu_pro_answer", "The answer is (J).") == "J"
+    assert parse_generation("mmlu_pro_answer", "reasoning\nE.\n") == "E"
+    assert parse_generation("mmlu_pro_answer", "Answer: (G)") == "G"
+    chan = ("<|channel|>analysis<|message|>thinking<|channel|>final<|message|>"
+            "```python\ndef f(x):\n    return x\nprint(f(2))\n```<|end|>")
+    assert parse_generation("lcb_code", chan) == "def f(x):\n    return x"
+    assert parse_generation("lcb_code", "import sys\n\ndef main():\n    pass\n\nmain()\nprose") == \
+        "import sys\n\ndef main():\n    pass"
+    assert parse_generation("lcb_code", "just words") is None
+    assert parse_generation("identity", " x ") == " x " and parse_generation("noop", None) is None
+    assert parse_generation("multiple_choice_answer", "The answer is B") == "B"
+    assert parse_generation("humaneval", "```python\nx = 1\n```") == "x = 1"
+
+
+def test_choice_parser_routes_to_multiple_choice_grading():
+    from uno_b200.eval.score import grade_row
+
+    row = {"generation": "<think>hmm</think> ANSWER: C", "ground_truth": "C"}
+    assert grade_row(row, None, task="gpqa_diamond", parser="gpqa_answer")["correct"] is True
+    assert grade_row({**row, "ground_truth": "A"}, None, task="gpqa_diamond", parser="gpqa_answer")["correct"] is False

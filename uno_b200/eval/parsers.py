@@ -6,7 +6,19 @@
   standalone letter of the final lines;
 * ``code_completion``: the last fenced code block (``python`` blocks first),
   else the text after a reasoning block;
-* ``passthrough``: the generation after any ``</think>`` marker.
+* ``passthrough``: the generation after any ``</think>`` marker;
+* ``noop`` / ``identity``: the generation unchanged;
+* ``gpqa_answer`` / ``mmlu_pro_answer``: the terminal option letter (A-D /
+  A-J) of a reasoning response, ``"?"`` when it names none;
+* ``lcb_code``: LiveCodeBench program extraction -- the final-channel
+  message of a channelled response, special tokens removed, the last fenced
+  Python block that defines something (or the last block), reduced to its
+  top-level definitions and imports;
+* ``humaneval`` and ``multiple_choice_answer`` are other names of
+  ``code_completion`` and ``mc_answer``.
+The extraction rules of the choice and LiveCodeBench parsers, and the order in
+which they are tried, are those of the reference protocol: they decide what is
+graded.
 """
 
 from __future__ import annotations
@@ -83,12 +95,127 @@ def extract_code(text: str | None) -> str | None:
     return body or None
 
 
+# ------------------------------------------------------- terminal choices
+def _final_part(text: str) -> str:
+    """The answer part of a reasoning response: after the first ``</think>``, else its last 500 characters."""
+    return text.split(_THINK_END, 1)[1].lstrip() if _THINK_END in text else text[-500:]
+
+
+def _choice_rules(hi: str, strict: bool) -> list[tuple[re.Pattern, int]]:
+    """``(pattern, mode)`` rules for option letters A..hi, in the order they are tried; mode 0 takes
+    the first match, 1 a closing mark at the very end, 2 the last letter standing alone on a line."""
+    opt = f"[A-{hi}a-{hi.lower()}]"
+    tail = re.compile(rf"(?:\*\*\(?({opt})\)?\*\*|\(({opt})\))\s*[.\s]*$")
+    boxed = re.compile(rf"\\boxed\{{[^}}]*?({opt})[^A-{hi}a-{hi.lower()}}}]*\}}")
+    if strict:  # four options: an explicit ANSWER line, "answer is X" / "answer: X", boxed, a closing mark
+        return [(re.compile(rf"ANSWER:\s*({opt})"), 0),
+                (re.compile(rf"[Aa]nswer\s*(?:is\s*:?\s*|:\s*)\*{{0,2}}\s*\(?({opt})\)?\*{{0,2}}"), 0),
+                (boxed, 0), (tail, 1)]
+    return [(re.compile(rf"[Aa]nswer is:?\s*\*{{0,2}}\(?({opt})\)?\*{{0,2}}"), 0), (boxed, 0), (tail, 1),
+            (re.compile(rf"(?:^|\n)\s*\(?({opt})[.)]\s*$", re.MULTILINE), 2),
+            (re.compile(rf"[Aa]nswer:?\s*\(?({opt})\)?"), 0)]
+
+
+def _pick_choice(text: str | None, rules) -> str:
+    if not text:
+        return "?"
+    part = _final_part(text)
+    for pattern, mode in rules:
+        if mode == 1:  # the closing mark must end the answer
+            m = pattern.search(part.strip())
+            if m:
+                return (m.group(1) or m.group(2)).upper()
+        elif mode == 2:  # the last option standing alone on a line
+            hits = pattern.findall(part)
+            if hits:
+                return hits[-1].upper()
+        else:
+            m = pattern.search(part)
+            if m:
+                return m.group(1).upper()
+    return "?"
+
+
+_GPQA_RULES = _choice_rules("D", strict=True)
+_MMLU_PRO_RULES = _choice_rules("J", strict=False)
+
+
+def parse_gpqa_answer(text: str | None) -> str:
+    return _pick_choice(text, _GPQA_RULES)
+
+
+def parse_mmlu_pro_answer(text: str | None) -> str:
+    return _pick_choice(text, _MMLU_PRO_RULES)
+
+
+# ---------------------------------------------------- LiveCodeBench code
+_CHANNEL = re.compile(r"<\|channel\|>\s*(?P<name>[^<\n]+)\s*<\|message\|>(?P<body>.*?)(?=(?:<\|channel\|>|<\|end\|>|$))",
+                      re.IGNORECASE | re.DOTALL)
+_SPECIAL = re.compile(r"<\|[^|]+(?:\|[^|]+)*\|>")
+_PY_BLOCK = re.compile(r"```(?:python3?|py)?\s*\n(.*?)```", re.IGNORECASE | re.DOTALL)
+_TOP_DEF = re.compile(r"^(def |async def |class |import |from \S+ import )")
+_TOP_IMPORT = re.compile(r"^(import |from \S+ import )")
+_DEFINES = re.compile(r"^(def |async def |class )", re.MULTILINE)
+_HAS_CODE = re.compile(r"^(def |async def |class |import |from \S+ import )", re.MULTILINE)
+
+
+def top_level_code(code: str) -> str:
+    """Top-level definitions with their bodies and the import lines; drops
+    example calls and prose around them (the code itself when nothing qualifies)."""
+    kept: list[str] = []
+    inside = False
+    for line in code.split("\n"):
+        bare = line.lstrip()
+        indented = line[:1].isspace()
+        if not indented and _TOP_DEF.match(bare):
+            inside = True
+            kept.append(line)
+        elif inside:
+            if not bare or indented:
+                kept.append(line)
+            else:
+                inside = False  # a top-level statement ends the definition and is dropped
+        elif not bare:
+            if kept:
+                kept.append(line)
+        elif _TOP_IMPORT.match(bare):
+            kept.append(line)
+    while kept and not kept[-1].strip():
+        kept.pop()
+    return "\n".join(kept) if kept else code
+
+
+def parse_lcb_code(text: str | None) -> str | None:
+    if text is None:
+        return None
+    segments = list(_CHANNEL.finditer(text))
+    if segments:
+        final = [m for m in segments if m.group("name").strip().lower() in ("final", "answer")]
+        text = (final or segments)[-1].group("body")
+    text = _SPECIAL.sub("", text).strip()
+    blocks = _PY_BLOCK.findall(text)
+    if blocks:
+        defining = [b for b in blocks if _DEFINES.search(b)]
+        return top_level_code((defining or blocks)[-1])
+    candidate = top_level_code(text)
+    return candidate if _HAS_CODE.search(candidate) else None
+
+
 PARSERS = {
     "passthrough": strip_reasoning,
+    "noop": lambda text: text,
+    "identity": lambda text: text,
     "boxed": last_boxed,
     "mc_answer": extract_mc_answer,
+    "multiple_choice_answer": extract_mc_answer,
+    "gpqa_answer": parse_gpqa_answer,
+    "mmlu_pro_answer": parse_mmlu_pro_answer,
     "code_completion": extract_code,
+    "humaneval": extract_code,
+    "lcb_code": parse_lcb_code,
 }
+CHOICE_PARSERS = frozenset({"mc_answer", "multiple_choice_answer", "gpqa_answer", "mmlu_pro_answer"})
+CODE_PARSERS = frozenset({"code_completion", "humaneval", "lcb_code"})
 
 
 def parse_generation(parser: str, text: str | None):

@@ -23,7 +23,7 @@ from typing import Any, Callable
 from uno_b200.eval.benchmarks import get_benchmark
 from uno_b200.eval.data import first_field, read_jsonl, ID_FIELDS
 from uno_b200.eval.graders import grade_code, grade_math, grade_multiple_choice, grade_with_judge
-from uno_b200.eval.parsers import parse_generation
+from uno_b200.eval.parsers import CHOICE_PARSERS, CODE_PARSERS, parse_generation
 
 
 def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: Callable | None = None,
@@ -50,12 +50,13 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
             return {"correct": None, "status": "ungraded: no judge endpoint"}
         question = row.get("question") or row.get("completion_input") or (record or {}).get("question", "")
         return grade_lcr(question, gen, truth, transport=judge, model=judge_model, **jopts)
-    if parser == "mc_answer":
-        return grade_multiple_choice(parse_generation("mc_answer", gen), truth)
-    if parser == "code_completion" or task in ("humaneval", "mbpp"):
+    if parser in CHOICE_PARSERS:
+        return grade_multiple_choice(parse_generation(parser, gen), truth)
+    if parser in CODE_PARSERS or task in ("humaneval", "mbpp"):
         if record is None:
             return {"correct": None, "status": "missing source record"}
-        return grade_code(parse_generation("code_completion", gen), record, timeout)
+        code_parser = parser if parser in CODE_PARSERS else "code_completion"
+        return grade_code(parse_generation(code_parser, gen) or "", record, timeout)
     if judge_model is not None:
         if judge is None:
             return {"correct": None, "status": "ungraded: no judge endpoint"}
