@@ -478,3 +478,18 @@ def test_training_cli_accepts_the_reference_option_names(tmp_path):
     with pytest.raises(SystemExit, match="dropout"):
         main(["--model", "preset:tiny-qwen3", "--output-dir", str(tmp_path / "r2"), "--device", "cpu",
               "--lora-dropout", "0.05"])
+
+
+def test_released_curriculum_schedule(tmp_path):
+    """Six half-epoch stages over three epochs: 28,125 steps, 14.7456 B tokens, 4,688 / 4,687 alternating."""
+    from uno_b200.train.curriculum import BlockCurriculumPlan, released_curriculum
+    from uno_b200.train.make_curriculum import main as make_curriculum
+
+    plan = BlockCurriculumPlan.from_mapping(released_curriculum())
+    assert plan.max_steps == 28125 and plan.total_tokens == 14_745_600_000
+    assert [s.block_size for s in plan.stages] == [2, 4, 6, 8, 12, 16]
+    assert [s.end_step - s.start_step for s in plan.stages] == [4688, 4687] * 3
+    assert plan.stage_for_step(4687).block_size == 2 and plan.stage_for_step(4688).block_size == 4
+    out = make_curriculum(["released", "--output", str(tmp_path / "released.yaml")])
+    assert out["max_steps"] == 28125 and BlockCurriculumPlan.from_yaml(tmp_path / "released.yaml").sha256() == \
+        plan.sha256()

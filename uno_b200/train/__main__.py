@@ -31,7 +31,7 @@ def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--model", required=True)
     p.add_argument("--output-dir", required=True)
-    p.add_argument("--curriculum")
+    p.add_argument("--curriculum", help="curriculum YAML, or 'released' for the released run's schedule")
     p.add_argument("--block-sizes", default="4,8,16")
     p.add_argument("--steps-per-stage", type=int, default=1)
     p.add_argument("--seq-len", type=int, default=128)
@@ -154,7 +154,11 @@ def main(argv: list[str] | None = None) -> list[dict]:
     if mask_id is None:
         raise SystemExit("the model config has no mask_token_id; pass --mask-token-id")
 
-    if args.curriculum:
+    if args.curriculum == "released":  # the released run's six-stage schedule
+        from uno_b200.train.curriculum import released_curriculum
+
+        plan = BlockCurriculumPlan.from_mapping(released_curriculum())
+    elif args.curriculum:
         plan = BlockCurriculumPlan.from_yaml(args.curriculum)
     else:
         global_batch = args.global_batch

@@ -181,3 +181,31 @@ def write_curriculum(path: str | Path, mapping: dict[str, Any]) -> Path:
     tmp.write_text(text)
     tmp.replace(path)
     return path
+
+
+RELEASED_BLOCK_SIZES = (2, 4, 6, 8, 12, 16)
+
+
+def released_curriculum(epochs: int = 3, block_sizes=RELEASED_BLOCK_SIZES) -> dict[str, Any]:
+    """The block-size schedule of the released Uno Qwen3-8B run as a curriculum mapping.
+
+    ``epochs`` passes over the recipe corpus (9,375 steps each) split into
+    ``len(block_sizes)`` stages of equal length in increasing block size: with
+    the defaults, six half-epoch stages that alternate 4,688 and 4,687 steps,
+    so every adjacent pair is exactly one epoch (28,125 steps, 14.7456 B
+    tokens in all).  Stage lengths are the cumulative split points rounded
+    half up (``training/configs/uno_3epoch_curriculum.yaml``).
+    """
+    from decimal import ROUND_HALF_UP, Decimal
+
+    total_steps = int(epochs) * RECIPE_STEPS_PER_EPOCH
+    n = len(block_sizes)
+    tps = RECIPE_SEQUENCE_LENGTH * RECIPE_GLOBAL_BATCH
+    ends = [int((Decimal(total_steps) * (i + 1) / n).to_integral_value(rounding=ROUND_HALF_UP)) for i in range(n)]
+    stages, prev = [], 0
+    for b, end in zip(block_sizes, ends):
+        stages.append({"block_size": int(b), "tokens": (end - prev) * tps})
+        prev = end
+    return {"version": 1, "tokens_per_step": tps, "sequence_length": RECIPE_SEQUENCE_LENGTH,
+            "global_batch_size": RECIPE_GLOBAL_BATCH, "total_tokens": total_steps * tps, "seed": RECIPE_SEED,
+            "stages": stages}

@@ -6,8 +6,9 @@
 # framework's trainer (`python -m uno_b200.train`, FSDP base weights + ZeRO-2
 # LoRA optimizer state).
 #
-# FIXED_BLOCK_SIZE=B (with EPOCHS, default 1) trains at one block size through a
-# generated one-stage curriculum instead of CURRICULUM.
+# CURRICULUM defaults to the released run's schedule (block sizes 2-16 over
+# three epochs); FIXED_BLOCK_SIZE=B (with EPOCHS, default 1) instead trains at
+# one block size through a generated one-stage curriculum.
 #
 # Required: MODEL (checkpoint dir or preset:NAME), DATA (prepared rows.jsonl
 # directory or "synthetic"), OUTPUT_ROOT (shared storage).  Optional knobs
@@ -32,7 +33,7 @@ TV_WEIGHT="${TV_WEIGHT:-1.0}"
 KL_WEIGHT="${KL_WEIGHT:-0.0}"
 CE_WEIGHT="${CE_WEIGHT:-0.0}"
 CE_TARGET="${CE_TARGET:-teacher}"
-CURRICULUM="${CURRICULUM:-}"
+CURRICULUM="${CURRICULUM:-released}"   # the released run's six-stage schedule, or a YAML path
 RUN_NAME="${RUN_NAME:-uno-$(date -u +%Y%m%dT%H%M%SZ)}"
 : "${MODEL:?set MODEL to a checkpoint directory or preset:NAME}"
 : "${DATA:?set DATA to a prepared corpus directory or synthetic}"
@@ -45,7 +46,7 @@ if (( GLOBAL_BATCH % per_step != 0 )); then
 fi
 OUTPUT_DIR="${OUTPUT_DIR:-${OUTPUT_ROOT}/runs/${RUN_NAME}}"
 LOG_DIR="${LOG_DIR:-${OUTPUT_ROOT}/logs/${RUN_NAME}}"
-if [[ -z "${CURRICULUM}" && -n "${FIXED_BLOCK_SIZE:-}" && "${UNO_NODE_WORKER:-0}" != "1" ]]; then
+if [[ -n "${FIXED_BLOCK_SIZE:-}" && "${UNO_NODE_WORKER:-0}" != "1" ]]; then
   # one block size for EPOCHS passes (python -m uno_b200.train.make_curriculum)
   CURRICULUM="${OUTPUT_DIR}/curriculum-b${FIXED_BLOCK_SIZE}.yaml"
   (cd "${REPO_ROOT}" && "${PYTHON_BIN}" -m uno_b200.train.make_curriculum fixed --output "${CURRICULUM}" \
