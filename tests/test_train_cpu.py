@@ -493,3 +493,16 @@ def test_released_curriculum_schedule(tmp_path):
     out = make_curriculum(["released", "--output", str(tmp_path / "released.yaml")])
     assert out["max_steps"] == 28125 and BlockCurriculumPlan.from_yaml(tmp_path / "released.yaml").sha256() == \
         plan.sha256()
+
+
+def test_learning_rate_schedules():
+    import pytest
+
+    from uno_b200.train.trainer import lr_at
+
+    # warmup from zero, then constant (the released recipe's warmup-stable schedule without decay)
+    assert [lr_at(s, 1.0, 4, 100) for s in range(6)] == [0.0, 0.25, 0.5, 0.75, 1.0, 1.0]
+    assert lr_at(99, 1.0, 4, 100) == 1.0
+    assert lr_at(4, 1.0, 4, 100, "cosine") == 1.0 and lr_at(100, 1.0, 4, 100, "cosine") == pytest.approx(0.0)
+    with pytest.raises(ValueError):
+        lr_at(10, 1.0, 4, 100, "linear")

@@ -43,6 +43,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--prompt-len", type=int, default=0)
     p.add_argument("--lr", "--learning-rate", dest="lr", type=float, default=1e-4)
     p.add_argument("--warmup-steps", type=int, default=0)
+    p.add_argument("--lr-schedule", choices=("constant", "cosine"), default="constant",
+                   help="after the warmup: constant (the released recipe) or cosine decay to 0")
     p.add_argument("--weight-decay", type=float, default=0.0)
     p.add_argument("--max-grad-norm", type=float, default=None, help="gradient-norm clip (default 1.0)")
     p.add_argument("--lora-rank", type=int, default=64)
@@ -186,13 +188,14 @@ def main(argv: list[str] | None = None) -> list[dict]:
         data_info = data_manifest([args.data])
     compat = {"model": args.model, "curriculum_sha256": plan.sha256(), "lora": vars(settings) | {"alpha": settings.resolved_alpha},
               "objective": vars(objective), "mask_token_id": int(mask_id), "data": data_info,
-              "micro_batch": args.micro_batch, "world_size": world}
+              "micro_batch": args.micro_batch, "world_size": world, "lr_schedule": args.lr_schedule}
     out = args.output_dir
     os.makedirs(out, exist_ok=True)
     trainer = UnoTrainer(model, lora, objective=objective, curriculum=plan, mask_token_id=mask_id, lr=args.lr,
                          warmup_steps=args.warmup_steps, weight_decay=args.weight_decay,
                          max_grad_norm=args.max_grad_norm, output_dir=out, checkpoint_layers=args.checkpoint_layers,
-                         seed=args.seed, process_group=group, base_model_name=args.model, fsdp=args.fsdp)
+                         seed=args.seed, process_group=group, base_model_name=args.model, fsdp=args.fsdp,
+                         lr_schedule=args.lr_schedule)
     if args.resume:
         validate_resume_manifest(out, compat)
         trainer.resume(args.resume)

@@ -11,8 +11,9 @@ decoder:
    loss = ``ce_weight*CE + kl_weight*KL + tv_weight*TV`` per supervised token
    (:func:`uno_b200.train.losses.fused_head_loss`);
 4. LoRA gradients are averaged over data-parallel ranks, clipped to
-   ``max_grad_norm`` and applied with AdamW under a linear-warmup / cosine
-   schedule -- ZeRO-2 style (each rank keeps the moments of one shard), on
+   ``max_grad_norm`` and applied with AdamW -- linear warmup from zero, then
+   the constant learning rate of the released recipe (a warmup-stable schedule
+   without decay steps), or a cosine decay (``lr_schedule="cosine"``) -- ZeRO-2 style (each rank keeps the moments of one shard), on
    CUDA as one fused reduce-scatter + clip + AdamW + all-gather kernel
    (:class:`uno_b200.train.optim.ShardedLoraAdamW`).
 
@@ -42,9 +43,19 @@ from uno_b200.train.losses import fused_head_loss
 from uno_b200.train.optim import ShardedLoraAdamW
 
 
-def lr_at(step: int, base_lr: float, warmup: int, total: int) -> float:
+def lr_at(step: int, base_lr: float, warmup: int, total: int, schedule: str = "constant") -> float:
+    """Learning rate of optimizer step ``step`` (0-based).
+
+    ``constant``: ``base * step / warmup`` during the warmup, then ``base``
+    (``training/train.py:282-284``: warmup-stable-decay with no decay steps).
+    ``cosine``: the same warmup, then a half cosine from ``base`` to 0 at ``total``.
+    """
     if warmup > 0 and step < warmup:
-        return base_lr * (step + 1) / warmup
+        return base_lr * step / warmup
+    if schedule == "constant":
+        return base_lr
+    if schedule != "cosine":
+        raise ValueError(f"unknown learning-rate schedule {schedule!r}")
     span = max(1, total - warmup)
     frac = min(1.0, max(0.0, (step - warmup) / span))
     return base_lr * 0.5 * (1.0 + math.cos(math.pi * frac))
@@ -56,7 +67,7 @@ class UnoTrainer:
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, output_dir: str | None = None,
                  checkpoint_layers: bool = False, seed: int = 0, process_group=None,
                  base_model_name: str | None = None, loss_chunk: int = 1024, native_gemms: bool = True,
-                 fsdp: bool = False):
+                 fsdp: bool = False, lr_schedule: str = "constant"):
         objective.validate()
         self.model = model
         self.lora = lora
@@ -65,6 +76,9 @@ class UnoTrainer:
         self.mask_token_id = int(mask_token_id)
         self.base_lr = float(lr)
         self.warmup = int(warmup_steps)
+        if lr_schedule not in ("constant", "cosine"):
+            raise ValueError(f"unknown learning-rate schedule {lr_schedule!r}")
+        self.lr_schedule = lr_schedule
         self.max_grad_norm = float(max_grad_norm)
         self.output_dir = Path(output_dir) if output_dir else None
         self.checkpoint_layers = bool(checkpoint_layers)
@@ -145,7 +159,7 @@ class UnoTrainer:
             total += float(loss.detach()) / len(micro_batches)
             tokens += info["tokens"]
             noised += info["noised"]
-        lr = lr_at(self.step, self.base_lr, self.warmup, self.curriculum.max_steps)
+        lr = lr_at(self.step, self.base_lr, self.warmup, self.curriculum.max_steps, self.lr_schedule)
         self.optimizer.set_lr(lr)
         on_gpu = self.device.type == "cuda"
         if on_gpu:  # the optimizer step holds the exposed communication: gradient reduce-scatter + all-gather
