@@ -295,12 +295,13 @@ def test_lcr_grader_parses_json_grade():
 
     def judge(payload):
         seen.append(payload)
-        return 'Reasoning... {"GRADE": "CORRECT"}' if "Paris" in payload["messages"][0]["content"] else "{}"
+        text = " ".join(m["content"] for m in payload["messages"])
+        return 'Reasoning... {"GRADE": "CORRECT"}' if "Paris" in text.split("STUDENT ANSWER:")[-1] else "{}"
 
     assert grade_lcr("Capital of France?", "<think>hmm</think>Paris", "Paris", transport=judge, model="m")["correct"]
     assert not grade_lcr("Capital of France?", "Lyon", "Lyon is wrong", transport=lambda p: "INCORRECT",
                          model="m")["correct"]
-    assert seen[0]["model"] == "m" and seen[0]["temperature"] == 0
+    assert seen[0]["model"] == "m" and seen[0]["messages"][0]["role"] == "system"
 
 
 def test_prepare_installs_pinned_artifact_and_rejects_mismatch(tmp_path, monkeypatch):
@@ -427,7 +428,8 @@ def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
         def do_POST(self):  # noqa: N802 - http.server API
             body = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
             seen.append((self.path, body["model"], self.headers.get("Authorization"), body))
-            reply = json.dumps({"choices": [{"message": {"content": "CORRECT"}}]}).encode()
+            reply = json.dumps({"choices": [{"message": {"content": "extracted_final_answer: 5\ncorrect: yes"}}]}
+                               ).encode()
             self.send_response(200)
             self.send_header("Content-Type", "application/json")
             self.send_header("Content-Length", str(len(reply)))
@@ -505,3 +507,41 @@ def test_choice_parser_routes_to_multiple_choice_grading():
     row = {"generation": "<think>hmm</think> ANSWER: C", "ground_truth": "C"}
     assert grade_row(row, None, task="gpqa_diamond", parser="gpqa_answer")["correct"] is True
     assert grade_row({**row, "ground_truth": "A"}, None, task="gpqa_diamond", parser="gpqa_answer")["correct"] is False
+
+
+def test_judge_protocols_hle_omniscience_lcr(tmp_path):
+    """Per-benchmark judge prompts and verdicts; HLE letter questions skip the judge; the
+    AA-Omniscience scores are its accuracy, non-hallucination rate and index over 600 questions."""
+    from uno_b200.eval.graders import judge_messages, parse_verdict
+    from uno_b200.eval.score import score_file
+
+    assert parse_verdict("hle", "<think>x</think>extracted_final_answer: 7\ncorrect: yes\nconfidence: 90") == 1
+    assert parse_verdict("hle", "correct: no") == 0
+    assert [parse_verdict("aa_omniscience", r) for r in ("A", "B", "C", "D", "")] == [1, -1, 0, 0, 0]
+    assert parse_verdict("aa_lcr", '{"answer": {"GRADE": "correct"}}') == 1 and parse_verdict("aa_lcr", "INCORRECT") == 0
+    msgs = judge_messages("aa_lcr", "docs...\n=== QUESTION ===\nWho?\n\nAnswer:", "Ann", "Ann")
+    assert msgs[0]["role"] == "system" and "QUESTION: Who?\n" in msgs[1]["content"]
+    assert "[correct_answer]: 42" in judge_messages("hle", "q", 42, "r")[0]["content"]
+
+    data = tmp_path / "omni.jsonl"
+    data.write_text("".join(json.dumps({"id": f"o{i}", "completion_input": f"question {i}", "ground_truth": "x"}) + "\n"
+                            for i in range(4)))
+    gens = tmp_path / "gens.jsonl"
+    gens.write_text("".join(json.dumps({"id": f"o{i}", "sample": 0, "generation": f"g{i}", "ground_truth": "x"}) + "\n"
+                            for i in range(4)))
+    verdicts = {"question 0": "A", "question 1": "B", "question 2": "C", "question 3": "A"}
+
+    def judge(payload):
+        text = payload["messages"][-1]["content"]
+        return next(v for q, v in verdicts.items() if f"Question: {q}\n" in text)
+
+    scores = score_file(gens, benchmark="omniscience", data=data, judge=judge, judge_model="j")
+    assert scores["num_correct"] == 2 and scores["num_incorrect"] == 1
+    assert scores["omniscience_index"] == (2 - 1) / 600 and scores["non_hallucination_rate"] == 1 - 1 / 600
+
+    hle = tmp_path / "hle.jsonl"
+    hle.write_text(json.dumps({"id": "h", "completion_input": "pick", "ground_truth": "C",
+                               "answer_type": "multipleChoice"}) + "\n")
+    hg = tmp_path / "hg.jsonl"
+    hg.write_text(json.dumps({"id": "h", "sample": 0, "generation": "The answer is C", "ground_truth": "C"}) + "\n")
+    assert score_file(hg, benchmark="hle", data=hle, judge=None)["accuracy"] == 1.0  # graded without a judge

@@ -17,6 +17,7 @@ Behaviour of ``evaluation/graders/*.py``:
 
 from __future__ import annotations
 
+import json
 import os
 import re
 import subprocess
@@ -184,17 +185,96 @@ def grade_with_judge(question: str, answer: Any, response: str, *, model: str, t
     return {"judge": verdict[:64], "correct": verdict.startswith("CORRECT")}
 
 
-# ------------------------------------------------------------------ AA-LCR
-# Behaviour of ``evaluation/graders/lcr.py``: a judge model sees the question,
-# the candidate answer and the reference answer and must reply with a JSON
-# grade; anything without a parsable ``"GRADE"`` counts as incorrect.  The
-# endpoint and model come from UNO_LCR_JUDGE_URL / UNO_LCR_JUDGE_MODEL (key:
-# UNO_LCR_JUDGE_API_KEY); a base URL without ``/v1`` gets it appended.
-LCR_TEMPLATE = ("Decide whether the candidate answer to the question below is semantically correct, using the "
-                "reference answer as ground truth. Respond with only {{\"GRADE\":\"CORRECT\"}} or "
-                "{{\"GRADE\":\"INCORRECT\"}}.\n\nQuestion:\n{question}\n\nCandidate answer:\n{answer}\n\n"
-                "Reference answer:\n{reference}")
-_LCR_GRADE = re.compile(r'"GRADE"\s*:\s*"(CORRECT|INCORRECT)"', re.IGNORECASE)
+# ------------------------------------------------------- judge protocols
+# The LLM-graded benchmarks (AA-LCR, HLE, AA-Omniscience) are graded by a
+# judge model with fixed prompts and verdict formats; the prompt texts below
+# are those benchmarks' grading protocol (as the reference evaluation sends
+# them), because a different prompt changes the grades.  The judge reads only
+# the visible answer, after the last reasoning block.  Verdicts: AA-LCR a JSON
+# {"GRADE": ...} (or a bare CORRECT / INCORRECT); HLE a "correct: yes|no"
+# line; AA-Omniscience one letter, A correct (+1), B incorrect (-1), C partial
+# and D not attempted (0).  LCR endpoints come from UNO_LCR_JUDGE_URL /
+# UNO_LCR_JUDGE_MODEL (key: UNO_LCR_JUDGE_API_KEY) when none is passed.
+LCR_SYSTEM = "You are a teacher grading a quiz, and output JSON."
+LCR_PROMPT = ("You are a teacher grading a quiz.\nYou are given a question, the student's answer, and the true "
+              "answer, and are asked to score the student answer as either CORRECT or INCORRECT.\n\nExample "
+              "Format:\nQUESTION: {query}\nSTUDENT ANSWER: {result}\nTRUE ANSWER: {answer}\n\nOutput:\n"
+              "{{\"GRADE\": \"CORRECT\" or \"INCORRECT\"}}")
+HLE_PROMPT = (
+    "Judge whether the following [response] to [question] is correct or not based on the precise and "
+    "unambiguous [correct_answer] below.\n\n[question]: {question}\n\n[response]: {response}\n\nYour judgement "
+    "must be in the format and criteria specified below:\n\nextracted_final_answer: The final exact answer "
+    "extracted from the [response]. Put the extracted answer as 'None' if there is no exact, final answer to "
+    "extract from the response.\n\n[correct_answer]: {correct_answer}\n\nreasoning: Explain why the "
+    "extracted_final_answer is correct or incorrect based on [correct_answer], focusing only on if there are "
+    "meaningful differences between [correct_answer] and the extracted_final_answer. Do not comment on any "
+    "background to the problem, do not attempt to solve the problem, do not argue for any answer different than "
+    "[correct_answer], focus only on whether the answers match.\n\ncorrect: Answer 'yes' if "
+    "extracted_final_answer matches the [correct_answer] given above, or is within a small margin of error for "
+    "numerical problems. Answer 'no' otherwise, i.e. if there if there is any inconsistency, ambiguity, "
+    "non-equivalency, or if the extracted answer is incorrect.\n\nconfidence: The extracted confidence score "
+    "between 0% and 100% from [response]. Put 100 if there is no confidence score available.")
+OMNISCIENCE_PROMPT = (
+    "Your job is to look at a question, a gold target, and a predicted answer, and then assign a grade of either "
+    "[\"CORRECT\", \"INCORRECT\", \"PARTIAL_ANSWER\", \"NOT_ATTEMPTED\"].\n\nCORRECT: The answer fully matches or "
+    "is equivalent to the gold target\nINCORRECT: The answer contradicts or differs in meaning from the gold "
+    "target\nPARTIAL_ANSWER: The answer is accurate and nearly complete but not at the correct level of detail\n"
+    "NOT_ATTEMPTED: Used only when the model refuses, omits, or explicitly states it does not know the answer, or "
+    "needs more context or tools to answer the question\n\nHere is a new example.\n\nQuestion: {question}\n"
+    "Gold target: {target}\nPredicted answer: {predicted_answer}\n\nGrade the predicted answer of this new "
+    "question as one of:\nA: CORRECT\nB: INCORRECT\nC: PARTIAL_ANSWER\nD: NOT_ATTEMPTED\n\nJust return the "
+    "letters \"A\", \"B\", \"C\", or \"D\", with no text around it.")
+JUDGED_TASKS = ("aa_lcr", "hle", "aa_omniscience")
+OMNISCIENCE_DENOMINATOR = 600  # the benchmark's question count: scores are per question of the full set
+_THINK_CLOSE = re.compile(r"</(?:ifm\|)?think[^>]*>", re.IGNORECASE)
+
+
+def visible_answer(text: str | None) -> str:
+    """The text after the last reasoning block."""
+    value = text or ""
+    closes = list(_THINK_CLOSE.finditer(value))
+    return value[closes[-1].end():].strip() if closes else value.strip()
+
+
+def judge_messages(task: str, question: str, answer: Any, response: str) -> list[dict]:
+    response = response or "No answer"
+    if task == "aa_lcr":
+        q = question.split("\n=== QUESTION ===\n")[-1]
+        if q.endswith("\n\nAnswer:"):
+            q = q[: -len("\n\nAnswer:")]
+        return [{"role": "system", "content": LCR_SYSTEM},
+                {"role": "user", "content": LCR_PROMPT.format(query=q.strip(), result=response, answer=answer)}]
+    if task == "hle":
+        return [{"role": "user", "content": HLE_PROMPT.format(question=question, response=response,
+                                                              correct_answer=answer)}]
+    if task == "aa_omniscience":
+        return [{"role": "user", "content": OMNISCIENCE_PROMPT.format(question=question, target=answer,
+                                                                      predicted_answer=response)}]
+    raise ValueError(f"no judge protocol for task {task!r}")
+
+
+def parse_verdict(task: str, reply: str | None) -> int:
+    """+1 correct, -1 incorrect (AA-Omniscience only), 0 otherwise."""
+    text = visible_answer(reply)
+    if task == "hle":
+        m = re.search(r'"?correct"?\s*:\s*"?(yes|no)"?', text, re.IGNORECASE)
+        return int(bool(m) and m.group(1).lower() == "yes")
+    if task == "aa_omniscience":
+        m = re.search(r"\b([ABCD])\b", text.upper())
+        return {"A": 1, "B": -1}.get(m.group(1), 0) if m else 0
+    braces = re.search(r"\{.*\}", text, re.DOTALL)
+    if braces:
+        try:
+            obj = json.loads(braces.group(0))
+            grade = obj.get("GRADE", obj.get("grade"))
+            if isinstance(obj.get("answer"), dict):
+                grade = obj["answer"].get("GRADE", obj["answer"].get("grade", grade))
+            if isinstance(grade, str):
+                return int(grade.upper() == "CORRECT")
+        except ValueError:
+            pass
+    m = re.search(r"\b(CORRECT|INCORRECT)\b", text, re.IGNORECASE)
+    return int(bool(m) and m.group(1).upper() == "CORRECT")
 
 
 def lcr_transport_from_env() -> Callable:
@@ -207,14 +287,29 @@ def lcr_transport_from_env() -> Callable:
     return http_chat_transport(url, os.environ.get("UNO_LCR_JUDGE_API_KEY"))
 
 
+def grade_judged(task: str, question: str, response: str, answer: Any, *, transport: Callable, model: str,
+                 temperature: float | None = None, max_tokens: int | None = None,
+                 reasoning_effort: str | None = None) -> dict:
+    """One judge call under the task's protocol: ``{"grade", "correct", "judge"}``."""
+    payload = {"model": model, "messages": judge_messages(task, question, answer, response)}
+    if temperature is not None:
+        payload["temperature"] = float(temperature)
+    if max_tokens is not None:
+        payload["max_tokens"] = int(max_tokens)
+    if reasoning_effort:
+        payload["reasoning_effort"] = reasoning_effort
+    try:
+        reply = transport(payload)
+    except Exception as exc:  # a failed judge call grades 0, as the protocol does
+        return {"grade": 0, "correct": False, "judge_error": str(exc)[:256]}
+    grade = parse_verdict(task, reply)
+    return {"grade": grade, "correct": grade == 1, "judge": (reply or "")[:256]}
+
+
 def grade_lcr(question: str, answer: str, reference: Any, *, transport: Callable | None = None,
               model: str | None = None, temperature: float | None = None, max_tokens: int | None = None,
               reasoning_effort: str | None = None) -> dict:
-    transport = transport or lcr_transport_from_env()
-    model = model or os.environ.get("UNO_LCR_JUDGE_MODEL", "judge")
-    payload = _judge_payload(model, LCR_TEMPLATE.format(question=question, answer=strip_reasoning(answer),
-                                                        reference=reference),
-                             temperature, max_tokens, reasoning_effort, 32)
-    reply = transport(payload)
-    m = _LCR_GRADE.search(reply or "")
-    return {"judge": (reply or "")[:256], "correct": bool(m) and m.group(1).upper() == "CORRECT"}
+    """AA-LCR grade (``grade_judged`` with the endpoint from the environment when none is given)."""
+    return grade_judged("aa_lcr", question, answer, reference, transport=transport or lcr_transport_from_env(),
+                        model=model or os.environ.get("UNO_LCR_JUDGE_MODEL", "judge"), temperature=temperature,
+                        max_tokens=max_tokens, reasoning_effort=reasoning_effort)

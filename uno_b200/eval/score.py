@@ -22,7 +22,8 @@ from typing import Any, Callable
 
 from uno_b200.eval.benchmarks import get_benchmark
 from uno_b200.eval.data import first_field, read_jsonl, ID_FIELDS
-from uno_b200.eval.graders import grade_code, grade_math, grade_multiple_choice, grade_with_judge
+from uno_b200.eval.graders import JUDGED_TASKS, OMNISCIENCE_DENOMINATOR, grade_code, grade_judged, grade_math, \
+    grade_multiple_choice, grade_with_judge
 from uno_b200.eval.parsers import CHOICE_PARSERS, CODE_PARSERS, parse_generation
 
 
@@ -43,13 +44,18 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
 
         codes = run_generation(extract_python_code(gen), parse_tests(truth), int(timeout))
         return {"correct": generation_passed(codes), "test_results": codes}
-    if task == "aa_lcr":
-        from uno_b200.eval.graders import grade_lcr
+    if task in JUDGED_TASKS:
+        rec = record or {}
+        if task == "hle" and rec.get("answer_type") == "multipleChoice":  # letter answers need no judge
+            from uno_b200.eval.parsers import extract_mc_answer
 
+            gold = str(truth).strip()[:1].upper() if truth else None
+            pick = extract_mc_answer(gen)
+            return {"prediction": pick, "correct": pick is not None and pick == gold}
         if judge is None:
             return {"correct": None, "status": "ungraded: no judge endpoint"}
-        question = row.get("question") or row.get("completion_input") or (record or {}).get("question", "")
-        return grade_lcr(question, gen, truth, transport=judge, model=judge_model, **jopts)
+        question = str(rec.get("completion_input") or rec.get("problem") or row.get("question") or "")
+        return grade_judged(task, question, gen, truth, transport=judge, model=judge_model or "judge", **jopts)
     if parser in CHOICE_PARSERS:
         return grade_multiple_choice(parse_generation(parser, gen), truth)
     if parser in CODE_PARSERS or task in ("humaneval", "mbpp"):
@@ -111,6 +117,13 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
         "accuracy": sum(bool(g["correct"]) for g in graded) / len(graded) if graded else None,
         "question_accuracy": (sum(sum(v) / len(v) for v in per_q.values()) / len(per_q)) if per_q else None,
     }
+    if task == "aa_omniscience":  # the benchmark's own metrics, over its full question count
+        right = sum(1 for g in grades if g.get("grade") == 1)
+        wrong = sum(1 for g in grades if g.get("grade") == -1)
+        scores.update({"denominator": OMNISCIENCE_DENOMINATOR, "num_correct": right, "num_incorrect": wrong,
+                       "accuracy": right / OMNISCIENCE_DENOMINATOR,
+                       "non_hallucination_rate": 1.0 - wrong / OMNISCIENCE_DENOMINATOR,
+                       "omniscience_index": (right - wrong) / OMNISCIENCE_DENOMINATOR})
     if summary is not None and Path(summary).is_file():
         s = json.loads(Path(summary).read_text())
         for key in ("output_tokens_per_second", "decoder_tokens_per_sequence_forward", "total_output_tokens"):
