@@ -545,3 +545,17 @@ def test_judge_protocols_hle_omniscience_lcr(tmp_path):
     hg = tmp_path / "hg.jsonl"
     hg.write_text(json.dumps({"id": "h", "sample": 0, "generation": "The answer is C", "ground_truth": "C"}) + "\n")
     assert score_file(hg, benchmark="hle", data=hle, judge=None)["accuracy"] == 1.0  # graded without a judge
+
+
+def test_protocol_math_grading():
+    from uno_b200.eval import math_grading
+    from uno_b200.eval.graders import grade_math
+
+    if not math_grading.available():
+        pytest.skip("math_verify is not installed")
+    for gen, truth, ok in (("so \\boxed{12}", "12", True), ("thus \\boxed{\\frac{1}{2}}", "0.5", True),
+                           ("\\boxed{\\dfrac{3}{4}}", "\\frac{3}{4}", True), ("The answer is 42.", "42", True),
+                           ("#### 1,234", "1234", True), ("<think>\\boxed{9}</think> so 9", "9", True),
+                           ("\\boxed{5 cm}", "5", True), ("\\boxed{13}", "12", False), ("The answer is 7", "8", False)):
+        assert grade_math(gen, truth)["correct"] is ok, (gen, truth)
+    assert math_grading.normalise_answer("\\left( 1{,}000 \\right)") == "(1000)"

@@ -81,6 +81,13 @@ def math_equal(pred: str | None, truth: str | None, tol: float = 1e-6) -> bool:
 
 
 def grade_math(generation: str, ground_truth: Any) -> dict:
+    """Math grading of the evaluation protocol (:mod:`uno_b200.eval.math_grading`, on
+    ``math_verify``); without that package, the last boxed answer after the
+    reasoning (else the last line) compared with sympy."""
+    from uno_b200.eval import math_grading
+
+    if math_grading.available():
+        return math_grading.grade(generation, ground_truth)
     body = strip_reasoning(generation)
     pred = last_boxed(body)
     if pred is None:
