@@ -23,7 +23,10 @@ def test_parsers():
     assert parsers.last_boxed(r"so \boxed{\frac{1}{2}} then \boxed{x^{2}+1}") == "x^{2}+1"
     assert parsers.last_boxed("no box") is None
     assert parsers.extract_mc_answer("<think>maybe A</think>The answer is (C).") == "C"
-    assert parsers.extract_mc_answer(r"... \boxed{\text{B}}") == "B"
+    assert parsers.extract_mc_answer(r"... \boxed{B}") == "B"
+    assert parsers.extract_mc_answer(r"... \boxed{\text{B}}") is None  # the protocol reads bare boxed letters only
+    assert parsers.extract_mc_answer("<answer>(2)</answer>") == "B" and parsers.extract_mc_answer("Final answer: **E**") == "E"
+    assert parsers.extract_mc_answer("<think>x</think>\nB. because") == "B"
     assert parsers.extract_mc_answer("Reasoning...\nD") == "D"
     code = "text\n```python\ndef f(x):\n    return x + 1\n```\nmore"
     assert parsers.extract_code(code) == "def f(x):\n    return x + 1"

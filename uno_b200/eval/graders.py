@@ -98,8 +98,12 @@ def grade_math(generation: str, ground_truth: Any) -> dict:
 
 # ------------------------------------------------------------ multiple choice
 def grade_multiple_choice(prediction: str | None, ground_truth: Any) -> dict:
-    truth = str(ground_truth).strip().upper()
-    return {"prediction": prediction, "correct": prediction is not None and prediction.strip().upper() == truth}
+    """The predicted option against the reference's first character (digits 1-5 read as A-E)."""
+    from uno_b200.eval.parsers import normalise_choice
+
+    truth = normalise_choice(str(ground_truth)[:1]) if ground_truth is not None else None
+    return {"prediction": prediction,
+            "correct": prediction is not None and truth is not None and prediction.strip().upper() == truth}
 
 
 # ------------------------------------------------------------------- code

@@ -1,9 +1,8 @@
 """Answer extraction from generations (``evaluation/parsers.py`` behaviour).
 
 * ``boxed``: content of the last ``\\boxed{...}`` (balanced braces);
-* ``mc_answer``: the chosen option letter (A-J), preferring an explicit
-  "answer is X" / "Answer: X" statement, then a boxed letter, then the last
-  standalone letter of the final lines;
+* ``mc_answer``: the chosen option (A-E, digits 1-5 read as A-E) by the
+  protocol's ordered line and tail rules (``extract_mc_answer``);
 * ``code_completion``: the last fenced code block (``python`` blocks first),
   else the text after a reasoning block;
 * ``passthrough``: the generation after any ``</think>`` marker;
@@ -55,31 +54,87 @@ def last_boxed(text: str | None) -> str | None:
     return None
 
 
-_MC_STRONG = [re.compile(p, re.IGNORECASE) for p in (
-    r"answer\s*(?:is|:)?\s*[\(\[]?\s*\**\s*([A-J])\b",
-    r"\bchoice\s*(?:is|:)\s*[\(\[]?([A-J])\b",
-    r"\boption\s*(?:is|:)?\s*[\(\[]?([A-J])\b",
+# Multiple-choice answers (A-E, or 1-5 read as A-E), in the protocol's order:
+# the first line after the reasoning (answer tags, a boxed letter, or a whole
+# line that states the answer), then the last lines from the bottom up (also
+# statements inside a sentence), then a choice leading a line after the
+# reasoning, then the last tag or statement in the final 4,096 characters.
+_EMPH = r"(?:\*\*|__|`)?"
+_CHOICE = r"([A-E1-5])"
+_ANSWER_WORDS = rf"(?:final[.:]?\s*)?answer\b\s*[:：-]?\s*(?:is\s*)?{_EMPH}\s*(?:option\s*)?[\(\[]?\s*{_CHOICE}"
+_CHOICE_WORDS = rf"(?:the\s+)?choice\s+is\s+{_EMPH}\s*(?:option\s*)?[\(\[]?\s*{_CHOICE}"
+_LINE_END = rf"\s*[\)\]]?\s*{_EMPH}\s*(?:[.!?])?\s*$"
+_MC_TAGS = [re.compile(p, re.IGNORECASE) for p in (
+    rf"<(?:final\s*)?answer>\s*[\(\[]?\s*{_CHOICE}\s*[\)\]]?\s*</(?:final\s*)?answer>",
+    rf"<answer>\s*[\(\[]?\s*{_CHOICE}\s*[\)\]]?\s*</answer>",
+    rf"\\(?:boxed|fbox)\s*\{{\s*{_CHOICE}\s*\}}",
 )]
-_MC_WEAK = re.compile(r"(?:^|[\s\(\[\*])([A-J])(?:[\)\]\.\*:]|\s*$)")
+_MC_LINE = [re.compile(p, re.IGNORECASE) for p in (
+    rf"^\s*{_ANSWER_WORDS}{_LINE_END}",
+    rf"^\s*{_CHOICE_WORDS}{_LINE_END}",
+    rf"^\s*{_EMPH}\s*[\(\[]?\s*{_CHOICE}{_LINE_END}",
+)]
+_MC_INLINE = [re.compile(p, re.IGNORECASE) for p in (
+    rf"\b{_ANSWER_WORDS}\s*[\)\]]?\s*{_EMPH}",
+    rf"\b{_CHOICE_WORDS}\s*[\)\]]?\s*{_EMPH}",
+    rf"\b(?:option|choice)\s*{_EMPH}\s*[\(\[]?\s*{_CHOICE}\s*[\)\]]?\s*{_EMPH}\s+"
+    r"(?:is|would\s+be|remains?|works?|fits?|correct|best|right|compatible|consistent|larger)\b",
+)]
+_MC_LEADING = re.compile(rf"^\s*(?:final\s+(?:answer|choice)\s*[:=-]?\s*)?(?:option\s*)?[\(\[]?\s*{_CHOICE}"
+                         r"(?=[\s\)\].,:;!\-]|$)", re.IGNORECASE)
+_CHAT_END = re.compile(r"(?:<\|(?:ifm\|)?im_end\|>|<\|endoftext\|>)\s*$", re.IGNORECASE)
+_REASONING_END = re.compile(r"</(?:ifm\|)?think[^>]*>", re.IGNORECASE)
+_MC_LINES, _MC_TAIL = 96, 4096
+
+
+def normalise_choice(value: str | None) -> str | None:
+    """Upper-case letter; the digits 1-5 stand for A-E."""
+    if value is None:
+        return None
+    v = value.strip().upper()
+    return "ABCDE"[int(v) - 1] if v in {"1", "2", "3", "4", "5"} else (v or None)
+
+
+def _line_choice(line: str, inline: bool) -> str | None:
+    for pattern in _MC_TAGS + _MC_LINE + (_MC_INLINE if inline else []):
+        m = pattern.search(line)
+        if m:
+            return normalise_choice(m.group(1))
+    return None
 
 
 def extract_mc_answer(text: str | None) -> str | None:
-    body = strip_reasoning(text)
-    if not body:
+    if text is None:
         return None
-    boxed = last_boxed(body)
-    if boxed:
-        m = re.search(r"\b([A-J])\b", boxed.replace("\\text{", " ").replace("}", " "))
-        if m:
-            return m.group(1).upper()
-    for pat in _MC_STRONG:
-        hits = pat.findall(body)
+    text = _CHAT_END.sub("", text).strip()
+    if not text:
+        return None
+    closes = list(_REASONING_END.finditer(text))
+    body = (text[closes[-1].end():].strip() or text) if closes else text
+    lines = [ln.strip() for ln in body.splitlines() if ln.strip()]
+    last_lines = lines[-_MC_LINES:]
+    if lines:
+        got = _line_choice(lines[0], inline=False)
+        if got is not None:
+            return got
+        if closes:
+            m = _MC_LEADING.match(lines[0])
+            if m:
+                return normalise_choice(m.group(1))
+    for line in reversed(last_lines):
+        got = _line_choice(line, inline=True)
+        if got is not None:
+            return got
+    if closes:
+        for line in reversed(last_lines):
+            m = _MC_LEADING.match(line)
+            if m:
+                return normalise_choice(m.group(1))
+    tail = body[-_MC_TAIL:]
+    for pattern in _MC_TAGS + _MC_INLINE:
+        hits = list(pattern.finditer(tail))
         if hits:
-            return hits[-1].upper()
-    for line in reversed([ln.strip() for ln in body.splitlines() if ln.strip()][-3:]):
-        hits = _MC_WEAK.findall(line)
-        if hits:
-            return hits[-1].upper()
+            return normalise_choice(hits[-1].group(1))
     return None
 
 
