@@ -29,7 +29,7 @@ def test_parsers():
     assert parsers.extract_mc_answer("<think>x</think>\nB. because") == "B"
     assert parsers.extract_mc_answer("Reasoning...\nD") == "D"
     code = "text\n```python\ndef f(x):\n    return x + 1\n```\nmore"
-    assert parsers.extract_code(code) == "def f(x):\n    return x + 1"
+    assert parsers.extract_code(code) == "def f(x):\n    return x + 1\n"
     with pytest.raises(ValueError):
         parsers.parse_generation("nope", "x")
 
@@ -501,7 +501,7 @@ def test_reference_parser_names():
     assert parse_generation("lcb_code", "just words") is None
     assert parse_generation("identity", " x ") == " x " and parse_generation("noop", None) is None
     assert parse_generation("multiple_choice_answer", "The answer is B") == "B"
-    assert parse_generation("humaneval", "```python\nx = 1\n```") == "x = 1"
+    assert parse_generation("humaneval", "```python\nx = 1\n```") == "x = 1\n"
 
 
 def test_choice_parser_routes_to_multiple_choice_grading():
@@ -562,3 +562,35 @@ def test_protocol_math_grading():
                            ("\\boxed{5 cm}", "5", True), ("\\boxed{13}", "12", False), ("The answer is 7", "8", False)):
         assert grade_math(gen, truth)["correct"] is ok, (gen, truth)
     assert math_grading.normalise_answer("\\left( 1{,}000 \\right)") == "(1000)"
+
+
+def test_protocol_code_grading_on_prepared_records(tmp_path):
+    """HumanEval and MBPP rows in the prepared format (tests in ground_truth, the prompt in
+    completion_input) grade through score_file with the protocol's program assembly."""
+    from uno_b200.eval.code_grading import extract_mbpp_code
+    from uno_b200.eval.score import score_file
+
+    prompt = 'def inc(x):\n    """Add one."""\n'
+    he = tmp_path / "he.jsonl"
+    he.write_text(json.dumps({"id": "h0", "completion_input": prompt,
+                              "ground_truth": {"test": "def check(candidate):\n    assert candidate(2) == 3\n",
+                                               "entry_point": "inc"}}) + "\n")
+    gens = ["    return x + 1\n",                                   # body only
+            "def inc(y):\n    return y + 1\n",                      # whole function, renamed parameter
+            "<think>easy</think>\n```python\ndef inc(x):\n    return x + 1\n```",  # fenced after reasoning
+            "    return x\n"]                                        # wrong
+    hg = tmp_path / "hg.jsonl"
+    hg.write_text("".join(json.dumps({"id": "h0", "sample": i, "generation": g}) + "\n" for i, g in enumerate(gens)))
+    he_scores = score_file(hg, benchmark="humaneval", data=he, grades_out=tmp_path / "hgr.jsonl")
+    grades = [json.loads(x)["correct"] for x in (tmp_path / "hgr.jsonl").read_text().splitlines()]
+    assert grades == [True, True, True, False] and he_scores["accuracy"] == 0.75
+
+    tests = "assert add(1, 2) == 3"
+    assert extract_mbpp_code("```python\ndef helper():\n    pass\n```\n```python\ndef add(a, b):\n    return a + b\n```",
+                             tests).startswith("def add")
+    mb = tmp_path / "mb.jsonl"
+    mb.write_text(json.dumps({"id": "m0", "completion_input": "task", "ground_truth": tests}) + "\n")
+    mg = tmp_path / "mg.jsonl"
+    mg.write_text("".join(json.dumps({"id": "m0", "sample": i, "generation": g}) + "\n" for i, g in enumerate(
+        ["Here:\n```python\ndef add(a, b):\n    return a + b\n```\n[DONE]", "[BEGIN]\ndef add(a, b):\n    return a - b\n[DONE]"])))
+    assert score_file(mg, benchmark="mbpp", data=mb)["accuracy"] == 0.5

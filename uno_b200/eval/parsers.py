@@ -3,8 +3,8 @@
 * ``boxed``: content of the last ``\\boxed{...}`` (balanced braces);
 * ``mc_answer``: the chosen option (A-E, digits 1-5 read as A-E) by the
   protocol's ordered line and tail rules (``extract_mc_answer``);
-* ``code_completion``: the last fenced code block (``python`` blocks first),
-  else the text after a reasoning block;
+* ``code_completion``: the first fenced Python block after the first
+  reasoning block (``extract_code``);
 * ``passthrough``: the generation after any ``</think>`` marker;
 * ``noop`` / ``identity``: the generation unchanged;
 * ``gpqa_answer`` / ``mmlu_pro_answer``: the terminal option letter (A-D /
@@ -138,16 +138,26 @@ def extract_mc_answer(text: str | None) -> str | None:
     return None
 
 
-_FENCE = re.compile(r"```([A-Za-z0-9_+-]*)\s*\n(.*?)```", re.DOTALL)
+_CODE_FENCE = re.compile(r"```(?:python|py)?\s*\n(.*?)```", re.DOTALL)
 
 
 def extract_code(text: str | None) -> str | None:
-    body = strip_reasoning(text)
-    blocks = _FENCE.findall(body)
-    if blocks:
-        python = [code for lang, code in blocks if lang.lower() in ("python", "py", "python3")]
-        return (python or [code for _, code in blocks])[-1].strip("\n")
-    return body or None
+    """``code_completion``: the text after the first reasoning block (for a block that
+    never closes, its first fenced block or last paragraph), then its first fenced
+    Python block; ``None`` when nothing but whitespace is left."""
+    if text is None:
+        return None
+    t = _CHAT_END.sub("", text)
+    close = re.search(r"</(?:think|ifm\|think)>\s*", t, re.IGNORECASE)
+    if close:
+        t = t[close.end():]
+    elif re.match(r"\s*<(?:think|ifm\|think)>", t, re.IGNORECASE):
+        fence = _CODE_FENCE.search(t)
+        t = fence.group(1) if fence else t.split("\n\n")[-1]
+    fence = _CODE_FENCE.search(t)
+    if fence:
+        t = fence.group(1)
+    return t if t.strip() else None
 
 
 # ------------------------------------------------------- terminal choices

@@ -22,7 +22,7 @@ from typing import Any, Callable
 
 from uno_b200.eval.benchmarks import get_benchmark
 from uno_b200.eval.data import first_field, read_jsonl, ID_FIELDS
-from uno_b200.eval.graders import JUDGED_TASKS, OMNISCIENCE_DENOMINATOR, grade_code, grade_judged, grade_math, \
+from uno_b200.eval.graders import JUDGED_TASKS, OMNISCIENCE_DENOMINATOR, grade_judged, grade_math, \
     grade_multiple_choice, grade_with_judge
 from uno_b200.eval.parsers import CHOICE_PARSERS, CODE_PARSERS, parse_generation
 
@@ -61,8 +61,10 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     if parser in CODE_PARSERS or task in ("humaneval", "mbpp"):
         if record is None:
             return {"correct": None, "status": "missing source record"}
-        code_parser = parser if parser in CODE_PARSERS else "code_completion"
-        return grade_code(parse_generation(code_parser, gen) or "", record, timeout)
+        from uno_b200.eval.code_grading import grade_code_record
+
+        parsed = parse_generation(parser, gen) if parser in CODE_PARSERS else None
+        return grade_code_record(gen, parsed, record, timeout)
     if judge_model is not None:
         if judge is None:
             return {"correct": None, "status": "ungraded: no judge endpoint"}
