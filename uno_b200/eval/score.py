@@ -37,8 +37,9 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     if task == "ifeval":
         from uno_b200.eval.ifeval import grade_ifeval
 
-        prompt = row.get("question") or (record or {}).get("prompt", "")
-        return grade_ifeval(gen, truth if truth is not None else (record or {}), prompt)
+        rec = record or {}
+        prompt = rec.get("completion_input") or rec.get("prompt") or row.get("question") or ""
+        return grade_ifeval(gen, truth if truth is not None else rec.get("ground_truth", rec), prompt)
     if task in ("lcb", "lcbv6", "livecodebench"):
         from uno_b200.eval.lcb import extract_python_code, generation_passed, parse_tests, run_generation
 
