@@ -27,10 +27,15 @@ import re
 _THINK_END = "</think>"
 
 
+_REASONING_CLOSE = re.compile(r"</(?:ifm\|)?think[^>]*>", re.IGNORECASE)  # </think>, K2's </ifm|think>
+
+
 def strip_reasoning(text: str | None) -> str:
+    """The text after the last reasoning block (``</think>`` or ``</ifm|think>``), stripped."""
     if text is None:
         return ""
-    return text.rsplit(_THINK_END, 1)[-1].strip() if _THINK_END in text else text.strip()
+    closes = list(_REASONING_CLOSE.finditer(text))
+    return text[closes[-1].end():].strip() if closes else text.strip()
 
 
 def last_boxed(text: str | None) -> str | None:
