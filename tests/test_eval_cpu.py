@@ -594,3 +594,19 @@ def test_protocol_code_grading_on_prepared_records(tmp_path):
     mg.write_text("".join(json.dumps({"id": "m0", "sample": i, "generation": g}) + "\n" for i, g in enumerate(
         ["Here:\n```python\ndef add(a, b):\n    return a + b\n```\n[DONE]", "[BEGIN]\ndef add(a, b):\n    return a - b\n[DONE]"])))
     assert score_file(mg, benchmark="mbpp", data=mb)["accuracy"] == 0.5
+
+
+def test_scorer_reads_reference_runner_rows(tmp_path):
+    """Rows written by the reference runner (record:sampleN ids, source_row / sample_index, or a
+    generations list) grade like this framework's own rows."""
+    from uno_b200.eval.score import score_file
+
+    gens = tmp_path / "ref.jsonl"
+    gens.write_text("".join(json.dumps(r) + "\n" for r in (
+        {"id": "q1:sample0", "source_row": "q1", "sample_index": 0, "generation": "\\boxed{5}", "ground_truth": "5"},
+        {"id": "q1:sample1", "source_row": "q1", "sample_index": 1, "generation": "\\boxed{6}", "ground_truth": "5"},
+        {"source_row": "q2", "generations": ["\\boxed{2}", "\\boxed{2}"], "ground_truth": "2"})))
+    scores = score_file(gens, task="math", grades_out=tmp_path / "g.jsonl")
+    assert scores["rows"] == 4 and scores["accuracy"] == 0.75 and scores["question_accuracy"] == 0.75
+    ids = [(json.loads(x)["id"], json.loads(x)["sample"]) for x in (tmp_path / "g.jsonl").read_text().splitlines()]
+    assert ids == [("q1", 0), ("q1", 1), ("q2", 0), ("q2", 1)]

@@ -200,7 +200,8 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
         rid = idx if rid is None else rid
         for s in range(args.num_samples):
             items.append({"id": rid, "sample": s, "prompt_ids": ids, "prompt": text,
-                          "ground_truth": first_field(rec, ANSWER_FIELDS)})
+                          "ground_truth": first_field(rec, ANSWER_FIELDS), "chat_input": msgs,
+                          "completion_input": rec.get("completion_input")})
     done = set()
     if out.is_file():
         for row in read_jsonl(out):
@@ -251,7 +252,15 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
             total_tokens += len(o["token_ids"])
             row = {"id": it["id"], "sample": it["sample"], "question": it["prompt"],
                    "generation": o["text"], "token_count": len(o["token_ids"]), "budget": budget,
-                   "ground_truth": it["ground_truth"], "stats": o.get("stats", {})}
+                   "ground_truth": it["ground_truth"], "stats": o.get("stats", {}),
+                   # the reference runner's row keys, so that its scorer reads these files too
+                   "source_row": it["id"], "sample_index": it["sample"], "problem": it["prompt"],
+                   "rendered_prompt": it["prompt"], "chat_input": it["chat_input"],
+                   "prompt_token_count": len(it["prompt_ids"]), "output_token_count": len(o["token_ids"]),
+                   "context_length": args.max_model_len, "active_forward_reserve": reserve,
+                   "resolved_max_tokens": budget}
+            if it["completion_input"] is not None:
+                row["completion_input"] = it["completion_input"]
             if args.save_token_ids:
                 row["token_ids"] = list(o["token_ids"])
             rows.append(row)

@@ -74,6 +74,25 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     return grade_math(gen, truth)
 
 
+def expand_generation_rows(rows: list[dict]) -> list[dict]:
+    """One row per generation with ``id`` = the source record and ``sample``.
+
+    Reads this framework's rows and the reference runner's (``source_row``,
+    ``sample_index``, an ``id`` of ``record:sampleN``, or a ``generations``
+    list with one entry per sample)."""
+    out = []
+    for i, row in enumerate(rows):
+        rid = row.get("source_row", row.get("id", i))
+        gens = row.get("generations")
+        if isinstance(gens, list):
+            for k, g in enumerate(gens):
+                out.append({**row, "id": rid, "sample": k, "generation": g})
+            continue
+        sample = row.get("sample", row.get("sample_index", 0))
+        out.append({**row, "id": rid, "sample": sample})
+    return out
+
+
 def score_file(generations: str | Path, *, benchmark: str | None = None, data: str | Path | None = None,
                parser: str | None = None, grades_out: str | Path | None = None,
                scores_out: str | Path | None = None, summary: str | Path | None = None,
@@ -85,7 +104,7 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
     ``timeout`` overrides the benchmark's per-test grader timeout; ``workers``
     grading threads run at once (code runs in its own sandbox subprocess and
     judge calls are network-bound, so threads overlap them)."""
-    rows = read_jsonl(generations)
+    rows = expand_generation_rows(read_jsonl(generations))
     bench = get_benchmark(benchmark) if benchmark else None
     task = task or (bench.task if bench else "math")
     parser = parser or (bench.parser if bench else "passthrough")
