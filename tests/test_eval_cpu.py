@@ -610,3 +610,13 @@ def test_scorer_reads_reference_runner_rows(tmp_path):
     assert scores["rows"] == 4 and scores["accuracy"] == 0.75 and scores["question_accuracy"] == 0.75
     ids = [(json.loads(x)["id"], json.loads(x)["sample"]) for x in (tmp_path / "g.jsonl").read_text().splitlines()]
     assert ids == [("q1", 0), ("q1", 1), ("q2", 0), ("q2", 1)]
+
+
+def test_grouped_pass_at_k():
+    from uno_b200.eval.score import grouped_summary, pass_at_k
+
+    assert pass_at_k(5, 0, 1) == 0.0 and pass_at_k(5, 5, 1) == 1.0 and abs(pass_at_k(5, 1, 1) - 0.2) < 1e-12
+    assert abs(pass_at_k(5, 1, 5) - 1.0) < 1e-12 and pass_at_k(2, 1, 5) == 1.0  # k capped at n
+    s = grouped_summary({"a": [True, False, False, False, False], "b": [False] * 5})
+    assert s["num_problems"] == 2 and s["max_samples_per_problem"] == 5
+    assert abs(s["pass_at_1"] - 0.1) < 1e-12 and s["pass_at_5"] == 0.5 and "pass_at_10" not in s

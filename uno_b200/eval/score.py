@@ -74,6 +74,30 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     return grade_math(gen, truth)
 
 
+def pass_at_k(n: int, c: int, k: int) -> float:
+    """Unbiased pass@k of a problem with ``c`` of ``n`` samples correct (``k`` capped at ``n``)."""
+    from math import comb
+
+    if k <= 0:
+        return 0.0
+    k = min(k, n)
+    return 1.0 if n - c < k else 1.0 - comb(n - c, k) / comb(n, k)
+
+
+def grouped_summary(per_problem: dict[str, list[bool]]) -> dict[str, Any]:
+    """Problem count, samples per problem, and avg@k / pass@k for k = 1, 5, 10 (the
+    reference scorer's summary keys): avg@k averages each problem's first k samples."""
+    most = max((len(v) for v in per_problem.values()), default=0)
+    out: dict[str, Any] = {"num_problems": len(per_problem), "max_samples_per_problem": most}
+    for k in (1, 5, 10):
+        if most < k:
+            continue
+        first_k = [x for v in per_problem.values() for x in v[:k]]
+        out[f"avg_at_{k}"] = sum(first_k) / len(first_k) if first_k else float("nan")
+        out[f"pass_at_{k}"] = sum(pass_at_k(len(v), sum(v), k) for v in per_problem.values()) / len(per_problem)
+    return out
+
+
 def expand_generation_rows(rows: list[dict]) -> list[dict]:
     """One row per generation with ``id`` = the source record and ``sample``.
 
@@ -138,6 +162,9 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
         "graded": len(graded),
         "accuracy": sum(bool(g["correct"]) for g in graded) / len(graded) if graded else None,
         "question_accuracy": (sum(sum(v) / len(v) for v in per_q.values()) / len(per_q)) if per_q else None,
+        "num_generations": len(graded),
+        "num_correct": sum(bool(g["correct"]) for g in graded),
+        **grouped_summary(per_q),
     }
     if task == "aa_omniscience":  # the benchmark's own metrics, over its full question count
         right = sum(1 for g in grades if g.get("grade") == 1)
