@@ -457,7 +457,8 @@ def test_eval_runner_grades_judge_benchmarks_through_an_endpoint(tmp_path):
                   "--no-progress", "--grades", str(tmp_path / "g.jsonl"), "--scores", str(tmp_path / "s.json")])
     finally:
         server.shutdown()
-    assert s["scores"]["graded"] == 2 and s["scores"]["accuracy"] == 1.0
+    assert s["scores"]["graded"] == 2 and s["scores"]["num_correct"] == 2
+    assert s["scores"]["fixed_denominator"] == 2158  # HLE's question count: the toy rows are 2 of them
     assert seen and all(p == "/v1/chat/completions" and m == "stub-judge" and a == "Bearer k1"
                         for p, m, a, _ in seen)
     assert all(b["temperature"] == 0.3 and b["max_tokens"] == 77 and b["reasoning_effort"] == "low"
@@ -547,7 +548,7 @@ def test_judge_protocols_hle_omniscience_lcr(tmp_path):
                                "answer_type": "multipleChoice"}) + "\n")
     hg = tmp_path / "hg.jsonl"
     hg.write_text(json.dumps({"id": "h", "sample": 0, "generation": "The answer is C", "ground_truth": "C"}) + "\n")
-    assert score_file(hg, benchmark="hle", data=hle, judge=None)["accuracy"] == 1.0  # graded without a judge
+    assert score_file(hg, benchmark="hle", data=hle, judge=None)["num_correct"] == 1  # graded without a judge
 
 
 def test_protocol_math_grading():
@@ -620,3 +621,16 @@ def test_grouped_pass_at_k():
     s = grouped_summary({"a": [True, False, False, False, False], "b": [False] * 5})
     assert s["num_problems"] == 2 and s["max_samples_per_problem"] == 5
     assert abs(s["pass_at_1"] - 0.1) < 1e-12 and s["pass_at_5"] == 0.5 and "pass_at_10" not in s
+
+
+def test_fixed_denominator_counts_missing_generations(tmp_path):
+    from uno_b200.eval.score import score_file
+
+    gens = tmp_path / "gpqa.jsonl"  # 2 of GPQA-Diamond's 198 x 5 generations, both right
+    gens.write_text("".join(json.dumps({"id": f"g{i}", "sample": 0, "generation": "ANSWER: A", "ground_truth": "A"})
+                            + "\n" for i in range(2)))
+    scores = score_file(gens, benchmark="gpqa_diamond")
+    assert scores["fixed_denominator"] == 198 * 5 and scores["accuracy"] == 2 / 990
+    summary = tmp_path / "summary.json"
+    summary.write_text(json.dumps({"num_samples_per_problem": 1}))
+    assert score_file(gens, benchmark="gpqa_diamond", summary=summary)["fixed_denominator"] == 198

@@ -269,6 +269,8 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
     summary = {"protocol": PROTOCOL_NAME, "protocol_date": PROTOCOL_DATE, "benchmark": bench.name if bench else None,
                "protocol_arm": args.protocol_arm, "overrides": overrides, "model": args.model,
                "gated_lora_path": adapter, "requests": len(items), "generated": len(pending),
+               "num_problems": len(records), "num_samples_per_problem": args.num_samples,
+               "num_generations": len(items),
                "resumed": len(done), "skipped_no_budget": [[s["id"], s["sample"]] for s, _ in skipped],
                "total_output_tokens": total_tokens, "elapsed_seconds": elapsed,
                "output_tokens_per_second": total_tokens / elapsed if elapsed else 0.0,

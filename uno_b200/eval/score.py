@@ -74,6 +74,9 @@ def grade_row(row: dict, record: dict | None, *, task: str, parser: str, judge: 
     return grade_math(gen, truth)
 
 
+FIXED_DENOMINATOR_TASKS = ("gpqa_diamond", "hle", "aa_lcr")
+
+
 def pass_at_k(n: int, c: int, k: int) -> float:
     """Unbiased pass@k of a problem with ``c`` of ``n`` samples correct (``k`` capped at ``n``)."""
     from math import comb
@@ -173,6 +176,15 @@ def score_file(generations: str | Path, *, benchmark: str | None = None, data: s
                        "accuracy": right / OMNISCIENCE_DENOMINATOR,
                        "non_hallucination_rate": 1.0 - wrong / OMNISCIENCE_DENOMINATOR,
                        "omniscience_index": (right - wrong) / OMNISCIENCE_DENOMINATOR})
+    if bench is not None and task in FIXED_DENOMINATOR_TASKS:
+        # the benchmark's full count: a missing generation counts as a wrong one
+        samples = int(bench.num_samples)
+        if summary is not None and Path(summary).is_file():
+            gen_summary = json.loads(Path(summary).read_text())
+            samples = int(gen_summary.get("num_samples_per_problem", gen_summary.get("num_samples", samples)))
+        expected = bench.expected_rows * samples
+        scores["fixed_denominator"] = expected
+        scores["accuracy"] = scores["num_correct"] / expected
     if summary is not None and Path(summary).is_file():
         s = json.loads(Path(summary).read_text())
         for key in ("output_tokens_per_second", "decoder_tokens_per_sequence_forward", "total_output_tokens"):
