@@ -506,3 +506,25 @@ def test_learning_rate_schedules():
     assert lr_at(4, 1.0, 4, 100, "cosine") == 1.0 and lr_at(100, 1.0, 4, 100, "cosine") == pytest.approx(0.0)
     with pytest.raises(ValueError):
         lr_at(10, 1.0, 4, 100, "linear")
+
+
+def test_training_data_from_prepared_directories(tmp_path):
+    """``--data DIR`` works for rows.jsonl directories and for ``datasets`` directories saved by the
+    reference preparer, and the run manifest fingerprints the directory's files."""
+    import json
+
+    from datasets import Dataset
+
+    from uno_b200.train.data import data_manifest, load_jsonl
+
+    rows = [{"input_ids": [5, 6, 7], "labels": [-100, 6, 7]}, {"input_ids": [8, 9, 10], "labels": [8, 9, 10]}]
+    mine = tmp_path / "mine"
+    mine.mkdir()
+    (mine / "rows.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+    (mine / "uno_dataset_manifest.json").write_text(json.dumps({"hash": {"content_sha256": "abc"}}))
+    theirs = tmp_path / "theirs"
+    Dataset.from_list(rows).save_to_disk(str(theirs))
+    assert load_jsonl(mine) == rows and load_jsonl(theirs) == rows
+    m = data_manifest([mine])
+    assert m["corpus_hash"] == {"content_sha256": "abc"} and {f["path"] for f in m["files"]} >= {"rows.jsonl"}
+    assert data_manifest([theirs])["files"]

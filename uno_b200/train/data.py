@@ -68,10 +68,20 @@ def pack_rows(rows: list[dict], seq_len: int, pad_id: int = 0) -> list[dict[str,
 
 
 def load_jsonl(path: str | Path) -> list[dict]:
-    """Token rows from a JSONL file, or from ``rows.jsonl`` of a prepared corpus directory."""
+    """Token rows ``{"input_ids", "labels"}`` from a JSONL file or a prepared corpus directory:
+    ``rows.jsonl`` (written by ``uno_b200.train.prepare``) or a Hugging Face ``datasets``
+    directory saved with ``save_to_disk`` (the reference preparer's output)."""
     path = Path(path)
     if path.is_dir():
-        path = path / "rows.jsonl"
+        if (path / "rows.jsonl").is_file():
+            path = path / "rows.jsonl"
+        elif (path / "state.json").is_file() or (path / "dataset_info.json").is_file():
+            from datasets import load_from_disk
+
+            return [{"input_ids": list(r["input_ids"]), "labels": list(r["labels"])}
+                    for r in load_from_disk(str(path))]
+        else:
+            raise FileNotFoundError(f"{path} has neither rows.jsonl nor a saved datasets directory")
     with open(path, encoding="utf-8") as fh:
         return [json.loads(line) for line in fh if line.strip()]
 
@@ -87,11 +97,26 @@ def batches_from_rows(packed: list[dict[str, torch.Tensor]], batch_size: int, se
 
 
 def data_manifest(paths: list[str | Path]) -> dict:
-    files = []
-    for p in sorted(str(x) for x in paths):
+    """sha256 and size of every data file (a directory contributes its files, and the corpus
+    hash of its ``uno_dataset_manifest.json`` when present)."""
+    files, corpus = [], None
+    expanded = []
+    for x in paths:
+        x = Path(x)
+        if x.is_dir():
+            manifest = x / "uno_dataset_manifest.json"
+            if manifest.is_file():
+                corpus = json.loads(manifest.read_text()).get("hash")
+            expanded += [f for f in sorted(x.rglob("*")) if f.is_file() and not f.name.startswith(".")]
+        else:
+            expanded.append(x)
+    for p in sorted(str(x) for x in expanded):
         h = hashlib.sha256()
         with open(p, "rb") as fh:
             for chunk in iter(lambda: fh.read(1 << 20), b""):
                 h.update(chunk)
         files.append({"path": Path(p).name, "sha256": h.hexdigest(), "bytes": Path(p).stat().st_size})
-    return {"version": 1, "files": files}
+    out = {"version": 1, "files": files}
+    if corpus is not None:
+        out["corpus_hash"] = corpus
+    return out
