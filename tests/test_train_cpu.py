@@ -528,3 +528,28 @@ def test_training_data_from_prepared_directories(tmp_path):
     m = data_manifest([mine])
     assert m["corpus_hash"] == {"content_sha256": "abc"} and {f["path"] for f in m["files"]} >= {"rows.jsonl"}
     assert data_manifest([theirs])["files"]
+
+
+def test_prepared_rows_are_padded_one_per_sequence(tmp_path):
+    import json
+
+    import pytest
+
+    from uno_b200.train.__main__ import main
+    from uno_b200.train.data import pad_rows
+
+    rows = [{"input_ids": [5, 6, 7], "labels": [-100, 6, 7]}, {"input_ids": [8, 9], "labels": [8, 9]}]
+    seqs = pad_rows(rows, 4, pad_id=0)
+    assert [s["input_ids"].tolist() for s in seqs] == [[5, 6, 7, 0], [8, 9, 0, 0]]
+    assert [s["labels"].tolist() for s in seqs] == [[-100, 6, 7, -100], [8, 9, -100, -100]]
+    with pytest.raises(ValueError, match="sequence length"):
+        pad_rows(rows, 2)
+    data = tmp_path / "rows.jsonl"
+    data.write_text("".join(json.dumps({"input_ids": [7 + i % 50] * 40, "labels": [7 + i % 50] * 40}) + "\n"
+                            for i in range(8)))
+    hist = main(["--model", "preset:tiny-qwen3", "--output-dir", str(tmp_path / "run"), "--device", "cpu",
+                 "--data", str(data), "--block-sizes", "4", "--steps-per-stage", "2", "--seq-len", "64",
+                 "--global-batch", "2", "--lora-rank", "8"])
+    assert [m["step"] for m in hist] == [1, 2] and all(m["tokens"] > 0 for m in hist)
+    man = json.loads((tmp_path / "run" / "uno_training_manifest.json").read_text())
+    assert man["compatibility"]["data"]["collation"] == "pad"

@@ -41,6 +41,8 @@ def build_parser() -> argparse.ArgumentParser:
                    help="with --block-sizes: sets the global batch to world * micro-batch * steps")
     p.add_argument("--data", "--dataset-path", dest="data", default="synthetic")
     p.add_argument("--prompt-len", type=int, default=0)
+    p.add_argument("--pack-rows", action="store_true",
+                   help="pack several prepared rows per sequence instead of one padded row per sequence")
     p.add_argument("--lr", "--learning-rate", dest="lr", type=float, default=1e-4)
     p.add_argument("--warmup-steps", type=int, default=0)
     p.add_argument("--lr-schedule", choices=("constant", "cosine"), default="constant",
@@ -121,7 +123,8 @@ def main(argv: list[str] | None = None) -> list[dict]:
     from uno_b200.models.presets import resolve_preset
     from uno_b200.train import BlockCurriculumPlan, LoraSettings, TrainableLoRA, UnoObjectiveConfig, UnoTrainer
     from uno_b200.train.config import manifest_digest, validate_resume_manifest, write_run_manifest
-    from uno_b200.train.data import batches_from_rows, data_manifest, load_jsonl, pack_rows, synthetic_batches
+    from uno_b200.train.data import batches_from_rows, data_manifest, load_jsonl, pack_rows, pad_rows, \
+        synthetic_batches
     from uno_b200.utils.hf_compat import load_model_config
     from uno_b200.utils.loader import dummy_init, load_model
 
@@ -183,9 +186,10 @@ def main(argv: list[str] | None = None) -> list[dict]:
                                     seed=args.seed * 7919 + rank)
         data_info = {"kind": "synthetic-zipf-1.1", "seed": args.seed}
     else:
-        batches = batches_from_rows(pack_rows(load_jsonl(args.data), plan.sequence_length), args.micro_batch,
+        collate = pack_rows if args.pack_rows else pad_rows
+        batches = batches_from_rows(collate(load_jsonl(args.data), plan.sequence_length), args.micro_batch,
                                     seed=args.seed * 7919 + rank)
-        data_info = data_manifest([args.data])
+        data_info = data_manifest([args.data]) | {"collation": "pack" if args.pack_rows else "pad"}
     compat = {"model": args.model, "curriculum_sha256": plan.sha256(), "lora": vars(settings) | {"alpha": settings.resolved_alpha},
               "objective": vars(objective), "mask_token_id": int(mask_id), "data": data_info,
               "micro_batch": args.micro_batch, "world_size": world, "lr_schedule": args.lr_schedule}

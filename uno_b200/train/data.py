@@ -1,12 +1,13 @@
-"""Training data: synthetic Zipf batches, packed JSONL token rows, manifests.
+"""Training data: synthetic Zipf batches, padded or packed token rows, manifests.
 
 * :func:`synthetic_batches` -- random token ids drawn Zipf(a) over a fixed
   permutation of the vocabulary (the benchmark configs' "Zipf(1.1) random token
   ids"), optionally with an unsupervised prompt prefix;
-* :func:`pack_rows` -- packs pre-tokenised ``{"input_ids", "labels"}`` rows
-  into fixed-length sequences whose positions restart at every packed
-  example, right-padded with IGNORE labels (collation of
-  ``training/data.py:55-118``);
+* :func:`pad_rows` -- one pre-tokenised ``{"input_ids", "labels"}`` row per
+  sequence, right-padded with IGNORE labels (the released recipe's collator,
+  ``training/data.py:209-239``); the default of ``uno_b200.train``;
+* :func:`pack_rows` -- greedy packing of several rows into one sequence,
+  positions restarting per row (``--pack-rows``; not the recipe);
 * :func:`data_manifest` -- sha256 of the data files, pinned in the run
   manifest (``training/data.py:139-206``).
 """
@@ -38,8 +39,28 @@ def synthetic_batches(batch_size: int, seq_len: int, vocab_size: int, *, zipf_a:
                "position_ids": torch.arange(seq_len).expand(batch_size, seq_len).clone()}
 
 
+def pad_rows(rows: list[dict], seq_len: int, pad_id: int = 0) -> list[dict[str, torch.Tensor]]:
+    """One prepared row per sequence, right-padded to ``seq_len`` with ignored labels -- the
+    released recipe's collation (``training/data.py:209-239``).  The layout is causal, so the real
+    tokens never see the padding after them.  A row longer than ``seq_len`` is an error."""
+    out = []
+    for i, row in enumerate(rows):
+        ids = list(row["input_ids"])
+        lab = list(row.get("labels", ids))
+        if len(ids) != len(lab):
+            raise ValueError(f"row {i}: input_ids and labels must have the same length")
+        if len(ids) > seq_len:
+            raise ValueError(f"row {i} has {len(ids)} tokens, more than the sequence length {seq_len} "
+                             "(raise --seq-len, or pack rows with --pack-rows)")
+        pad = seq_len - len(ids)
+        out.append({"input_ids": torch.tensor(ids + [pad_id] * pad), "labels": torch.tensor(lab + [IGNORE_INDEX] * pad),
+                    "position_ids": torch.arange(seq_len)})
+    return out
+
+
 def pack_rows(rows: list[dict], seq_len: int, pad_id: int = 0) -> list[dict[str, torch.Tensor]]:
-    """Greedy first-fit packing of token rows into ``seq_len`` sequences."""
+    """Greedy first-fit packing of token rows into ``seq_len`` sequences (positions restart per
+    row, but a later row attends to the earlier rows of its pack: an option, not the recipe)."""
     out, cur_ids, cur_lab, cur_pos = [], [], [], []
 
     def flush():

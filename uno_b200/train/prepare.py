@@ -18,7 +18,7 @@ that a corpus prepared here hashes to the reference's manifest):
   and supervised-token counts.
 
 Output: ``rows.jsonl`` (one ``{"input_ids", "labels"}`` object per row, the
-format :func:`uno_b200.train.data.pack_rows` reads) and
+format :func:`uno_b200.train.data.load_jsonl` reads) and
 ``uno_dataset_manifest.json`` (source, tokenizer, recipe, hash).  Input is a
 local JSONL / JSON file with a ``conversations`` field per row, or a dataset
 id that the ``datasets`` package can load when a network is available.
