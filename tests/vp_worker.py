@@ -6,6 +6,8 @@ fused-collective workspace; the results must equal the single-GPU kernels on
 the full rows (samples and arg-max exactly, verify decisions up to summation
 order, which these inputs do not reach).  The draft-tree candidates merged from
 the shards must equal the top-K of the full rows, and build the same trees.
+Top-k / top-p sampling and verification merged from the shards must take the
+same decisions as the same merge over the full rows.
 """
 
 import os
@@ -85,6 +87,24 @@ def main():
         if not (torch.equal(t_full.token_ids, t_vp.token_ids) and torch.equal(t_full.parent_indices,
                                                                                t_vp.parent_indices)):
             failures.append(f"tree B={B} K={K}: trees differ")
+    # top-k / top-p: merged shard candidates (NCCL all-gather) == the same merge on the full rows
+    from uno_b200.engine import vp_filtered as vpf
+
+    def nccl_gather(x):
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous())
+        return torch.cat(parts, dim=-1)
+
+    full = (torch.randn(48, V, device="cuda", generator=g) * 3).bfloat16()
+    draft = (full.float() + torch.randn(48, V, device="cuda", generator=g)).bfloat16()
+    for k, p in ((20, 1.0), (0, 0.9), (50, 0.8)):
+        sh = lambda x: x[:, rank * Vs:(rank + 1) * Vs].contiguous()  # noqa: E731
+        tok, q = vpf.sample(sh(draft), k, p, 0.7, rank * Vs, nccl_gather, 3, 1)
+        acc, corr = vpf.verify(sh(full), tok, q, k, p, 0.7, rank * Vs, nccl_gather, 3, 2)
+        tok1, q1 = vpf.sample(draft, k, p, 0.7, 0, lambda x: x, 3, 1)
+        acc1, corr1 = vpf.verify(full, tok1, q1, k, p, 0.7, 0, lambda x: x, 3, 2)
+        if not (torch.equal(tok, tok1) and torch.equal(acc, acc1) and torch.equal(corr, corr1)):
+            failures.append(f"filtered k={k} p={p}: shard merge differs from the full rows")
     err = cuda.error_flag()
     if err:
         failures.append(f"device error flag {err}")

@@ -33,9 +33,10 @@ the lm_head leaves each rank a ``[rows, V/tp]`` logits shard and
 sampling and the unfiltered verify then run the vocab-parallel kernels, which
 exchange a few numbers per row between ranks instead of the logits; the
 Philox noise is keyed by global token id, so the tokens equal those of the
-same logits on one GPU.  Top-k / top-p gather the full logits first
-(``Sampler.full``); the draft tree merges per-shard top-K candidates
-(``draft_tree.shard_candidate_log_probs``).
+same logits on one GPU.  Top-k / top-p merge each rank's best candidates
+(``engine/vp_filtered.py``: exact, with the logits gathered only for a batch
+the candidates cannot decide); the draft tree merges per-shard top-K
+candidates (``draft_tree.shard_candidate_log_probs``).
 """
 
 from __future__ import annotations
@@ -138,7 +139,12 @@ class Sampler:
         if self._sharded(logits):
             if not sp.filtered(V):
                 return self.sample_full(logits, sp.temperature), None
-            logits = self.full(logits)
+            from uno_b200.engine import vp_filtered
+
+            k, p = filter_args(sp, V)
+            key = self._next()
+            return vp_filtered.sample(logits.reshape(-1, logits.shape[-1]), k, p, sp.temperature, self.shard.start,
+                                      self.shard.gather, self.seed, key)
         if sp.filtered(V):
             k, p = filter_args(sp, V)
             if native_filtered(logits):
@@ -198,6 +204,13 @@ class Sampler:
 
     def verify_filtered(self, clean_logits: torch.Tensor, spec: torch.Tensor, sp: SamplingParams,
                         draft_distribution):
+        if self._sharded(clean_logits) and not isinstance(draft_distribution, FilteredRows):
+            from uno_b200.engine import vp_filtered
+
+            k, p = filter_args(sp, self.shard.vocab)
+            key = self._next()
+            return vp_filtered.verify(clean_logits.reshape(-1, clean_logits.shape[-1]), spec, draft_distribution, k, p,
+                                      sp.temperature, self.shard.start, self.shard.gather, self.seed, key)
         clean_logits = self.full(clean_logits)
         V = clean_logits.shape[-1]
         if isinstance(draft_distribution, FilteredRows):
