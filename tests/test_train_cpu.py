@@ -553,3 +553,80 @@ def test_prepared_rows_are_padded_one_per_sequence(tmp_path):
     assert [m["step"] for m in hist] == [1, 2] and all(m["tokens"] > 0 for m in hist)
     man = json.loads((tmp_path / "run" / "uno_training_manifest.json").read_text())
     assert man["compatibility"]["data"]["collation"] == "pad"
+
+
+def test_wandb_reporting_and_credential_check(tmp_path, monkeypatch):
+    import json
+    import sys
+    import types
+
+    import pytest
+
+    from uno_b200.train.__main__ import main
+    from uno_b200.train.metrics_sink import check_wandb, wandb_credentials_present
+
+    calls = []
+
+    class Run:
+        def log(self, row, step):
+            calls.append(("log", step, sorted(row)))
+
+        def finish(self):
+            calls.append(("finish",))
+
+    fake = types.ModuleType("wandb")
+    fake.init = lambda **kw: calls.append(("init", kw["project"], kw["mode"], kw["name"])) or Run()
+    monkeypatch.setitem(sys.modules, "wandb", fake)
+    env = {"NETRC": str(tmp_path / "no-netrc")}
+    assert not wandb_credentials_present(env)
+    with pytest.raises(SystemExit, match="credentials"):
+        check_wandb("online", env)
+    (tmp_path / "netrc").write_text("machine api.wandb.ai login user password k3y\n")
+    assert wandb_credentials_present({"NETRC": str(tmp_path / "netrc")})
+    assert wandb_credentials_present({"WANDB_API_KEY": "x", **env})
+    monkeypatch.delitem(sys.modules, "wandb")
+    monkeypatch.setattr("builtins.__import__", _refuse_wandb(__import__))
+    with pytest.raises(SystemExit, match="wandb package"):
+        check_wandb("offline", env)
+    monkeypatch.undo()
+    monkeypatch.setitem(sys.modules, "wandb", fake)
+    out = tmp_path / "run"
+    main(["--model", "preset:tiny-qwen3", "--output-dir", str(out), "--device", "cpu", "--block-sizes", "4",
+          "--steps-per-stage", "2", "--seq-len", "32", "--global-batch", "2", "--lora-rank", "8",
+          "--wandb-mode", "offline", "--wandb-project", "p", "--run-name", "r1"])
+    assert calls[0] == ("init", "p", "offline", "r1") and calls[-1] == ("finish",)
+    assert [c[1] for c in calls if c[0] == "log"] == [1, 2]
+    assert "train/loss" in calls[1][2]
+    man = json.loads((out / "uno_training_manifest.json").read_text())
+    assert man["wandb"] == {"project": "p", "mode": "offline"}
+
+
+def _refuse_wandb(real_import):
+    def guarded(name, *args, **kwargs):
+        if name == "wandb":
+            raise ImportError("no wandb")
+        return real_import(name, *args, **kwargs)
+    return guarded
+
+
+def test_slurm_launcher_dry_run(tmp_path):
+    import os
+    import subprocess
+
+    script = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "uno_b200", "train",
+                          "run_slurm.sh")
+    env = {k: v for k, v in os.environ.items() if not k.startswith(("SLURM_", "WANDB_", "UNO_"))}
+    env.update(MODEL="preset:tiny-qwen3", DATA="synthetic", OUTPUT_ROOT=str(tmp_path), RUN_NAME="r1", DRY_RUN="1")
+    sub = subprocess.run(["bash", script], env=env, capture_output=True, text=True, timeout=60)
+    assert sub.returncode == 0, sub.stderr
+    assert sub.stdout.startswith("sbatch ") and "--nodes=2" in sub.stdout and "--job-name=r1" in sub.stdout
+    env.update(UNO_NODE_WORKER="1", SLURM_NNODES="2", SLURM_PROCID="1", MASTER_ADDR="127.0.0.1", MASTER_PORT="29500",
+               WANDB_MODE="disabled", SLURM_TMPDIR=str(tmp_path))
+    sub = subprocess.run(["bash", script], env=env, capture_output=True, text=True, timeout=60)
+    assert sub.returncode == 0, sub.stderr
+    cmd = sub.stdout.strip().splitlines()[-1].split()
+    assert cmd[1:3] == ["-m", "torch.distributed.run"] and "--node-rank=1" in cmd and "--nproc-per-node=8" in cmd
+    for flag, value in (("--global-batch", "128"), ("--seq-len", "4096"), ("--lr", "1e-5"), ("--warmup-steps", "562"),
+                        ("--curriculum", "released"), ("--run-name", "r1"), ("--wandb-mode", "disabled"),
+                        ("--lora-rank", "128")):
+        assert cmd[cmd.index(flag) + 1] == value, flag

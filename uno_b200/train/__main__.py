@@ -13,8 +13,9 @@ accepted as well: ``--learning-rate``, ``--per-device-batch-size``,
 (the loss weights), and ``--deepspeed CONFIG``, whose ZeRO stage, gradient
 clipping, micro-batch and accumulation settings map onto this trainer
 (stage 3 shards the frozen base like ``--fsdp``; stage 2 is the default
-sharded optimizer).  Metrics go to stdout and ``OUTPUT_DIR/metrics.jsonl``;
-the Weights & Biases options are accepted and unused.
+sharded optimizer).  Metrics go to stdout and ``OUTPUT_DIR/metrics.jsonl``,
+and to a Weights & Biases run with ``--wandb-mode online|offline``
+(``train/metrics_sink.py``).
 """
 
 from __future__ import annotations
@@ -25,6 +26,8 @@ import os
 
 import torch
 import torch.distributed as dist
+
+from uno_b200.train.metrics_sink import MetricsSink, check_wandb
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -69,8 +72,11 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--local-rank", "--local_rank", dest="local_rank", type=int, default=-1,
                    help="launcher compatibility; LOCAL_RANK in the environment takes precedence")
     p.add_argument("--dataloader-num-workers", type=int, default=0, help="accepted; rows are packed in-process")
-    p.add_argument("--wandb-project", help="accepted; metrics are written to OUTPUT_DIR/metrics.jsonl")
-    p.add_argument("--wandb-mode", choices=("online", "offline", "disabled"), default="disabled")
+    p.add_argument("--wandb-project", default=os.environ.get("WANDB_PROJECT", "uno-training"),
+                   help="W&B project of the run (metrics also go to OUTPUT_DIR/metrics.jsonl)")
+    p.add_argument("--wandb-mode", choices=("online", "offline", "disabled"),
+                   default=os.environ.get("WANDB_MODE", "disabled"),
+                   help="W&B reporting; online needs credentials (default: $WANDB_MODE, else disabled)")
     p.add_argument("--max-steps", type=int, help="stop after this many optimizer steps (default: curriculum end)")
     p.add_argument("--fsdp", action="store_true",
                    help="CUDA: shard the frozen projection weights over the ranks (GEMMs read peers' rows)")
@@ -112,6 +118,7 @@ def apply_deepspeed_config(args, path: str) -> dict:
 
 def main(argv: list[str] | None = None) -> list[dict]:
     args = build_parser().parse_args(argv)
+    check_wandb(args.wandb_mode)
     deepspeed = apply_deepspeed_config(args, args.deepspeed) if args.deepspeed else None
     if args.micro_batch is None:
         args.micro_batch = 1
@@ -204,25 +211,24 @@ def main(argv: list[str] | None = None) -> list[dict]:
         validate_resume_manifest(out, compat)
         trainer.resume(args.resume)
     elif rank == 0:
-        extra = {"compatibility_sha256_short": manifest_digest(compat)[:12], "run_name": args.run_name}
+        extra = {"compatibility_sha256_short": manifest_digest(compat)[:12], "run_name": args.run_name,
+                 "wandb": {"project": args.wandb_project, "mode": args.wandb_mode}}
         if deepspeed is not None:
             extra["deepspeed_config"] = {"path": args.deepspeed, "applied": deepspeed}
         write_run_manifest(out, compat, extra)
     last = min(plan.max_steps, args.max_steps or plan.max_steps)
     history = []
-    log = open(os.path.join(out, "metrics.jsonl"), "a", encoding="utf-8") if rank == 0 else None
+    sink = MetricsSink(out, rank=rank, wandb_mode=args.wandb_mode, wandb_project=args.wandb_project,
+                       run_name=args.run_name, config=compat, resume=bool(args.resume))
     try:
         while trainer.step < last:
             metrics = trainer.train_step([next(batches) for _ in range(accumulation)])
             history.append(metrics)
-            if log is not None:
-                log.write(json.dumps(metrics) + "\n")
-                log.flush()
-                if trainer.step % max(1, args.logging_steps) == 0 or trainer.step == last:
-                    print(json.dumps(metrics), flush=True)
+            sink.log(metrics)
+            if rank == 0 and (trainer.step % max(1, args.logging_steps) == 0 or trainer.step == last):
+                print(json.dumps(metrics), flush=True)
     finally:
-        if log is not None:
-            log.close()
+        sink.close()
     if rank == 0:
         lora.save(os.path.join(out, "final_adapter"), args.model)
     if group is not None:

@@ -14,7 +14,17 @@
 # directory or "synthetic"), OUTPUT_ROOT (shared storage).  Optional knobs
 # below; GLOBAL_BATCH must divide by NODES * GPUS_PER_NODE * MICRO_BATCH
 # (the quotient is the gradient-accumulation count).
+#
+# DRY_RUN=1 prints the sbatch / srun / torchrun command it would run and exits.
 set -euo pipefail
+
+launch() {
+  if [[ "${DRY_RUN:-0}" == "1" ]]; then
+    printf '%q ' "$@"; printf '\n'
+    exit 0
+  fi
+  exec "$@"
+}
 
 REPO_ROOT="${UNO_REPO_ROOT:-$(cd "$(dirname "${BASH_SOURCE[0]}")/../.." && pwd)}"
 PYTHON_BIN="${PYTHON_BIN:-python}"
@@ -35,6 +45,8 @@ CE_WEIGHT="${CE_WEIGHT:-0.0}"
 CE_TARGET="${CE_TARGET:-teacher}"
 CURRICULUM="${CURRICULUM:-released}"   # the released run's six-stage schedule, or a YAML path
 RUN_NAME="${RUN_NAME:-uno-$(date -u +%Y%m%dT%H%M%SZ)}"
+WANDB_MODE="${WANDB_MODE:-online}"       # online needs `wandb login` or WANDB_API_KEY; offline or disabled otherwise
+WANDB_PROJECT="${WANDB_PROJECT:-uno-training}"
 : "${MODEL:?set MODEL to a checkpoint directory or preset:NAME}"
 : "${DATA:?set DATA to a prepared corpus directory or synthetic}"
 : "${OUTPUT_ROOT:?set OUTPUT_ROOT to shared storage}"
@@ -54,7 +66,8 @@ if [[ -n "${FIXED_BLOCK_SIZE:-}" && "${UNO_NODE_WORKER:-0}" != "1" ]]; then
     --global-batch-size "${GLOBAL_BATCH}")
 fi
 export REPO_ROOT PYTHON_BIN NODES GPUS_PER_NODE MICRO_BATCH GLOBAL_BATCH SEQ_LEN LORA_RANK LORA_TARGET LR \
-  WARMUP_STEPS TV_WEIGHT KL_WEIGHT CE_WEIGHT CE_TARGET CURRICULUM RUN_NAME MODEL DATA OUTPUT_DIR LOG_DIR
+  WARMUP_STEPS TV_WEIGHT KL_WEIGHT CE_WEIGHT CE_TARGET CURRICULUM RUN_NAME MODEL DATA OUTPUT_DIR LOG_DIR \
+  WANDB_MODE WANDB_PROJECT
 
 if [[ "${UNO_NODE_WORKER:-0}" == "1" ]]; then
   # one task per node: exec torchrun for this node's GPUs
@@ -66,13 +79,13 @@ if [[ "${UNO_NODE_WORKER:-0}" == "1" ]]; then
        --seq-len "${SEQ_LEN}" --global-batch "${GLOBAL_BATCH}" --micro-batch "${MICRO_BATCH}"
        --lora-rank "${LORA_RANK}" --lora-target "${LORA_TARGET}" --lr "${LR}" --warmup-steps "${WARMUP_STEPS}"
        --tv-weight "${TV_WEIGHT}" --kl-weight "${KL_WEIGHT}" --ce-weight "${CE_WEIGHT}" --ce-target "${CE_TARGET}"
-       --checkpoint-layers)
+       --checkpoint-layers --run-name "${RUN_NAME}" --wandb-mode "${WANDB_MODE}" --wandb-project "${WANDB_PROJECT}")
   [[ -n "${CURRICULUM}" ]] && cmd+=(--curriculum "${CURRICULUM}")
   [[ -n "${LORA_ALPHA:-}" ]] && cmd+=(--lora-alpha "${LORA_ALPHA}")
   [[ -n "${RESUME:-}" ]] && cmd+=(--resume "${RESUME}")
   printf 'node %s:' "${SLURM_PROCID}"; printf ' %q' "${cmd[@]}"; printf '\n'
   cd "${REPO_ROOT}"
-  exec "${cmd[@]}"
+  launch "${cmd[@]}"
 fi
 
 mkdir -p "${LOG_DIR}" "${OUTPUT_DIR}"
@@ -80,9 +93,9 @@ if [[ -n "${SLURM_JOB_ID:-}" ]]; then
   # already inside an allocation: start one worker task per node
   export MASTER_ADDR="${MASTER_ADDR:-$(scontrol show hostnames "${SLURM_JOB_NODELIST}" | head -n 1)}"
   export MASTER_PORT="${MASTER_PORT:-$((20000 + SLURM_JOB_ID % 20000))}"
-  UNO_NODE_WORKER=1 exec srun --nodes="${NODES}" --ntasks-per-node=1 --cpus-per-task="${CPUS_PER_TASK}" \
+  UNO_NODE_WORKER=1 launch srun --nodes="${NODES}" --ntasks-per-node=1 --cpus-per-task="${CPUS_PER_TASK}" \
     --kill-on-bad-exit=1 bash "${BASH_SOURCE[0]}"
 fi
-exec sbatch --job-name="${RUN_NAME}" --nodes="${NODES}" --ntasks-per-node=1 --gpus-per-node="${GPUS_PER_NODE}" \
+launch sbatch --job-name="${RUN_NAME}" --nodes="${NODES}" --ntasks-per-node=1 --gpus-per-node="${GPUS_PER_NODE}" \
   --cpus-per-task="${CPUS_PER_TASK}" --time="${TIME_LIMIT}" --output="${LOG_DIR}/%x-%j.out" \
   --export=ALL "${BASH_SOURCE[0]}"
