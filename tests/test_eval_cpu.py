@@ -634,3 +634,78 @@ def test_fixed_denominator_counts_missing_generations(tmp_path):
     summary = tmp_path / "summary.json"
     summary.write_text(json.dumps({"num_samples_per_problem": 1}))
     assert score_file(gens, benchmark="gpqa_diamond", summary=summary)["fixed_denominator"] == 198
+
+
+def test_pull_suite_settings_from_env_and_canonical_guard(tmp_path):
+    import pytest
+
+    from uno_b200.eval.benchmarks import get_benchmark
+    from uno_b200.eval.pull_suite import apply_env, build_parser, resolve_suite, worker_settings, \
+        write_suite_summary
+
+    def parse(argv, env):
+        args = build_parser().parse_args(["jobs", *argv])
+        apply_env(args, env)
+        return args
+
+    bench = get_benchmark("gsm8k")
+    args = parse([], {"NANO_MODEL": "m", "NANO_BENCHMARKS": "gsm8k", "NANO_SAVE_TOKEN_IDS": "1",
+                      "NANO_STOP_TOKEN_IDS": "5,6", "NANO_DIFFUSION_BLOCK_SIZE": "8"})
+    assert args.model == "m" and args.benchmark == ["gsm8k"] and args.save_token_ids and args.stop_token_ids == [5, 6]
+    assert args.diffusion_block_size == 8 and args.tree_candidate_top_k == 16
+    assert resolve_suite(args) == {}
+    assert (args.num_samples, args.context_length, args.top_p) == (bench.num_samples, bench.max_model_len,
+                                                                    bench.top_p)
+    assert args.max_num_batched_tokens == bench.max_model_len
+    # the command line wins over the environment; a departure needs a protocol arm
+    args = parse(["--top-p", "0.5"], {"NANO_BENCHMARKS": "gsm8k", "NANO_TOP_P": "0.7"})
+    assert args.top_p == 0.5
+    with pytest.raises(SystemExit, match="protocol-arm"):
+        resolve_suite(args)
+    args = parse(["--top-p", "0.5", "--limit", "3"], {"NANO_BENCHMARKS": "gsm8k", "NANO_PROTOCOL_ARM": "arm-a"})
+    assert set(resolve_suite(args)) == {"top_p", "limit"}
+    with pytest.raises(SystemExit, match="one benchmark"):
+        resolve_suite(parse([], {"NANO_BENCHMARKS": "gsm8k,math500"}))
+    args = parse([], {"NANO_BENCHMARKS": "gsm8k math500", "NANO_PROTOCOL_ARM": "uniform"})
+    assert resolve_suite(args) == {} and args.max_num_seqs == 64
+
+    manifest = {"model": "m", "diffusion_block_size": 8, "sampling": {"temperature": 0.6, "top_p": 0.95, "top_k": 20},
+                "request": {"mask_token_id": 9, "stop_token_ids": [5], "noise_mode": "random_uniform",
+                            "noise_salt": None, "ignore_eos": False},
+                "engine": {"max_num_seqs": 32, "max_model_len": 4096, "tree_verify_size": None,
+                           "cuda_graph_block_sizes": [1, 8]}, "benchmarks": [{"name": "gsm8k"}]}
+    sp, kw = worker_settings(manifest, build_parser().parse_args(["worker", "--device", "cpu"]))
+    assert (sp.temperature, sp.top_k, sp.mask_token_id, sp.stop_token_ids, sp.diffusion_block_size) == \
+        (0.6, 20, 9, [5], 8)
+    assert kw["max_num_seqs"] == 32 and kw["max_model_len"] == 4096 and "tree_verify_size" not in kw
+    assert kw["device"] == "cpu" and kw["max_diffusion_block_size"] == 8
+
+    path = tmp_path / "suite_summary.json"
+    a = write_suite_summary(path, manifest, 4, {"num_generations": 10, "output_tokens": 4000, "elapsed_seconds": 2.0})
+    assert a["invocation_output_tokens_per_second_per_gpu"] == 500.0
+    b = write_suite_summary(path, manifest, 4, {"num_generations": 0, "output_tokens": 0, "elapsed_seconds": 1.0})
+    assert b["generation_invocation_output_tokens_per_second"] == 2000.0 and b["benchmarks"] == ["gsm8k"]
+    assert len(json.loads(path.read_text())["invocations"]) == 2
+
+
+def test_pull_suite_jobs_role_writes_engine_and_request_settings(tmp_path, monkeypatch):
+    from uno_b200.eval.benchmarks import get_benchmark
+    from uno_b200.eval.pull_suite import main
+
+    model = _chat_model_dir(tmp_path)
+    root = tmp_path / "data"
+    root.mkdir()
+    (root / get_benchmark("gsm8k").data_path.name).write_text(_dataset(tmp_path).read_text())
+    monkeypatch.setenv("NANO_RESULTS_ROOT", str(tmp_path / "results"))
+    monkeypatch.setenv("NANO_RUN_NAME", "r1")
+    monkeypatch.setenv("NANO_BENCHMARKS", "gsm8k")
+    monkeypatch.setenv("NANO_MODEL", str(model))
+    monkeypatch.setenv("NANO_DATA_ROOT", str(root))
+    monkeypatch.setenv("NANO_SAVE_TOKEN_IDS", "true")
+    main(["jobs", "--stop-token-ids", "3"])
+    run = tmp_path / "results" / "r1"
+    man = json.loads((run / "run_manifest.json").read_text())
+    assert man["engine"]["max_model_len"] == get_benchmark("gsm8k").max_model_len
+    assert man["request"]["stop_token_ids"] == [3] and man["protocol_arm"] is None and man["overrides"] == {}
+    jobs = [json.loads(x) for x in (run / "jobs.jsonl").read_text().splitlines()]
+    assert jobs and all(j["save_token_ids"] for j in jobs)

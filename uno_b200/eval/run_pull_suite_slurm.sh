@@ -8,8 +8,10 @@
 #   3. workers:     one engine per GPU on every node (srun), pulling jobs;
 #   4. score:       split the results per benchmark and grade them.
 # Required: MODEL.  Optional: BENCHMARKS, DATA_ROOT, NUM_SAMPLES, LIMIT,
-# DIFFUSION_BLOCK_SIZE, TEMPERATURE, TOP_P, TOP_K, RESULTS_ROOT, RUN_NAME,
-# SKIP_GRADING=1, DRY_RUN=1 (print the four commands, run nothing).
+# DIFFUSION_BLOCK_SIZE, TEMPERATURE, TOP_P, TOP_K, PROTOCOL_ARM (required for
+# any departure from the benchmark's canonical settings), RESULTS_ROOT, RUN_NAME,
+# SKIP_GRADING=1, DRY_RUN=1 (print the four commands, run nothing).  The
+# reference launcher's NANO_* variables are read as defaults by every role.
 set -euo pipefail
 REPO_ROOT="${UNO_REPO_ROOT:-${SLURM_SUBMIT_DIR:-$(pwd)}}"
 PYTHON_BIN="${PYTHON_BIN:-python}"
@@ -33,6 +35,7 @@ for b in ${BENCHMARKS:-gsm8k}; do jobs_cmd+=(--benchmark "${b}"); done
 [[ -n "${TEMPERATURE:-}" ]] && jobs_cmd+=(--temperature "${TEMPERATURE}")
 [[ -n "${TOP_P:-}" ]] && jobs_cmd+=(--top-p "${TOP_P}")
 [[ -n "${TOP_K:-}" ]] && jobs_cmd+=(--top-k "${TOP_K}")
+[[ -n "${PROTOCOL_ARM:-}" ]] && jobs_cmd+=(--protocol-arm "${PROTOCOL_ARM}")
 coord_cmd=("${PYTHON_BIN}" -m uno_b200.eval.pull_suite coordinator "${common[@]}" --jobs "${RUN_DIR}/jobs.jsonl"
            --output "${RUN_DIR}/results.jsonl" --address "0.0.0.0:${PORT}" --num-workers "${WORKERS}")
 worker_cmd=(srun --nodes="${NODES}" --ntasks="${WORKERS}" --ntasks-per-node="$((WORKERS / NODES))"
