@@ -209,3 +209,21 @@ def test_masks():
     am = ancestor_masks(par)
     assert am.tolist() == [[1, 3, 5, 11]]
     assert causal_suffix_masks(64)[-1].item() == -1
+
+
+def test_command_channel_size_from_environment():
+    import pytest
+
+    from uno_b200.engine.control import CommandChannel, channel_bytes
+
+    assert channel_bytes({}) == 64 << 20
+    assert channel_bytes({"INFERENCE_ENGINE_SHM_SIZE": str(1 << 20)}) == 1 << 20
+    with pytest.raises(ValueError):
+        channel_bytes({"INFERENCE_ENGINE_SHM_SIZE": "12"})
+    ch = CommandChannel(None, 0, 1, size=8192)
+    try:
+        assert ch.capacity >= 8192
+        with pytest.raises(ValueError, match="INFERENCE_ENGINE_SHM_SIZE"):
+            ch.commit(ch.capacity + 1)
+    finally:
+        ch.close()

@@ -40,6 +40,20 @@ _MAX_RANKS = 64
 _HDR = _LINE * (3 + 2 * _MAX_RANKS)
 _DEFAULT_BYTES = 64 << 20
 
+
+def channel_bytes(env=None) -> int:
+    """Payload capacity of the command channel: ``INFERENCE_ENGINE_SHM_SIZE`` bytes when set (the
+    reference engine's knob for large prefill batches, ``nano_vllm_uno/engine/model_runner.py:160``),
+    else 64 MiB."""
+    env = os.environ if env is None else env
+    raw = env.get("INFERENCE_ENGINE_SHM_SIZE")
+    if raw is None or not raw.strip():
+        return _DEFAULT_BYTES
+    size = int(raw)
+    if size < 4096:
+        raise ValueError(f"INFERENCE_ENGINE_SHM_SIZE={size} is below the 4096-byte minimum")
+    return size
+
 MSG_PICKLE = 1
 MSG_RUN = 2
 
@@ -155,7 +169,8 @@ class CommandChannel:
 
     def commit(self, nbytes: int) -> None:
         if nbytes > self.capacity:
-            raise ValueError(f"command of {nbytes} bytes exceeds the {self.capacity}-byte channel")
+            raise ValueError(f"command of {nbytes} bytes exceeds the {self.capacity}-byte channel "
+                             "(raise INFERENCE_ENGINE_SHM_SIZE or lower max_num_seqs)")
         self._words[1, 0] = nbytes
         self._words[0, 0] = self._seq() + 1  # published last: readers see a complete payload
 
@@ -290,7 +305,7 @@ class ChannelControlPlane:
 
         box = [None]
         if rank == 0:
-            ch = CommandChannel(None, 0, world, timeout_s=timeout_s)
+            ch = CommandChannel(None, 0, world, size=channel_bytes(), timeout_s=timeout_s)
             box[0] = ch.name
         dist.broadcast_object_list(box, src=0, group=group)
         if rank != 0:
