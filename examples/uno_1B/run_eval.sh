@@ -3,7 +3,7 @@
 # evaluation protocol, through the generic recipe with DP replicas, block 16.
 set -euo pipefail
 cd "$(dirname "${BASH_SOURCE[0]}")/../.."
-MODEL="${MODEL:-IFM/K2-Horizon-0.9B}" BLOCK="${BLOCK:-16}" exec bash examples/uno_qwen3_8b/run_eval.sh \
+MODEL="${MODEL:-IFM/K2-Horizon-0.9B}" BLOCK="${BLOCK:-16}" exec bash examples/uno_qwen3_8B/run_eval.sh \
   --model-revision "${MODEL_REVISION:-ee770e713760cf6350e4322cdbbff91a163b7d70}" \
   --gated-lora-path "${GATED_LORA_PATH:-IFM/K2-Horizon-0.9B-Uno}" \
   --gated-lora-revision "${GATED_LORA_REVISION:-b0d8896a301a2f4bc755538b1234a35100da50d0}" \

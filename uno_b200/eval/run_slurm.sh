@@ -12,7 +12,7 @@ if [[ $# -ne 1 ]]; then
   exit 2
 fi
 REPO_ROOT="${UNO_REPO_ROOT:-${SLURM_SUBMIT_DIR:-$(pwd)}}"
-RECIPE="${REPO_ROOT}/examples/${MODEL_EXAMPLE:-uno_qwen3_8b}/run_eval.sh"
+RECIPE="${REPO_ROOT}/examples/${MODEL_EXAMPLE:-uno_qwen3_8B}/run_eval.sh"
 [[ -f "${RECIPE}" ]] || { echo "no evaluation recipe at ${RECIPE}" >&2; exit 127; }
 export DP="${DP:-${SLURM_GPUS_ON_NODE:-8}}"
 BENCHMARKS="$1" exec bash "${RECIPE}"

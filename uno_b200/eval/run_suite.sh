@@ -2,12 +2,12 @@
 # Evaluation suite on this machine: each benchmark in turn through a model
 # recipe (examples/$MODEL_EXAMPLE/run_eval.sh), collecting the ones that fail.
 #   BENCHMARKS="gsm8k math500"  subset (default: every registered benchmark)
-#   MODEL_EXAMPLE=uno_qwen3_8b  recipe directory under examples/
+#   MODEL_EXAMPLE=uno_qwen3_8B  recipe directory under examples/
 #   DRY_RUN=1                   print the commands, run nothing
 set -uo pipefail
 REPO_ROOT="${UNO_REPO_ROOT:-$(cd "$(dirname "${BASH_SOURCE[0]}")/../.." && pwd)}"
 PYTHON_BIN="${PYTHON_BIN:-python}"
-MODEL_EXAMPLE="${MODEL_EXAMPLE:-uno_qwen3_8b}"
+MODEL_EXAMPLE="${MODEL_EXAMPLE:-uno_qwen3_8B}"
 RECIPE="${REPO_ROOT}/examples/${MODEL_EXAMPLE}/run_eval.sh"
 if [[ ! -f "${RECIPE}" ]]; then
   echo "no evaluation recipe at ${RECIPE} (MODEL_EXAMPLE is one of: $(ls "${REPO_ROOT}/examples" | tr '\n' ' '))" >&2

@@ -6,7 +6,7 @@
 set -euo pipefail
 REPO_ROOT="${UNO_REPO_ROOT:-$(cd "$(dirname "${BASH_SOURCE[0]}")/../.." && pwd)}"
 PYTHON_BIN="${PYTHON_BIN:-python}"
-MODEL_EXAMPLE="${MODEL_EXAMPLE:-uno_qwen3_8b}"
+MODEL_EXAMPLE="${MODEL_EXAMPLE:-uno_qwen3_8B}"
 RUN_NAME="${RUN_NAME:-suite}"
 RESULTS_ROOT="${RESULTS_ROOT:-${REPO_ROOT}/results/${MODEL_EXAMPLE}}"
 LOG_DIR="${LOG_DIR:-${RESULTS_ROOT}/${RUN_NAME}/slurm}"
