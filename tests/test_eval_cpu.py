@@ -158,7 +158,7 @@ def _port():
 def test_pull_suite_distributes_resumes_and_guards_manifest(tmp_path):
     from uno_b200.eval.pull_suite import completed_keys, run_coordinator
 
-    ctx = mp.get_context("fork")
+    ctx = mp.get_context("spawn")  # forked children of a process with torch threads can deadlock
     manifest = {"model": "toy", "protocol": "p1"}
     jobs = [{"benchmark": "toy", "id": f"q{i}", "sample": s, "ground_truth": str(i)} for i in range(7) for s in (0, 1)]
     results = tmp_path / "results.jsonl"

@@ -282,12 +282,12 @@ def test_sharded_adamw_matches_torch_adamw_two_ranks():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    ctx = mp.get_context("fork")
+    ctx = mp.get_context("spawn")  # forked children of a process with torch threads can deadlock
     box = ctx.Queue()
     procs = [ctx.Process(target=_adamw_worker, args=(r, 2, port, box)) for r in range(2)]
     for p in procs:
         p.start()
-    out = dict((r, (ps, ns)) for r, ps, ns in (box.get(timeout=60) for _ in procs))
+    out = dict((r, (ps, ns)) for r, ps, ns in (box.get(timeout=120) for _ in procs))
     for p in procs:
         p.join(30)
     shapes = [(3, 5), (7,), (2, 2, 3)]
