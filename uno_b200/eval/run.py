@@ -41,6 +41,18 @@ def _int_list(value: str) -> list[int]:
     return [int(x) for x in str(value).split(",") if x.strip()]
 
 
+def default_replicas(args) -> int:
+    """``--data-parallel-size``, else one replica per visible GPU (at most 8) divided by the TP size."""
+    if args.data_parallel_size is not None:
+        return int(args.data_parallel_size)
+    if args.device != "cuda":
+        return 1
+    import torch
+
+    gpus = min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 1
+    return max(1, gpus // max(1, int(args.tensor_parallel_size)))
+
+
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--benchmark")
@@ -58,7 +70,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--scores", type=Path, help="scores JSON (default: scores.json beside --output)")
     p.add_argument("--summary-output", type=Path)
     p.add_argument("--limit", type=int)
-    p.add_argument("--num-samples", type=int)
+    p.add_argument("--num-samples", "--repetitions", dest="num_samples", type=int,
+                   help="generations per problem (default: the benchmark's)")
     p.add_argument("--temperature", type=float)
     p.add_argument("--top-p", type=float)
     p.add_argument("--top-k", type=int)
@@ -74,7 +87,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--tree-verify-size", type=int)
     p.add_argument("--tree-candidate-top-k", type=int, default=16)
     p.add_argument("--tensor-parallel-size", type=int, default=1)
-    p.add_argument("--data-parallel-size", type=int, default=1)
+    p.add_argument("--data-parallel-size", type=int,
+                   help="engine replicas (default: one per visible GPU up to 8, as the reference's 8 on a full node; "
+                        "1 on the CPU)")
     p.add_argument("--device", choices=("cuda", "cpu"), default="cuda")
     p.add_argument("--load-format", default="auto")
     p.add_argument("--mask-token-id", type=int)
@@ -223,7 +238,7 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
     if pending:
         llm = LLM(model_dir or model, tokenizer_path=args.tokenizer_path or model_dir, gated_lora_path=adapter,
                   device=args.device, load_format=args.load_format, tensor_parallel_size=args.tensor_parallel_size,
-                  data_parallel_size=args.data_parallel_size, max_num_seqs=args.max_num_seqs,
+                  data_parallel_size=default_replicas(args), max_num_seqs=args.max_num_seqs,
                   max_model_len=args.max_model_len, max_num_batched_tokens=args.max_num_batched_tokens,
                   max_diffusion_block_size=args.diffusion_block_size,
                   cuda_graph_block_sizes=args.cuda_graph_block_sizes or sorted({1, args.diffusion_block_size}),
