@@ -709,3 +709,14 @@ def test_pull_suite_jobs_role_writes_engine_and_request_settings(tmp_path, monke
     assert man["request"]["stop_token_ids"] == [3] and man["protocol_arm"] is None and man["overrides"] == {}
     jobs = [json.loads(x) for x in (run / "jobs.jsonl").read_text().splitlines()]
     assert jobs and all(j["save_token_ids"] for j in jobs)
+
+
+def test_eval_runner_replica_default():
+    from types import SimpleNamespace
+
+    from uno_b200.eval.run import build_parser, default_replicas
+
+    args = build_parser().parse_args(["--model", "m", "--repetitions", "2"])
+    assert args.num_samples == 2 and args.data_parallel_size is None
+    assert default_replicas(SimpleNamespace(data_parallel_size=None, device="cpu", tensor_parallel_size=1)) == 1
+    assert default_replicas(SimpleNamespace(data_parallel_size=3, device="cuda", tensor_parallel_size=1)) == 3
