@@ -106,7 +106,8 @@ def shard_candidates(rows: torch.Tensor, count: int, inv_t: float, vocab_start: 
     else:
         vals, ids = ranked_top(rows, C)
     scaled = vals.double() * float(inv_t)
-    lse = torch.logsumexp(rows.double() * float(inv_t), dim=1, keepdim=True)
+    # the shard's log-normaliser in fp32 (one pass over the shard; the merge runs in fp64)
+    lse = torch.logsumexp(rows.float() * float(inv_t), dim=1, keepdim=True).double()
     packed = torch.cat([(ids + int(vocab_start)).double(), scaled, lse], dim=1)
     everyone = gather(packed)
     tp = everyone.shape[1] // (2 * C + 1)
