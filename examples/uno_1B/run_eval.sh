@@ -3,6 +3,7 @@
 # evaluation protocol, through the generic recipe with DP replicas, block 16.
 set -euo pipefail
 cd "$(dirname "${BASH_SOURCE[0]}")/../.."
+if [[ $# -gt 0 && "$1" != -* ]]; then export BENCHMARKS="$1"; shift; fi  # run_eval.sh BENCHMARK [flags]
 MODEL="${MODEL:-IFM/K2-Horizon-0.9B}" BLOCK="${BLOCK:-16}" exec bash examples/uno_qwen3_8B/run_eval.sh \
   --model-revision "${MODEL_REVISION:-ee770e713760cf6350e4322cdbbff91a163b7d70}" \
   --gated-lora-path "${GATED_LORA_PATH:-IFM/K2-Horizon-0.9B-Uno}" \

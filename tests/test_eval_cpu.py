@@ -720,3 +720,22 @@ def test_eval_runner_replica_default():
     assert args.num_samples == 2 and args.data_parallel_size is None
     assert default_replicas(SimpleNamespace(data_parallel_size=None, device="cpu", tensor_parallel_size=1)) == 1
     assert default_replicas(SimpleNamespace(data_parallel_size=3, device="cuda", tensor_parallel_size=1)) == 3
+
+
+def test_model_eval_recipes_take_the_benchmark_positionally(tmp_path):
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = {k: v for k, v in os.environ.items() if k not in ("MODEL", "BENCHMARKS", "DP")}
+    env.update(DRY_RUN="1", RESULTS_ROOT=str(tmp_path), RUN_NAME="r", DATA_PARALLEL_SIZE="2")
+    for recipe, model in (("uno_qwen3_8B", "s-sahoo/uno-qwen3-8B"), ("uno_8B", "IFM/K2-Horizon-7B"),
+                          ("uno_1B", "IFM/K2-Horizon-0.9B")):
+        out = subprocess.run(["bash", os.path.join(root, "examples", recipe, "run_eval.sh"), "gsm8k",
+                              "--protocol-arm", "a"], env=env, capture_output=True, text=True, timeout=60)
+        assert out.returncode == 0, out.stderr
+        lines = out.stdout.strip().splitlines()
+        assert lines[0].split()[-1] == "gsm8k" and len(lines) == 2, lines
+        run = lines[1].split()
+        assert run[run.index("--benchmark") + 1] == "gsm8k" and run[run.index("--model") + 1] == model
+        assert run[run.index("--data-parallel-size") + 1] == "2" and run[-2:] == ["--protocol-arm", "a"]
+    assert not any(tmp_path.iterdir())  # a dry run writes nothing

@@ -170,7 +170,11 @@ def main(argv: list[str] | None = None) -> dict[str, Any]:
     if args.data is None:
         if bench is None:
             raise ValueError("--data is required when --benchmark is not set")
-        args.data = bench.data_path
+        # the prepared file under UNO_EVAL_DATA_DIR, prepared now when it is missing (pinned bundle
+        # from UNO_EVAL_PROTOCOL_SOURCE_DIR or the Hub, public datasets otherwise)
+        from uno_b200.eval.prepare import prepare_benchmark_data
+
+        args.data = prepare_benchmark_data(bench.name, output_dir=bench.data_path.parent)
     if not Path(args.data).is_file():
         raise FileNotFoundError(f"dataset not found: {args.data} (set UNO_EVAL_DATA_DIR or pass --data)")
     if bench is not None:
