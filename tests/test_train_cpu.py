@@ -630,3 +630,22 @@ def test_slurm_launcher_dry_run(tmp_path):
                         ("--curriculum", "released"), ("--run-name", "r1"), ("--wandb-mode", "disabled"),
                         ("--lora-rank", "128")):
         assert cmd[cmd.index(flag) + 1] == value, flag
+
+
+def test_training_recipe_dry_run_uses_the_released_settings():
+    import os
+    import subprocess
+
+    from uno_b200.train.__main__ import build_parser
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = {k: v for k, v in os.environ.items() if not k.startswith(("SLURM_", "NODES", "CURRICULUM", "LORA_", "LR"))}
+    env.update(DRY_RUN="1", RUN_NAME="r")
+    out = subprocess.run(["bash", os.path.join(root, "examples", "uno_qwen3_8B", "run_train.sh"), "--max-steps", "2"],
+                         env=env, capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    cmd = out.stdout.split()
+    args = build_parser().parse_args(cmd[cmd.index("uno_b200.train") + 1:])
+    assert (args.lora_rank, args.lora_alpha, args.lr, args.warmup_steps, args.global_batch, args.curriculum) == \
+        (128, 2048, 1e-5, 562, 128, "released")
+    assert args.max_steps == 2 and args.fsdp
