@@ -191,15 +191,16 @@ def _worker(rank, world, port, box):
     dist.destroy_process_group()
 
 
-def test_sampler_on_gloo_ranks_takes_identical_decisions():
+@pytest.mark.parametrize("world", [2, 4])
+def test_sampler_on_gloo_ranks_takes_identical_decisions(world):
     ctx = mp.get_context("spawn")
     box = ctx.Queue()
-    port, world = _port(), 2
+    port = _port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, box)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(box.get(timeout=180) for _ in range(world))
     for p in procs:
         p.join(60)
-    assert got[0] == got[1]
+    assert all(got[r] == got[0] for r in range(world))
     assert all(case[3] and case[4] for case in got[0])
